@@ -1,0 +1,319 @@
+"""ctypes binding of libfa4d.so (the C ABI in include/fa4d.h) plus the tensor
+plumbing the autograd op needs: stride extraction, output/workspace allocation
+and stream selection.  PyTorch only supplies device memory and the current
+stream; all attention arithmetic runs in the library's sm_100a kernels.
+
+There is no fallback: if the library is missing or cannot be loaded, every entry
+point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Optional
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libfa4d.so"
+
+FA4D_BF16 = 0
+FA4D_F16 = 1
+CAUSAL_NONE = 0
+CAUSAL_TOP_LEFT = 1
+CAUSAL_BOTTOM_RIGHT = 2
+
+FA4D_OK = 0
+FA4D_ERR_INVALID = -1
+FA4D_ERR_UNSUPPORTED = -2
+FA4D_ERR_CUDA = -3
+FA4D_ERR_DRIVER = -4
+FA4D_ERR_LAYOUT = -5
+FA4D_ERR_WORKSPACE = -6
+
+EXPORTED_SYMBOLS = (
+    "fa4d_lse_row_stride",
+    "fa4d_bwd_workspace_size",
+    "fa4d_fwd",
+    "fa4d_bwd",
+    "fa4d_last_error",
+    "fa4d_device_status",
+    "fa4d_abi_version",
+)
+
+_i64x3 = ctypes.c_int64 * 3
+
+
+class FwdArgs(ctypes.Structure):
+    """Mirror of ``fa4d_fwd_args``."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("lse", ctypes.c_void_p),
+        ("mask", ctypes.c_void_p),
+        ("score", ctypes.c_void_p),
+        ("q_stride", _i64x3),
+        ("k_stride", _i64x3),
+        ("v_stride", _i64x3),
+        ("o_stride", _i64x3),
+        ("mask_stride", _i64x3),
+        ("score_stride", _i64x3),
+        ("B", ctypes.c_int32),
+        ("Tq", ctypes.c_int32),
+        ("Tk", ctypes.c_int32),
+        ("Hq", ctypes.c_int32),
+        ("Hk", ctypes.c_int32),
+        ("D", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("causal", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("reserved", ctypes.c_int32 * 3),
+    ]
+
+
+class BwdArgs(ctypes.Structure):
+    """Mirror of ``fa4d_bwd_args``."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("dout", ctypes.c_void_p),
+        ("lse", ctypes.c_void_p),
+        ("mask", ctypes.c_void_p),
+        ("score", ctypes.c_void_p),
+        ("dq", ctypes.c_void_p),
+        ("dk", ctypes.c_void_p),
+        ("dv", ctypes.c_void_p),
+        ("q_stride", _i64x3),
+        ("k_stride", _i64x3),
+        ("v_stride", _i64x3),
+        ("o_stride", _i64x3),
+        ("do_stride", _i64x3),
+        ("dq_stride", _i64x3),
+        ("dk_stride", _i64x3),
+        ("dv_stride", _i64x3),
+        ("mask_stride", _i64x3),
+        ("score_stride", _i64x3),
+        ("B", ctypes.c_int32),
+        ("Tq", ctypes.c_int32),
+        ("Tk", ctypes.c_int32),
+        ("Hq", ctypes.c_int32),
+        ("Hk", ctypes.c_int32),
+        ("D", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("causal", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("deterministic", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+_LIB: Optional[ctypes.CDLL] = None
+
+
+def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
+    """Loads libfa4d.so once and declares the prototypes of include/fa4d.h."""
+    global _LIB
+    if _LIB is not None and path is None:
+        return _LIB
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise RuntimeError(
+            f"{p} is missing: build it with `python {HERE / 'build.py'}` "
+            "(the attention op has no fallback implementation)"
+        )
+    lib = ctypes.CDLL(str(p))
+    lib.fa4d_lse_row_stride.argtypes = [ctypes.c_int32]
+    lib.fa4d_lse_row_stride.restype = ctypes.c_int64
+    lib.fa4d_bwd_workspace_size.argtypes = [ctypes.c_int32] * 4
+    lib.fa4d_bwd_workspace_size.restype = ctypes.c_size_t
+    lib.fa4d_fwd.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
+    lib.fa4d_fwd.restype = ctypes.c_int
+    lib.fa4d_bwd.argtypes = [ctypes.POINTER(BwdArgs), ctypes.c_void_p]
+    lib.fa4d_bwd.restype = ctypes.c_int
+    lib.fa4d_last_error.argtypes = []
+    lib.fa4d_last_error.restype = ctypes.c_char_p
+    lib.fa4d_device_status.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    lib.fa4d_device_status.restype = ctypes.c_int
+    lib.fa4d_abi_version.argtypes = []
+    lib.fa4d_abi_version.restype = ctypes.c_int
+    if path is None:
+        _LIB = lib
+    return lib
+
+
+class LayoutError(ValueError):
+    """Raised when a tensor's strides cannot be read by TMA (caller may copy and retry)."""
+
+
+def _raise(lib: ctypes.CDLL, rc: int, what: str) -> None:
+    msg = (lib.fa4d_last_error() or b"").decode(errors="replace")
+    text = f"{what}: {msg} (code {rc})"
+    if rc == FA4D_ERR_LAYOUT:
+        raise LayoutError(text)
+    if rc in (FA4D_ERR_INVALID, FA4D_ERR_UNSUPPORTED, FA4D_ERR_WORKSPACE):
+        raise ValueError(text)
+    raise RuntimeError(text)
+
+
+def _dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return FA4D_BF16
+    if dt == torch.float16:
+        return FA4D_F16
+    raise ValueError(f"unsupported dtype {dt}: expected bf16 or fp16")
+
+
+def _bth_strides(x: torch.Tensor) -> tuple:
+    """(batch, seq, head) element strides of a [B, T, H, D] view."""
+    return (x.stride(0), x.stride(1), x.stride(2))
+
+
+def _bias_strides(x: Optional[torch.Tensor]) -> tuple:
+    """(batch, head, row) strides of a [B|1, H|1, Tq, Tk] tensor; broadcast dims get 0."""
+    if x is None:
+        return (0, 0, 0)
+    sb = 0 if x.shape[0] == 1 else x.stride(0)
+    sh = 0 if x.shape[1] == 1 else x.stride(1)
+    return (sb, sh, x.stride(2))
+
+
+def tma_friendly(x: torch.Tensor) -> bool:
+    """True if a [B, T, H, D] 16-bit view can be described by a TMA tensor map."""
+    if x.stride(3) != 1 or x.data_ptr() % 16 != 0:
+        return False
+    for dim in range(3):
+        if x.shape[dim] != 1 and (x.stride(dim) <= 0 or x.stride(dim) % 8 != 0):
+            return False
+    return True
+
+
+def as_tma(x: torch.Tensor) -> torch.Tensor:
+    return x if tma_friendly(x) else x.contiguous()
+
+
+def prepare_bias(x: Optional[torch.Tensor], dtype: torch.dtype) -> Optional[torch.Tensor]:
+    """Mask/score as the kernel reads them: given dtype, unit key stride (broadcast views kept)."""
+    if x is None:
+        return None
+    if x.dtype != dtype:
+        x = x.to(dtype)
+    if x.stride(3) != 1:
+        x = x.contiguous()
+    return x
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def lse_row_stride(Tq: int) -> int:
+    return int(load_library().fa4d_lse_row_stride(int(Tq)))
+
+
+def forward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    mask: Optional[torch.Tensor],
+    score: Optional[torch.Tensor],
+    scale: float,
+    causal: int,
+) -> tuple:
+    """Runs fa4d_fwd.  q: [B, Tq, Hq, D] view, k/v: [B, Tk, Hk, D] views (TMA-friendly).
+    Returns (O [B, Tq, Hq, D] contiguous, LSE [B, Hq, lse_row_stride(Tq)] fp32)."""
+    lib = load_library()
+    B, Tq, Hq, D = q.shape
+    Tk, Hk = k.shape[1], k.shape[2]
+    o = torch.empty((B, Tq, Hq, D), dtype=q.dtype, device=q.device)
+    lse = torch.empty((B, Hq, lse_row_stride(Tq)), dtype=torch.float32, device=q.device)
+    a = FwdArgs()
+    a.q, a.k, a.v, a.o, a.lse = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr()
+    a.mask = mask.data_ptr() if mask is not None else None
+    a.score = score.data_ptr() if score is not None else None
+    a.q_stride = _i64x3(*_bth_strides(q))
+    a.k_stride = _i64x3(*_bth_strides(k))
+    a.v_stride = _i64x3(*_bth_strides(v))
+    a.o_stride = _i64x3(*_bth_strides(o))
+    a.mask_stride = _i64x3(*_bias_strides(mask))
+    a.score_stride = _i64x3(*_bias_strides(score))
+    a.B, a.Tq, a.Tk, a.Hq, a.Hk, a.D = B, Tq, Tk, Hq, Hk, D
+    a.dtype = _dtype_code(q.dtype)
+    a.causal = int(causal)
+    a.scale = float(scale)
+    with torch.cuda.device(q.device):
+        rc = lib.fa4d_fwd(ctypes.byref(a), _stream_ptr(q.device))
+    if rc != FA4D_OK:
+        _raise(lib, rc, "fa4d_fwd")
+    return o, lse
+
+
+def backward(
+    dout: torch.Tensor,
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    o: torch.Tensor,
+    lse: torch.Tensor,
+    mask: Optional[torch.Tensor],
+    score: Optional[torch.Tensor],
+    scale: float,
+    causal: int,
+) -> tuple:
+    """Runs fa4d_bwd on [B, T, H, D] views.  Returns (dQ, dK, dV) contiguous in the
+    input dtype, dK/dV summed over the GQA group."""
+    lib = load_library()
+    B, Tq, Hq, D = q.shape
+    Tk, Hk = k.shape[1], k.shape[2]
+    dq = torch.empty((B, Tq, Hq, D), dtype=q.dtype, device=q.device)
+    dk = torch.empty((B, Tk, Hk, D), dtype=q.dtype, device=q.device)
+    dv = torch.empty((B, Tk, Hk, D), dtype=q.dtype, device=q.device)
+    ws_bytes = int(lib.fa4d_bwd_workspace_size(B, Tq, Hq, D))
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=q.device)
+    a = BwdArgs()
+    a.q, a.k, a.v, a.o, a.dout = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr()
+    a.lse = lse.data_ptr()
+    a.mask = mask.data_ptr() if mask is not None else None
+    a.score = score.data_ptr() if score is not None else None
+    a.dq, a.dk, a.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    a.q_stride = _i64x3(*_bth_strides(q))
+    a.k_stride = _i64x3(*_bth_strides(k))
+    a.v_stride = _i64x3(*_bth_strides(v))
+    a.o_stride = _i64x3(*_bth_strides(o))
+    a.do_stride = _i64x3(*_bth_strides(dout))
+    a.dq_stride = _i64x3(*_bth_strides(dq))
+    a.dk_stride = _i64x3(*_bth_strides(dk))
+    a.dv_stride = _i64x3(*_bth_strides(dv))
+    a.mask_stride = _i64x3(*_bias_strides(mask))
+    a.score_stride = _i64x3(*_bias_strides(score))
+    a.B, a.Tq, a.Tk, a.Hq, a.Hk, a.D = B, Tq, Tk, Hq, Hk, D
+    a.dtype = _dtype_code(q.dtype)
+    a.causal = int(causal)
+    a.scale = float(scale)
+    a.deterministic = 0
+    a.workspace = ws.data_ptr()
+    a.workspace_bytes = ws_bytes
+    with torch.cuda.device(q.device):
+        rc = lib.fa4d_bwd(ctypes.byref(a), _stream_ptr(q.device))
+    if rc != FA4D_OK:
+        _raise(lib, rc, "fa4d_bwd")
+    return dq, dk, dv
+
+
+def device_status(device: Optional[torch.device] = None, clear: bool = True) -> int:
+    """Synchronises the current stream and returns the kernels' timeout bits (0 = none)."""
+    lib = load_library()
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(device):
+        rc = lib.fa4d_device_status(_stream_ptr(device), 1 if clear else 0)
+    if rc < 0:
+        _raise(lib, rc, "fa4d_device_status")
+    return rc

@@ -1,0 +1,290 @@
+// fa4d_api.cu — the C ABI declared in include/fa4d.h: argument validation, TMA
+// tensor-map encoding and kernel dispatch.  No allocation happens here; every
+// buffer (including the backward workspace) is owned by the caller.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "fa4d.h"
+#include "fa4d_kernels.h"
+
+namespace {
+
+// Device status word: kernels OR FA4D_DEV_* bits into it when a bounded wait gives up.
+__device__ int g_status_word = 0;
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int ok() {
+  g_last_error.clear();
+  return FA4D_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// Address of g_status_word on the current device, looked up once per device.
+int* status_word_ptr() {
+  static std::mutex mu;
+  static int* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Tensor map over a [B, T, H, D] 16-bit tensor given element strides (b, t, h):
+// dims (D, T, H, B), box (64, rows, 1, 1), 128-B swizzle, zero fill out of bounds.
+int encode_bthd(CUtensorMap* m, const void* ptr, int B, int T, int H, int D, const int64_t st[3], int rows,
+                bool bf16, const char* name) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(FA4D_ERR_DRIVER, "cuTensorMapEncodeTiled is not available from the CUDA driver");
+  if (!aligned(ptr, 16)) return fail(FA4D_ERR_LAYOUT, "%s: base address is not 16-byte aligned", name);
+  const int64_t sz[3] = {B, T, H};
+  int64_t bytes[3];
+  for (int i = 0; i < 3; ++i) {
+    bytes[i] = st[i] * 2;
+    // A size-1 dimension is never stepped over; give it a valid stride that is at
+    // least as large as the whole tensor so no size rule can trip on it.
+    if (sz[i] == 1) bytes[i] = static_cast<int64_t>(D) * 2 * B * T * H;
+    if (bytes[i] <= 0 || bytes[i] % 16 != 0 || bytes[i] >= (int64_t(1) << 40))
+      return fail(FA4D_ERR_LAYOUT, "%s: stride %lld (elements) is not a positive multiple of 8", name,
+                  static_cast<long long>(st[i]));
+  }
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(bytes[1]), static_cast<cuuint64_t>(bytes[2]),
+                           static_cast<cuuint64_t>(bytes[0])};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(rows), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FA4D_ERR_DRIVER, "%s: cuTensorMapEncodeTiled failed (%d)", name, int(r));
+  return FA4D_OK;
+}
+
+int check_common(int B, int Tq, int Tk, int Hq, int Hk, int D, int dtype, int causal, float scale) {
+  if (B < 1 || Tq < 1 || Tk < 1 || Hq < 1 || Hk < 1)
+    return fail(FA4D_ERR_INVALID, "sizes must be positive (B=%d Tq=%d Tk=%d Hq=%d Hk=%d)", B, Tq, Tk, Hq, Hk);
+  if (Hq % Hk != 0)
+    return fail(FA4D_ERR_INVALID, "query heads (%d) must be divisible by key/value heads (%d)", Hq, Hk);
+  if (B > 65535 || Hq > 65535) return fail(FA4D_ERR_INVALID, "B and Hq must be <= 65535");
+  if (Tq > (1 << 30) || Tk > (1 << 30)) return fail(FA4D_ERR_INVALID, "sequence length too large");
+  if (D != 64 && D != 128) return fail(FA4D_ERR_UNSUPPORTED, "head dim %d is not built (64, 128)", D);
+  if (dtype != FA4D_BF16 && dtype != FA4D_F16) return fail(FA4D_ERR_INVALID, "dtype %d is not bf16/f16", dtype);
+  if (causal < FA4D_CAUSAL_NONE || causal > FA4D_CAUSAL_BOTTOM_RIGHT)
+    return fail(FA4D_ERR_INVALID, "causal mode %d is unknown", causal);
+  if (!(scale == scale)) return fail(FA4D_ERR_INVALID, "scale is NaN");
+  return FA4D_OK;
+}
+
+// Row pointers of a [.., D] output written with 16-byte stores.
+int check_rows16(const void* ptr, const int64_t st[3], const char* name) {
+  if (!ptr) return fail(FA4D_ERR_INVALID, "%s is NULL", name);
+  if (!aligned(ptr, 16)) return fail(FA4D_ERR_LAYOUT, "%s: base address is not 16-byte aligned", name);
+  for (int i = 0; i < 3; ++i)
+    if (st[i] % 8 != 0) return fail(FA4D_ERR_LAYOUT, "%s: strides must be multiples of 8 elements", name);
+  return FA4D_OK;
+}
+
+int causal_offset(int causal, int Tq, int Tk) { return causal == FA4D_CAUSAL_BOTTOM_RIGHT ? Tk - Tq : 0; }
+
+int64_t lse_ld_of(int Tq) { return (static_cast<int64_t>(Tq) + 127) / 128 * 128; }
+
+}  // namespace
+
+extern "C" {
+
+int64_t fa4d_lse_row_stride(int32_t Tq) { return lse_ld_of(Tq); }
+
+size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D) {
+  const size_t dq = static_cast<size_t>(B) * Tq * Hq * D * sizeof(float);
+  const size_t dq_al = (dq + 255) / 256 * 256;
+  const size_t delta = static_cast<size_t>(B) * Hq * lse_ld_of(Tq) * sizeof(float);
+  return dq_al + (delta + 255) / 256 * 256;
+}
+
+const char* fa4d_last_error(void) { return g_last_error.c_str(); }
+
+int fa4d_abi_version(void) { return FA4D_ABI_VERSION; }
+
+int fa4d_device_status(void* stream, int clear) {
+  int* word = status_word_ptr();
+  if (!word) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, word, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && clear) {
+    e = cudaMemsetAsync(word, 0, sizeof(int), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  }
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "device status read failed: %s", cudaGetErrorString(e));
+  return v;
+}
+
+int fa4d_fwd(const fa4d_fwd_args* a, void* stream) {
+  if (!a) return fail(FA4D_ERR_INVALID, "args is NULL");
+  int rc = check_common(a->B, a->Tq, a->Tk, a->Hq, a->Hk, a->D, a->dtype, a->causal, a->scale);
+  if (rc) return rc;
+  if (!a->q || !a->k || !a->v || !a->o || !a->lse) return fail(FA4D_ERR_INVALID, "q, k, v, o and lse are required");
+  if ((rc = check_rows16(a->o, a->o_stride, "o"))) return rc;
+  const bool bf16 = a->dtype == FA4D_BF16;
+  fa4d::FwdParams p;
+  memset(&p, 0, sizeof(p));
+  if ((rc = encode_bthd(&p.tm_q, a->q, a->B, a->Tq, a->Hq, a->D, a->q_stride, 128, bf16, "q"))) return rc;
+  if ((rc = encode_bthd(&p.tm_k, a->k, a->B, a->Tk, a->Hk, a->D, a->k_stride, 128, bf16, "k"))) return rc;
+  if ((rc = encode_bthd(&p.tm_v, a->v, a->B, a->Tk, a->Hk, a->D, a->v_stride, 128, bf16, "v"))) return rc;
+  p.o = a->o;
+  p.lse = a->lse;
+  p.mask = a->mask;
+  p.score = a->score;
+  for (int i = 0; i < 3; ++i) {
+    p.o_stride[i] = a->o_stride[i];
+    p.mask_stride[i] = a->mask_stride[i];
+    p.score_stride[i] = a->score_stride[i];
+  }
+  p.B = a->B;
+  p.Tq = a->Tq;
+  p.Tk = a->Tk;
+  p.Hq = a->Hq;
+  p.Hk = a->Hk;
+  p.lse_ld = static_cast<int32_t>(lse_ld_of(a->Tq));
+  p.causal = a->causal != FA4D_CAUSAL_NONE;
+  p.causal_off = causal_offset(a->causal, a->Tq, a->Tk);
+  p.scale_log2 = static_cast<float>(static_cast<double>(a->scale) * 1.4426950408889634);
+  p.mask_vec = a->mask && aligned(a->mask, 4) && a->mask_stride[0] % 4 == 0 && a->mask_stride[1] % 4 == 0 &&
+               a->mask_stride[2] % 4 == 0;
+  p.score_vec = a->score && aligned(a->score, 16) && a->score_stride[0] % 4 == 0 && a->score_stride[1] % 4 == 0 &&
+                a->score_stride[2] % 4 == 0;
+  p.status = status_word_ptr();
+  if (!p.status) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
+  cudaError_t e = fa4d::launch_fwd(p, a->D, bf16, a->mask != nullptr, a->score != nullptr,
+                                   static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "forward launch failed: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+int fa4d_bwd(const fa4d_bwd_args* a, void* stream) {
+  if (!a) return fail(FA4D_ERR_INVALID, "args is NULL");
+  int rc = check_common(a->B, a->Tq, a->Tk, a->Hq, a->Hk, a->D, a->dtype, a->causal, a->scale);
+  if (rc) return rc;
+  if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse)
+    return fail(FA4D_ERR_INVALID, "q, k, v, o, dout and lse are required");
+  if (a->deterministic) return fail(FA4D_ERR_UNSUPPORTED, "deterministic dQ is reserved");
+  if ((rc = check_rows16(a->dq, a->dq_stride, "dq"))) return rc;
+  if ((rc = check_rows16(a->dk, a->dk_stride, "dk"))) return rc;
+  if ((rc = check_rows16(a->dv, a->dv_stride, "dv"))) return rc;
+  if ((rc = check_rows16(a->o, a->o_stride, "o"))) return rc;
+  const size_t need = fa4d_bwd_workspace_size(a->B, a->Tq, a->Hq, a->D);
+  if (!a->workspace || a->workspace_bytes < need || !aligned(a->workspace, 256))
+    return fail(FA4D_ERR_WORKSPACE, "workspace must be 256-B aligned and hold %zu bytes (got %zu)", need,
+                a->workspace_bytes);
+  const bool bf16 = a->dtype == FA4D_BF16;
+  const int64_t lse_ld = lse_ld_of(a->Tq);
+  float* dq_acc = static_cast<float*>(a->workspace);
+  const size_t dq_bytes = static_cast<size_t>(a->B) * a->Tq * a->Hq * a->D * sizeof(float);
+  float* delta = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + (dq_bytes + 255) / 256 * 256);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = status_word_ptr();
+  if (!status) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
+
+  fa4d::BwdParams p;
+  memset(&p, 0, sizeof(p));
+  if ((rc = encode_bthd(&p.tm_q, a->q, a->B, a->Tq, a->Hq, a->D, a->q_stride, 64, bf16, "q"))) return rc;
+  if ((rc = encode_bthd(&p.tm_do, a->dout, a->B, a->Tq, a->Hq, a->D, a->do_stride, 64, bf16, "dout"))) return rc;
+  if ((rc = encode_bthd(&p.tm_k, a->k, a->B, a->Tk, a->Hk, a->D, a->k_stride, 128, bf16, "k"))) return rc;
+  if ((rc = encode_bthd(&p.tm_v, a->v, a->B, a->Tk, a->Hk, a->D, a->v_stride, 128, bf16, "v"))) return rc;
+  p.lse = a->lse;
+  p.delta = delta;
+  p.dq_acc = dq_acc;
+  p.dk = a->dk;
+  p.dv = a->dv;
+  p.mask = a->mask;
+  p.score = a->score;
+  for (int i = 0; i < 3; ++i) {
+    p.dk_stride[i] = a->dk_stride[i];
+    p.dv_stride[i] = a->dv_stride[i];
+    p.mask_stride[i] = a->mask_stride[i];
+    p.score_stride[i] = a->score_stride[i];
+  }
+  p.B = a->B;
+  p.Tq = a->Tq;
+  p.Tk = a->Tk;
+  p.Hq = a->Hq;
+  p.Hk = a->Hk;
+  p.lse_ld = static_cast<int32_t>(lse_ld);
+  p.causal = a->causal != FA4D_CAUSAL_NONE;
+  p.causal_off = causal_offset(a->causal, a->Tq, a->Tk);
+  p.scale_log2 = static_cast<float>(static_cast<double>(a->scale) * 1.4426950408889634);
+  p.scale = a->scale;
+  p.status = status;
+
+  fa4d::PrepParams pp;
+  memset(&pp, 0, sizeof(pp));
+  pp.o = a->o;
+  pp.dout = a->dout;
+  pp.delta = delta;
+  pp.dq_acc = dq_acc;
+  for (int i = 0; i < 3; ++i) {
+    pp.o_stride[i] = a->o_stride[i];
+    pp.do_stride[i] = a->do_stride[i];
+  }
+  pp.B = a->B;
+  pp.Tq = a->Tq;
+  pp.Hq = a->Hq;
+  pp.D = a->D;
+  pp.lse_ld = static_cast<int32_t>(lse_ld);
+
+  fa4d::ConvertParams cp;
+  memset(&cp, 0, sizeof(cp));
+  cp.dq_acc = dq_acc;
+  cp.dq = a->dq;
+  for (int i = 0; i < 3; ++i) cp.dq_stride[i] = a->dq_stride[i];
+  cp.B = a->B;
+  cp.Tq = a->Tq;
+  cp.Hq = a->Hq;
+  cp.D = a->D;
+
+  cudaError_t e = fa4d::launch_bwd_prep(pp, bf16, s);
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "backward preprocess launch failed: %s", cudaGetErrorString(e));
+  e = fa4d::launch_bwd(p, a->D, bf16, a->mask != nullptr, a->score != nullptr, s);
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "backward launch failed: %s", cudaGetErrorString(e));
+  e = fa4d::launch_dq_convert(cp, bf16, s);
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "dQ convert launch failed: %s", cudaGetErrorString(e));
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,530 @@
+// fa4d_bwd.cu — FlashAttention-2 backward for sm_100a with an optional 4D mask/score.
+//
+// Math follows the reference backward (python/fa2.py:181-302): P is recomputed from
+// the saved log2-domain LSE, dV = P^T dO, dP = dO V^T, dS = P (dP - Delta) scale,
+// dK = dS^T Q, dQ = dS K, with Delta = rowsum(O * dO) (python/fa2.py:142-179).
+// Unlike the reference, one CTA owns a 128-key tile of one KV head and loops over
+// every query head of its GQA group, so dK/dV are summed in tensor memory and
+// stored once in the input dtype (the reference sums the group with fp32 atomics,
+// python/fa2.py:299-302, or with a bf16 host-side sum, python/fa2.py:548-549).
+// dQ is accumulated in fp32 with coalesced red.global.add and cast afterwards.
+//
+// CTA = 128 keys x one (batch, KV head); 384 threads:
+//   warp 0      TMA producer (K/V once; Q, dO, LSE, Delta per 64-row query tile)
+//   warp 1      tcgen05.mma issuer
+//   warp 2      TMEM allocator
+//   warps 4-7   P / dS computation (one thread per key row) and the dK/dV epilogue
+//   warps 8-11  dQ drain (one thread per head-dim lane) into the fp32 accumulator
+// TMEM: S^T x2 [0,64) [64,128), dP^T [128,192), dQ^T [192,256), dV [256,256+D),
+// dK [256+D, 256+2D).  All MMAs are kind::f16 with fp32 accumulation.
+#include <cfloat>
+
+#include "fa4d.h"
+#include "fa4d_kernels.h"
+#include "fa4d_ptx.cuh"
+
+namespace fa4d {
+
+namespace {
+
+constexpr int kBwdThreads = 384;
+
+template <int D>
+struct BwdLayout {
+  static constexpr int kKV = 128 * D * 2;  // K or V tile (128 keys)
+  static constexpr int kQT = 64 * D * 2;   // Q or dO tile (64 queries)
+  static constexpr int kDS = 128 * 64 * 2; // dS^T tile (128 keys x 64 queries, 16-bit)
+  static constexpr int kK = 0;
+  static constexpr int kV = kK + kKV;
+  static constexpr int kQ = kV + kKV;        // 2 stages
+  static constexpr int kDO = kQ + 2 * kQT;   // 2 stages
+  static constexpr int kDSb = kDO + 2 * kQT; // 2 buffers
+  static constexpr int kLSE = kDSb + 2 * kDS;   // 2 stages x 64 floats
+  static constexpr int kDelta = kLSE + 2 * 256; // 2 stages x 64 floats
+  static constexpr int kBar = kDelta + 2 * 256;
+  static constexpr int kNumBars = 16;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kBytes = kMisc + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+};
+
+// S^T = K Q^T (or dP^T = V dO^T): M=128 keys, N=64 queries, K=D; both K-major.
+template <int D, bool kBF16>
+__device__ __forceinline__ void issue_kt(uint32_t tD, uint32_t sA, uint32_t sB) {
+  constexpr uint32_t idesc = make_idesc(128, 64, kBF16, false, false);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t offa = static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 32);
+    const uint32_t offb = static_cast<uint32_t>((kk >> 2) * 8192 + (kk & 3) * 32);
+    mma_ss(tD, sw128_desc(sA + offa, 16, 1024), sw128_desc(sB + offb, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+  }
+}
+
+// dV += P^T dO : M=128 keys, N=D, K=64 queries; P^T from TMEM, dO MN-major.
+template <int D, bool kBF16>
+__device__ __forceinline__ void issue_dv(uint32_t tD, uint32_t tP, uint32_t sDO, bool acc) {
+  constexpr uint32_t idesc = make_idesc(128, D, kBF16, false, true);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+    mma_ts(tD, tP + kk * 8, sw128_desc(sDO + kk * 2048, 8192, 1024), idesc, (acc || kk > 0) ? 1u : 0u);
+}
+
+// dK += dS^T Q : M=128 keys, N=D, K=64 queries; dS^T K-major in smem, Q MN-major.
+template <int D, bool kBF16>
+__device__ __forceinline__ void issue_dk(uint32_t tD, uint32_t sDS, uint32_t sQ, bool acc) {
+  constexpr uint32_t idesc = make_idesc(128, D, kBF16, false, true);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+    mma_ss(tD, sw128_desc(sDS + kk * 32, 16, 1024), sw128_desc(sQ + kk * 2048, 8192, 1024), idesc,
+           (acc || kk > 0) ? 1u : 0u);
+}
+
+// dQ^T = K^T dS^T : M=D, N=64 queries, K=128 keys; K MN-major, dS^T MN-major.
+template <int D, bool kBF16>
+__device__ __forceinline__ void issue_dq(uint32_t tD, uint32_t sK, uint32_t sDS) {
+  constexpr uint32_t idesc = make_idesc(D, 64, kBF16, true, true);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    mma_ss(tD, sw128_desc(sK + kk * 2048, 16384, 1024), sw128_desc(sDS + kk * 2048, 8192, 1024), idesc,
+           kk > 0 ? 1u : 0u);
+}
+
+template <int D, bool kBF16, bool kMask, bool kScore>
+__global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_constant__ BwdParams p) {
+  using L = BwdLayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;    // [2]
+  uint64_t* q_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* dp_full = bars + 7;
+  uint64_t* p_full = bars + 8;
+  uint64_t* ds_full = bars + 9;
+  uint64_t* ds_empty = bars + 10; // [2]
+  uint64_t* dq_full = bars + 12;
+  uint64_t* dq_empty = bars + 13;
+  uint64_t* dkv_full = bars + 14;
+  uint64_t* mma_drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int k0 = blockIdx.x * 128;
+  const int hk = blockIdx.y;
+  const int b = blockIdx.z;
+  const int G = p.Hq / p.Hk;
+
+  // Query tiles this key tile interacts with.
+  int first_qt = 0;
+  if (p.causal) {
+    const long long qmin = static_cast<long long>(k0) - p.causal_off;  // q >= k - off
+    first_qt = qmin <= 0 ? 0 : static_cast<int>(qmin / 64);
+  }
+  const int num_qt_total = (p.Tq + 63) / 64;
+  const int nq = max(0, num_qt_total - first_qt);
+  const int N = G * nq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&ds_empty[i], 1);
+    }
+    mbar_init(dp_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(ds_full, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 128);
+    mbar_init(dkv_full, 1);
+    mbar_init(mma_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 192, kColDV = 256, kColDK = 256 + D;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && N > 0) {
+      prefetch_tmap(&p.tm_q);
+      prefetch_tmap(&p.tm_do);
+      prefetch_tmap(&p.tm_k);
+      prefetch_tmap(&p.tm_v);
+      mbar_arrive_expect_tx(kv_full, 2 * L::kKV);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_4d(smem + L::kK + c * 16384, &p.tm_k, kv_full, c * 64, k0, hk, b);
+        tma_load_4d(smem + L::kV + c * 16384, &p.tm_v, kv_full, c * 64, k0, hk, b);
+      }
+      int issued = 0;
+      for (int it = 0; it < N; ++it) {
+        const int st = it & 1;
+        const int g = it / nq;
+        const int h = hk * G + g;
+        const int q0 = (first_qt + it % nq) * 64;
+        if (!mbar_wait(&q_empty[st], ((it >> 1) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&q_full[st], 2 * L::kQT + 512);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(smem + L::kQ + st * L::kQT + c * 8192, &p.tm_q, &q_full[st], c * 64, q0, h, b);
+          tma_load_4d(smem + L::kDO + st * L::kQT + c * 8192, &p.tm_do, &q_full[st], c * 64, q0, h, b);
+        }
+        const int64_t row = (static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + q0;
+        bulk_load(smem + L::kLSE + st * 256, p.lse + row, 256, &q_full[st]);
+        bulk_load(smem + L::kDelta + st * 256, p.delta + row, 256, &q_full[st]);
+        issued = it + 1;
+      }
+      if (*reinterpret_cast<volatile int*>(abort_flag)) {
+        mbar_wait_short(kv_full, 0);
+        for (int it = max(0, issued - 2); it < issued; ++it) mbar_wait_short(&q_full[it & 1], (it >> 1) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && N > 0) {
+      const uint32_t sK = smem_u32(smem + L::kK);
+      const uint32_t sV = smem_u32(smem + L::kV);
+      const uint32_t sQ = smem_u32(smem + L::kQ);
+      const uint32_t sDO = smem_u32(smem + L::kDO);
+      const uint32_t sDS = smem_u32(smem + L::kDSb);
+      bool ok = mbar_wait(kv_full, 0, abort_flag) &&
+                mbar_wait(&q_full[0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_kt<D, kBF16>(tmem + kColS, sK, sQ);
+        tc_commit(&s_full[0]);
+        issue_kt<D, kBF16>(tmem + kColDP, sV, sDO);
+        tc_commit(dp_full);
+      }
+      for (int it = 0; ok && it < N; ++it) {
+        const int st = it & 1;
+        const int nx = (it + 1) & 1;
+        if (it + 1 < N) {
+          ok = mbar_wait(&q_full[nx], ((it + 1) >> 1) & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          issue_kt<D, kBF16>(tmem + kColS + 64 * nx, sK, sQ + nx * L::kQT);
+          tc_commit(&s_full[nx]);
+        }
+        ok = mbar_wait(p_full, it & 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        issue_dv<D, kBF16>(tmem + kColDV, tmem + kColS + 64 * st, sDO + st * L::kQT, it > 0);
+        ok = mbar_wait(ds_full, it & 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        issue_dk<D, kBF16>(tmem + kColDK, sDS + st * L::kDS, sQ + st * L::kQT, it > 0);
+        ok = mbar_wait(dq_empty, (it & 1) ^ 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        issue_dq<D, kBF16>(tmem + kColDQ, sK, sDS + st * L::kDS);
+        tc_commit(dq_full);
+        tc_commit(&q_empty[st]);
+        tc_commit(&ds_empty[st]);
+        if (it + 1 < N) {
+          issue_kt<D, kBF16>(tmem + kColDP, sV, sDO + nx * L::kQT);
+          tc_commit(dp_full);
+        }
+      }
+      if (ok) tc_commit(dkv_full);
+      tc_commit(mma_drain);
+      mbar_wait(mma_drain, 0, abort_flag);
+    }
+    __syncwarp();
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ P, dS and dK/dV epilogue
+    const int r = (warp & 3) * 32 + lane;
+    const int k = k0 + r;
+    const bool k_valid = k < p.Tk;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const float* sLSE = reinterpret_cast<const float*>(smem + L::kLSE);
+    const float* sDelta = reinterpret_cast<const float*>(smem + L::kDelta);
+    bool ok = true;
+    for (int it = 0; it < N; ++it) {
+      const int st = it & 1;
+      const int g = it / nq;
+      const int h = hk * G + g;
+      const int q0 = (first_qt + it % nq) * 64;
+      const uint32_t par = (it >> 1) & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], par, abort_flag) &&
+                                       mbar_wait(&q_full[st], par, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tS = tmem + lane_base + kColS + 64 * st;
+      uint32_t sr[64];
+      tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_wait_ld();
+
+      const float* lse = sLSE + st * 64;
+      const bool need_causal = p.causal && (k0 + 127 > q0 + p.causal_off);
+      const bool need_bounds = (q0 + 64 > p.Tq) || (k0 + 128 > p.Tk);
+      const float* score_col = nullptr;
+      const uint8_t* mask_col = nullptr;
+      if (kScore) score_col = p.score + b * p.score_stride[0] + h * p.score_stride[1] + k;
+      if (kMask) mask_col = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + k;
+      float pv[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const int q = q0 + c;
+        bool keep = true;
+        if (need_bounds) keep = k_valid && (q < p.Tq);
+        if (need_causal) keep = keep && (k <= q + p.causal_off);
+        float x = __uint_as_float(sr[c]);
+        if constexpr (kScore) {
+          if (keep) x += __ldg(score_col + static_cast<int64_t>(q) * p.score_stride[2]);
+        }
+        if constexpr (kMask) {
+          if (keep) keep = __ldg(mask_col + static_cast<int64_t>(q) * p.mask_stride[2]) != 0;
+        }
+        const float e = ex2(x * p.scale_log2 - lse[c]);
+        pv[c] = keep ? e : 0.f;
+      }
+      {
+        uint32_t pk[16];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = pack2<kBF16>(pv[32 * half + 2 * i], pv[32 * half + 2 * i + 1]);
+          tmem_st16(tS + 16 * half, pk);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full);
+
+      ok = __all_sync(0xffffffffu, mbar_wait(dp_full, it & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tDP = tmem + lane_base + kColDP;
+      tmem_ld32(tDP, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(tDP + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_wait_ld();
+      const float* delta = sDelta + st * 64;
+      uint32_t dsk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float d0 = pv[2 * i] * (__uint_as_float(sr[2 * i]) - delta[2 * i]) * p.scale;
+        const float d1 = pv[2 * i + 1] * (__uint_as_float(sr[2 * i + 1]) - delta[2 * i + 1]) * p.scale;
+        dsk[i] = pack2<kBF16>(d0, d1);
+      }
+      ok = __all_sync(0xffffffffu, mbar_wait(&ds_empty[st], par ^ 1, abort_flag));
+      if (!ok) break;
+      // Row r of the dS^T tile: 128 B in 8 chunks of 16 B, 128-B swizzled (chunk ^ (row % 8)).
+      uint8_t* ds_row = smem + L::kDSb + st * L::kDS + r * 128;
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc)
+        *reinterpret_cast<uint4*>(ds_row + ((cc ^ (r & 7)) << 4)) =
+            make_uint4(dsk[4 * cc], dsk[4 * cc + 1], dsk[4 * cc + 2], dsk[4 * cc + 3]);
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+
+    // dK / dV epilogue (zeros when no query interacts with this key tile).
+    uint16_t* dv_row = nullptr;
+    uint16_t* dk_row = nullptr;
+    if (k_valid) {
+      dv_row = reinterpret_cast<uint16_t*>(p.dv) + b * p.dv_stride[0] + static_cast<int64_t>(k) * p.dv_stride[1] +
+               hk * p.dv_stride[2];
+      dk_row = reinterpret_cast<uint16_t*>(p.dk) + b * p.dk_stride[0] + static_cast<int64_t>(k) * p.dk_stride[1] +
+               hk * p.dk_stride[2];
+    }
+    if (N > 0 && ok) {
+      ok = __all_sync(0xffffffffu, mbar_wait(dkv_full, 0, abort_flag));
+      tc_fence_after();
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t tA = tmem + lane_base + (which == 0 ? kColDV : kColDK);
+        uint16_t* dst_row = which == 0 ? dv_row : dk_row;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tA + 32 * c, v);
+          tmem_wait_ld();
+          if (k_valid) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = pack2<kBF16>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+            uint4* dst = reinterpret_cast<uint4*>(dst_row + 32 * c);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+          }
+        }
+      }
+    } else if (k_valid && N == 0) {
+#pragma unroll
+      for (int u = 0; u < D / 8; ++u) {
+        reinterpret_cast<uint4*>(dv_row)[u] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(dk_row)[u] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    tc_fence_before();
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ dQ drain
+    const int wq = warp & 3;
+    // M = D accumulator layout: D=128 uses all 128 lanes; D=64 (M=64) puts rows
+    // 16*wq .. 16*wq+15 in lanes 0-15 of each 32-lane quadrant.
+    const int d = (D == 128) ? (wq * 32 + lane) : (wq * 16 + lane);
+    const bool d_valid = (D == 128) || (lane < 16);
+    const uint32_t tDQ = tmem + (static_cast<uint32_t>(wq * 32) << 16) + kColDQ;
+    for (int it = 0; it < N; ++it) {
+      const int g = it / nq;
+      const int h = hk * G + g;
+      const int q0 = (first_qt + it % nq) * 64;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t v[64];
+      tmem_ld32(tDQ, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tmem_ld32(tDQ + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(dq_empty);
+      if (d_valid) {
+        float* base = p.dq_acc + ((static_cast<int64_t>(b) * p.Tq + q0) * p.Hq + h) * D + d;
+        const int64_t qstride = static_cast<int64_t>(p.Hq) * D;
+        const int qn = min(64, p.Tq - q0);
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (c < qn) red_add_f32(base + c * qstride, __uint_as_float(v[c]));
+      }
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && *reinterpret_cast<volatile int*>(abort_flag)) atomicOr(p.status, FA4D_DEV_TIMEOUT_BWD);
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Delta[b, h, t] = sum_d O * dO (0 for padding rows) and dq_acc row = 0.
+template <int D, bool kBF16>
+__global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
+  const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(p.B) * p.lse_ld * p.Hq;
+  if (w >= rows) return;
+  const int h = static_cast<int>(w % p.Hq);
+  const int t = static_cast<int>((w / p.Hq) % p.lse_ld);
+  const int b = static_cast<int>(w / (static_cast<int64_t>(p.Hq) * p.lse_ld));
+  float acc = 0.f;
+  if (t < p.Tq) {
+    constexpr int E = D / 32;  // elements per lane (2 or 4)
+    const uint16_t* o = reinterpret_cast<const uint16_t*>(p.o) + b * p.o_stride[0] +
+                        static_cast<int64_t>(t) * p.o_stride[1] + h * p.o_stride[2] + lane * E;
+    const uint16_t* g = reinterpret_cast<const uint16_t*>(p.dout) + b * p.do_stride[0] +
+                        static_cast<int64_t>(t) * p.do_stride[1] + h * p.do_stride[2] + lane * E;
+    if constexpr (E == 4) {
+      const uint2 ov = *reinterpret_cast<const uint2*>(o);
+      const uint2 gv = *reinterpret_cast<const uint2*>(g);
+      const float2 o0 = unpack2<kBF16>(ov.x), o1 = unpack2<kBF16>(ov.y);
+      const float2 g0 = unpack2<kBF16>(gv.x), g1 = unpack2<kBF16>(gv.y);
+      acc = o0.x * g0.x + o0.y * g0.y + o1.x * g1.x + o1.y * g1.y;
+    } else {
+      const uint32_t ov = *reinterpret_cast<const uint32_t*>(o);
+      const uint32_t gv = *reinterpret_cast<const uint32_t*>(g);
+      const float2 o0 = unpack2<kBF16>(ov), g0 = unpack2<kBF16>(gv);
+      acc = o0.x * g0.x + o0.y * g0.y;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    float* dq = p.dq_acc + ((static_cast<int64_t>(b) * p.Tq + t) * p.Hq + h) * D + lane * E;
+    if constexpr (E == 4)
+      *reinterpret_cast<float4*>(dq) = make_float4(0.f, 0.f, 0.f, 0.f);
+    else
+      *reinterpret_cast<float2*>(dq) = make_float2(0.f, 0.f);
+  }
+  if (lane == 0) p.delta[(static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t] = acc;
+}
+
+// dQ (input dtype) = dq_acc, 8 elements per thread.
+template <bool kBF16>
+__global__ void __launch_bounds__(256) dq_convert_kernel(const ConvertParams p) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int per_row = p.D / 8;
+  const int64_t total = static_cast<int64_t>(p.B) * p.Tq * p.Hq * per_row;
+  if (i >= total) return;
+  const int d8 = static_cast<int>(i % per_row);
+  const int64_t row = i / per_row;
+  const int h = static_cast<int>(row % p.Hq);
+  const int t = static_cast<int>((row / p.Hq) % p.Tq);
+  const int b = static_cast<int>(row / (static_cast<int64_t>(p.Hq) * p.Tq));
+  const float4* src = reinterpret_cast<const float4*>(p.dq_acc + row * p.D + d8 * 8);
+  const float4 a = src[0], c = src[1];
+  uint4 out = make_uint4(pack2<kBF16>(a.x, a.y), pack2<kBF16>(a.z, a.w), pack2<kBF16>(c.x, c.y),
+                         pack2<kBF16>(c.z, c.w));
+  uint16_t* dst = reinterpret_cast<uint16_t*>(p.dq) + b * p.dq_stride[0] + static_cast<int64_t>(t) * p.dq_stride[1] +
+                  h * p.dq_stride[2] + d8 * 8;
+  *reinterpret_cast<uint4*>(dst) = out;
+}
+
+template <int D, bool kBF16, bool kMask, bool kScore>
+cudaError_t launch_bwd_t(const BwdParams& p, cudaStream_t s) {
+  using L = BwdLayout<D>;
+  auto kern = bwd_kernel<D, kBF16, kMask, kScore>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+  if (e != cudaSuccess) return e;
+  dim3 grid((p.Tk + 127) / 128, p.Hk, p.B);
+  kern<<<grid, kBwdThreads, L::kAlloc, s>>>(p);
+  return cudaGetLastError();
+}
+
+template <int D, bool kBF16>
+cudaError_t launch_bwd_d(const BwdParams& p, bool m, bool sc, cudaStream_t s) {
+  if (m && sc) return launch_bwd_t<D, kBF16, true, true>(p, s);
+  if (m) return launch_bwd_t<D, kBF16, true, false>(p, s);
+  if (sc) return launch_bwd_t<D, kBF16, false, true>(p, s);
+  return launch_bwd_t<D, kBF16, false, false>(p, s);
+}
+
+}  // namespace
+
+cudaError_t launch_bwd(const BwdParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s) {
+  if (D == 128) return bf16 ? launch_bwd_d<128, true>(p, has_mask, has_score, s)
+                            : launch_bwd_d<128, false>(p, has_mask, has_score, s);
+  if (D == 64) return bf16 ? launch_bwd_d<64, true>(p, has_mask, has_score, s)
+                           : launch_bwd_d<64, false>(p, has_mask, has_score, s);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s) {
+  const int64_t rows = static_cast<int64_t>(p.B) * p.lse_ld * p.Hq;
+  const int64_t blocks = (rows * 32 + 255) / 256;
+  if (p.D == 128) {
+    if (bf16) bwd_prep_kernel<128, true><<<blocks, 256, 0, s>>>(p);
+    else bwd_prep_kernel<128, false><<<blocks, 256, 0, s>>>(p);
+  } else if (p.D == 64) {
+    if (bf16) bwd_prep_kernel<64, true><<<blocks, 256, 0, s>>>(p);
+    else bwd_prep_kernel<64, false><<<blocks, 256, 0, s>>>(p);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s) {
+  const int64_t total = static_cast<int64_t>(p.B) * p.Tq * p.Hq * (p.D / 8);
+  const int64_t blocks = (total + 255) / 256;
+  if (bf16) dq_convert_kernel<true><<<blocks, 256, 0, s>>>(p);
+  else dq_convert_kernel<false><<<blocks, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace fa4d

@@ -1,0 +1,87 @@
+// fa4d_kernels.h — parameter blocks handed to the sm_100a kernels and the launch
+// entry points the C ABI (fa4d_api.cu) dispatches to.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace fa4d {
+
+// Forward: one CTA owns 2 x 128 query rows of one (batch, query head) and streams
+// the key/value tiles of the matching KV head.
+struct FwdParams {
+  CUtensorMap tm_q;  // dims (D, Tq, Hq, B), box (64, 128, 1, 1), 128-B swizzle
+  CUtensorMap tm_k;  // dims (D, Tk, Hk, B), box (64, 128, 1, 1)
+  CUtensorMap tm_v;
+  void* o;
+  float* lse;
+  const uint8_t* mask;
+  const float* score;
+  int64_t o_stride[3];      // (b, t, h) elements
+  int64_t mask_stride[3];   // (b, h, row) elements
+  int64_t score_stride[3];
+  int32_t B, Tq, Tk, Hq, Hk;
+  int32_t lse_ld;           // LSE row stride (floats)
+  int32_t causal;           // 0 / 1 (a causal mode is on)
+  int32_t causal_off;       // key k is kept for query q iff k <= q + causal_off
+  float scale_log2;         // scale * log2(e)
+  int32_t mask_vec;         // 1: rows are 4-B aligned, 32-bit loads allowed
+  int32_t score_vec;        // 1: rows are 16-B aligned, 128-bit loads allowed
+  int* status;              // device status word (bounded-wait timeouts)
+};
+
+// Backward: one CTA owns 128 keys of one (batch, KV head), loops over every
+// query head of the GQA group and every 64-row query tile, accumulates dK/dV in
+// tensor memory and adds dQ into an fp32 accumulator.
+struct BwdParams {
+  CUtensorMap tm_q;   // dims (D, Tq, Hq, B), box (64, 64, 1, 1)
+  CUtensorMap tm_do;  // same for dO
+  CUtensorMap tm_k;   // dims (D, Tk, Hk, B), box (64, 128, 1, 1)
+  CUtensorMap tm_v;
+  const float* lse;     // [B, Hq, lse_ld]
+  const float* delta;   // [B, Hq, lse_ld]
+  float* dq_acc;        // [B, Tq, Hq, D] fp32, zeroed by the preprocess kernel
+  void* dk;
+  void* dv;
+  const uint8_t* mask;
+  const float* score;
+  int64_t dk_stride[3];
+  int64_t dv_stride[3];
+  int64_t mask_stride[3];
+  int64_t score_stride[3];
+  int32_t B, Tq, Tk, Hq, Hk;
+  int32_t lse_ld;
+  int32_t causal;
+  int32_t causal_off;
+  float scale_log2;
+  float scale;
+  int* status;
+};
+
+// Row dot products Delta = rowsum(O * dO) and zeroing of the dQ accumulator.
+struct PrepParams {
+  const void* o;
+  const void* dout;
+  float* delta;
+  float* dq_acc;
+  int64_t o_stride[3];
+  int64_t do_stride[3];
+  int32_t B, Tq, Hq, D;
+  int32_t lse_ld;
+};
+
+// dQ (input dtype, caller strides) = dQ accumulator.
+struct ConvertParams {
+  const float* dq_acc;
+  void* dq;
+  int64_t dq_stride[3];
+  int32_t B, Tq, Hq, D;
+};
+
+cudaError_t launch_fwd(const FwdParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);
+cudaError_t launch_bwd(const BwdParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);
+cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s);
+cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s);
+
+}  // namespace fa4d

@@ -1,0 +1,94 @@
+"""Autograd op ``flash_attention_with_4d_mask`` over the sm_100a C ABI.
+
+Drop-in for the reference op ``_flash_attention_with_4d_mask``
+(python/fa2.py:437-558): same positional signature
+``(Q, K, V, Mask, Score, scale, is_causal, use_atomic_backward, bhsd_input)``,
+output in the input layout, nine gradients (dQ, dK, dV and six ``None``).
+One optional tenth positional argument, ``causal_align`` ("top_left", the
+reference's semantics, or "bottom_right"), selects where the causal diagonal
+sits when Tq != Tk.
+
+Differences that do not change results: BHSD inputs are passed to the kernels as
+strided views instead of contiguous copies (a copy is made only when the strides
+cannot be described by a TMA tensor map), and all three gradients come back in the
+input dtype (the reference returns dQ in fp32 and lets autograd cast it,
+python/fa2.py:556).  ``use_atomic_backward`` is accepted for compatibility; both
+values run the same backward, in which dK/dV are summed over the GQA group inside
+the kernel and dQ is accumulated in fp32.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+_CAUSAL_ALIGN = {"top_left": _lib.CAUSAL_TOP_LEFT, "bottom_right": _lib.CAUSAL_BOTTOM_RIGHT}
+
+
+def causal_mode(is_causal: bool, causal_align: str = "top_left") -> int:
+    """Maps (is_causal, causal_align) to the C ABI's causal enum."""
+    if not is_causal:
+        return _lib.CAUSAL_NONE
+    try:
+        return _CAUSAL_ALIGN[causal_align]
+    except KeyError:
+        raise ValueError(f"unsupported causal_align: {causal_align}") from None
+
+
+def _fwd_views(Q, K, V, bhsd_input):
+    if bhsd_input:
+        Q, K, V = Q.transpose(1, 2), K.transpose(1, 2), V.transpose(1, 2)
+    return _lib.as_tma(Q), _lib.as_tma(K), _lib.as_tma(V)
+
+
+class _flash_attention_with_4d_mask(torch.autograd.Function):
+    @staticmethod
+    def forward(
+        ctx,
+        Q: torch.Tensor,
+        K: torch.Tensor,
+        V: torch.Tensor,
+        Mask: Optional[torch.Tensor] = None,
+        Score: Optional[torch.Tensor] = None,
+        scale: Optional[float] = None,
+        is_causal: Optional[bool] = False,
+        use_atomic_backward: Optional[bool] = True,
+        bhsd_input: Optional[bool] = True,
+        causal_align: str = "top_left",
+    ):
+        assert Q.dim() == 4 and K.dim() == 4 and V.dim() == 4
+        if not Q.is_cuda:
+            raise RuntimeError("flash_attention_with_4d_mask runs on CUDA (sm_100a) tensors only")
+        q, k, v = _fwd_views(Q, K, V, bhsd_input)
+        B, Tq, Hq, D = q.shape
+        if scale is None:
+            scale = D ** -0.5
+        mode = causal_mode(bool(is_causal), causal_align)
+        mask = _lib.prepare_bias(Mask, torch.bool) if Mask is not None else None
+        score = _lib.prepare_bias(Score, torch.float32) if Score is not None else None
+        O, LSE = _lib.forward(q, k, v, mask, score, float(scale), mode)
+        ctx.save_for_backward(q, k, v, O, LSE, mask, score)
+        ctx.scale = float(scale)
+        ctx.mode = mode
+        ctx.use_atomic_backward = use_atomic_backward
+        ctx.bhsd_input = bhsd_input
+        return O.transpose(1, 2) if bhsd_input else O
+
+    @staticmethod
+    def backward(ctx, dO: torch.Tensor):
+        q, k, v, O, LSE, mask, score = ctx.saved_tensors
+        if ctx.bhsd_input:
+            dO = dO.transpose(1, 2)
+        dO = _lib.as_tma(dO)
+        dQ, dK, dV = _lib.backward(dO, q, k, v, O, LSE, mask, score, ctx.scale, ctx.mode)
+        if ctx.bhsd_input:
+            dQ, dK, dV = dQ.transpose(1, 2), dK.transpose(1, 2), dV.transpose(1, 2)
+        return dQ, dK, dV, None, None, None, None, None, None, None
+
+
+flash_attention_with_4d_mask = _flash_attention_with_4d_mask.apply
+
+__all__ = ["flash_attention_with_4d_mask", "causal_mode"]

@@ -1,0 +1,140 @@
+/*
+ * fa4d.h — C ABI of the B200 (sm_100a) FlashAttention-2 forward/backward with an
+ * optional 4D bool mask and fp32 additive score.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes; no
+ * framework types cross this boundary.  The caller owns every buffer (inputs,
+ * outputs, LSE and the backward workspace).  The library keeps no state besides
+ * a per-device cache of the driver's tensor-map encoder and a device-side status
+ * word that kernels set when a bounded wait gives up.
+ *
+ * Layout convention (matches the kernels' native layout of the reference,
+ * python/fa2.py:38-44): Q/O/dO/dQ are [B, Tq, Hq, D] and K/V/dK/dV are
+ * [B, Tk, Hk, D], each described by element strides (batch, seq, head); the
+ * head-dim stride must be 1.  A BHSD tensor is passed as its transpose(1, 2)
+ * view, so no copy is needed.  mask is bool/uint8 and score is fp32, both
+ * [B or 1, Hq or 1, Tq, Tk] given by element strides (batch, head, row); a
+ * broadcast dimension may have stride 0; the key stride must be 1.
+ *
+ * Return value: 0 on success, a negative FA4D_ERR_* code otherwise;
+ * fa4d_last_error() gives a message for the calling thread.  All work is
+ * enqueued on the given stream (a cudaStream_t, NULL = legacy default stream)
+ * and nothing synchronises with the host.
+ */
+#ifndef FA4D_H_
+#define FA4D_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FA4D_ABI_VERSION 1
+
+enum fa4d_dtype { FA4D_BF16 = 0, FA4D_F16 = 1 };
+
+/* Causal alignment.  TOP_LEFT keeps key k for query q when k <= q, which is the
+ * reference's is_causal semantics (python/fa2.py:75,95 and
+ * benchmark/precision_check.py:164-167).  BOTTOM_RIGHT keeps k <= q + (Tk - Tq). */
+enum fa4d_causal { FA4D_CAUSAL_NONE = 0, FA4D_CAUSAL_TOP_LEFT = 1, FA4D_CAUSAL_BOTTOM_RIGHT = 2 };
+
+enum fa4d_status {
+  FA4D_OK = 0,
+  FA4D_ERR_INVALID = -1,     /* bad pointer, shape, stride or enum value */
+  FA4D_ERR_UNSUPPORTED = -2, /* valid but not built: head dim not in {64, 128} */
+  FA4D_ERR_CUDA = -3,        /* a CUDA runtime call or kernel launch failed */
+  FA4D_ERR_DRIVER = -4,      /* cuTensorMapEncodeTiled unavailable or failed */
+  FA4D_ERR_LAYOUT = -5,      /* strides/base not 16-byte aligned for TMA: pass a contiguous copy */
+  FA4D_ERR_WORKSPACE = -6    /* workspace missing or smaller than fa4d_bwd_workspace_size() */
+};
+
+typedef struct fa4d_fwd_args {
+  const void* q;           /* [B, Tq, Hq, D] */
+  const void* k;           /* [B, Tk, Hk, D] */
+  const void* v;           /* [B, Tk, Hk, D] */
+  void* o;                 /* [B, Tq, Hq, D], written */
+  float* lse;              /* [B, Hq, fa4d_lse_row_stride(Tq)] fp32, written (log2 domain) */
+  const uint8_t* mask;     /* optional, NULL = none; nonzero byte = keep */
+  const float* score;      /* optional, NULL = none; added to QK^T before scaling */
+  int64_t q_stride[3];     /* element strides (batch, seq, head) */
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  int64_t mask_stride[3];  /* element strides (batch, head, row) */
+  int64_t score_stride[3];
+  int32_t B, Tq, Tk, Hq, Hk, D;
+  int32_t dtype;           /* enum fa4d_dtype */
+  int32_t causal;          /* enum fa4d_causal */
+  float scale;             /* softmax scale applied to (QK^T + score) */
+  int32_t reserved[3];
+} fa4d_fwd_args;
+
+typedef struct fa4d_bwd_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;           /* forward output */
+  const void* dout;        /* [B, Tq, Hq, D] upstream gradient */
+  const float* lse;        /* as written by fa4d_fwd */
+  const uint8_t* mask;
+  const float* score;
+  void* dq;                /* [B, Tq, Hq, D] written, input dtype */
+  void* dk;                /* [B, Tk, Hk, D] written, input dtype (sum over the GQA group) */
+  void* dv;
+  int64_t q_stride[3];
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  int64_t do_stride[3];
+  int64_t dq_stride[3];
+  int64_t dk_stride[3];
+  int64_t dv_stride[3];
+  int64_t mask_stride[3];
+  int64_t score_stride[3];
+  int32_t B, Tq, Tk, Hq, Hk, D;
+  int32_t dtype;
+  int32_t causal;
+  float scale;
+  int32_t deterministic;   /* reserved, must be 0 */
+  void* workspace;         /* device scratch, >= fa4d_bwd_workspace_size() bytes, 256-B aligned */
+  size_t workspace_bytes;
+} fa4d_bwd_args;
+
+/* Row stride (in floats) of the LSE buffer: Tq rounded up to a multiple of 128.
+ * The LSE buffer holds B * Hq * fa4d_lse_row_stride(Tq) floats. */
+int64_t fa4d_lse_row_stride(int32_t Tq);
+
+/* Bytes of device scratch fa4d_bwd needs: an fp32 dQ accumulator [B, Tq, Hq, D]
+ * and the fp32 row dot products Delta [B, Hq, fa4d_lse_row_stride(Tq)]. */
+size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D);
+
+/* Forward: O = softmax(((Q K^T + score) * scale) masked) V and LSE.
+ * Replaces the launch of flash_attention_fwd_with_4d_mask at
+ * python/fa2.py:474-478 (kernel python/fa2.py:22-139). */
+int fa4d_fwd(const fa4d_fwd_args* args, void* stream);
+
+/* Backward: dQ, dK, dV from dO.  Replaces bwd_preprocess plus
+ * flash_attention_bwd_with_4d_mask_atomic / _reduce and the host-side casts and
+ * sums at python/fa2.py:508-549 (kernels python/fa2.py:142-426). */
+int fa4d_bwd(const fa4d_bwd_args* args, void* stream);
+
+/* Message for the last non-zero return on this thread ("" if none). */
+const char* fa4d_last_error(void);
+
+/* Reads (and with clear != 0 resets) the device status word after synchronising
+ * the stream: 0 = no kernel gave up a bounded wait; otherwise a bit set of
+ * FA4D_DEV_* flags.  Returns a negative FA4D_ERR_* code if the read fails. */
+#define FA4D_DEV_TIMEOUT_FWD 1
+#define FA4D_DEV_TIMEOUT_BWD 2
+int fa4d_device_status(void* stream, int clear);
+
+/* FA4D_ABI_VERSION of the loaded library. */
+int fa4d_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA4D_H_ */
