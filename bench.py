@@ -1,0 +1,521 @@
+#!/usr/bin/env python
+"""Benchmark of the attention hot path on B200: one JSON line on rank 0.
+
+Workload (a "step"): one forward + backward of FlashAttention-2 at the reference's
+headline configuration B=1, Tq=Tk=8192, Hq=32, Hk=8, D=128, bf16, non-causal, no
+mask/score (synthetic N(0,1) inputs), per GPU.  Multi-GPU runs are weak-scaled:
+rank r owns batch element r of a global batch of N (whole GQA groups, no data-path
+collective); NCCL is used only for the barrier, the max-over-ranks timing and a
+verification all-gather of per-rank output checksums outside the timed region.
+
+``value`` is whole-job TFLOP/s under the reference's FLOP convention
+(14 * B * Hq * Tq * Tk * D per fwd+bwd, benchmark/throughput_check.py:85-92) with
+inputs resident in HBM; ``e2e`` is the same metric through the public API
+(``tilelang_flash_attention`` + autograd) with pinned host inputs and outputs,
+host<->device copies inside the timed region.  ``--impl reference`` times the
+reference's own CPU path (its fp32 eager attention, restated in oracle/eager.py)
+on the host cores.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+(torchrun for N > 1).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "attn fwd & fwd+bwd TFLOPS/B200 (bf16 T8192 Hq32 Hk8 D128), % tensor/HBM roof"
+UNIT = "TFLOP/s"
+B, T, HQ, HK, D = 1, 8192, 32, 8, 128
+WORKLOAD = "cfg2: B1 Tq=Tk=8192 Hq32 Hk8 D128 bf16 non-causal, fwd+bwd per GPU"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) per launch of the backward main kernel at this workload,
+# from an ncu capture (profiles/bwd_main_cfg2.md); None until captured.
+NCU_BWD_MAIN_TRAFFIC = None
+L2_FLUSH_BYTES = 256 << 20
+
+
+def fwd_flops(b, hq, tq, tk, d, causal):
+    return 4.0 * b * hq * tq * tk * d * (0.5 if causal else 1.0)
+
+
+def fwd_bwd_flops(b, hq, tq, tk, d, causal):
+    return 14.0 * b * hq * tq * tk * d * (0.5 if causal else 1.0)
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling every 200 ms while the timed region runs."""
+
+    FIELDS = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.out = None
+        self.error = None
+        props = torch.cuda.get_device_properties(device)
+        self.bus = getattr(props, "pci_bus_id", None)
+        try:
+            self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.out, stderr=subprocess.STDOUT)
+        except Exception as e:  # no nvidia-smi
+            self.proc = None
+            self.error = f"{type(e).__name__}: {e}"
+
+    @staticmethod
+    def _bus_of(field: str):
+        try:  # "00000000:1B:00.0" -> 0x1B
+            return int(field.split(":")[1], 16)
+        except (IndexError, ValueError):
+            return None
+
+    def stop(self):
+        if self.proc is None:
+            return {"error": self.error or "nvidia-smi not started"}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.out.flush()
+        text = Path(self.out.name).read_text()
+        os.unlink(self.out.name)
+        rows = [[x.strip() for x in r.split(",")] for r in text.strip().splitlines() if r.strip()]
+        buses = {self._bus_of(r[0]) for r in rows if len(r) >= 9}
+        sm, mx, reasons = [], [], set()
+        for r in rows:
+            if len(r) < 9:
+                continue
+            if len(buses) > 1 and self.bus is not None and self._bus_of(r[0]) != self.bus:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for name, val in zip(self.NAMES, r[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"error": "no samples: " + text.strip()[:200]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- our arm
+def run_ours(args):
+    from fa2_with_4d_mask_b200 import _lib  # noqa: E402  (registered by the import below)
+    return _run_ours(args, _lib)
+
+
+def _run_ours(args, _lib):
+    import tilelang_fa2_4d_mask as api
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    peaks, peak_src = load_peaks()
+
+    # Rank r owns batch element r of the global batch (weak scaling).
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    mk = lambda shape: torch.randn(shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    q = mk((B, T, HQ, D))
+    k = mk((B, T, HK, D))
+    v = mk((B, T, HK, D))
+    do = mk((B, T, HQ, D))
+    scale = D ** -0.5
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    rec = {"fwd": [], "preprocess": [], "main": [], "dq_convert": [], "step": []}
+
+    def step(timed):
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        o, lse = _lib.forward(q, k, v, None, None, scale, _lib.CAUSAL_NONE)
+        e1.record(stream)
+        marks = []
+
+        def stage(name, launch):
+            a, b = ev(), ev()
+            a.record(stream)
+            launch()
+            b.record(stream)
+            marks.append((name, a, b))
+
+        _lib.backward(do, q, k, v, o, lse, None, None, scale, _lib.CAUSAL_NONE, stages=stage)
+        if timed:
+            rec["fwd"].append((e0, e1))
+            for name, a, b in marks:
+                rec[name].append((a, b))
+            rec["step"].append((e0, marks[-1][2]))
+        return o
+
+    sampler = ClockSampler(dev) if rank == 0 else None  # started early: nvidia-smi needs ~0.5 s to begin
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    for _ in range(args.steps):
+        flush.zero_()  # L2 flush between steps, outside the step's events
+        o = step(True)
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop() if sampler else None
+
+    ms = {k2: sum(a.elapsed_time(b) for a, b in v2) / max(1, len(v2)) for k2, v2 in rec.items()}
+    step_ms = torch.tensor([ms["step"]], device=dev, dtype=torch.float64)
+    if dist:
+        dist.all_reduce(step_ms, op=dist.ReduceOp.MAX)
+        # Verification only (outside the timed region): per-rank output checksums.
+        chk = o.float().abs().sum().reshape(1)
+        allchk = [torch.zeros_like(chk) for _ in range(world)]
+        dist.all_gather(allchk, chk)
+        if rank == 0 and not all(torch.isfinite(c).all() for c in allchk):
+            raise SystemExit("non-finite output on some rank")
+    t_step = float(step_ms.item())
+    per_rank = fwd_bwd_flops(B, HQ, T, T, D, False)
+    value = world * per_rank / (t_step * 1e-3) / 1e12
+    status = _lib.device_status(dev)
+
+    if rank != 0:
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return None
+
+    bwd_main_flops = fwd_bwd_flops(B, HQ, T, T, D, False) - fwd_flops(B, HQ, T, T, D, False)
+    main_tflops = bwd_main_flops / (ms["main"] * 1e-3) / 1e12
+    fwd_tflops = fwd_flops(B, HQ, T, T, D, False) / (ms["fwd"] * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"]
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic N(0,1) inputs, seeded per rank",
+        "config": {
+            "workload": WORKLOAD,
+            "global_batch": world * B,
+            "seq_len": T,
+            "heads_q": HQ,
+            "heads_kv": HK,
+            "head_dim": D,
+            "parallelism": f"dp{world} (batch shards, whole GQA groups per GPU, no data-path collective)",
+            "l2": "flushed between steps (256 MiB write outside the step's events)",
+        },
+        "fwd_tflops": round(fwd_tflops, 2),
+        "fwd_frac_of_peak": round(fwd_tflops / peak, 4),
+        "fwd_bwd_frac_of_peak": round(value / world / peak, 4),
+        "kernel_ms": {k2: round(v2, 4) for k2, v2 in ms.items() if k2 != "step"},
+        "roofline": {
+            "kernel": "bwd_kernel<128,bf16> (fa4d_bwd_main)",
+            "bound": "tensor",
+            "achieved": round(main_tflops, 2),
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": round(main_tflops / peak, 4),
+            "peak_source": f"{peak_src} bf16_tflops (burst, MEASURED_PEAKS.json)" if peak_src == "measured"
+            else "fallback 1590 TFLOP/s",
+            "algorithmic": "10*B*Hq*Tq*Tk*D FLOP per launch (bwd share of the 14x convention)",
+            "traffic": NCU_BWD_MAIN_TRAFFIC,
+        },
+        "gpu_launches": 4 * args.steps,
+        "device_status": status,
+        "clocks": clocks,
+    }
+    if args.extra and world == 1:
+        line["extra"] = extra_measurements(_lib, dev, peaks)
+    if args.e2e_steps > 0:
+        line["e2e"] = run_e2e(api, dev, args)
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return line
+
+
+def time_fn(fn, iters, warm=2):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+
+def _dev_inputs(dev, b, tq, tk, hq, hk, d, seed):
+    """Seeded N(0,1) bf16 BHSD views over [B, T, H, D] storage, generated on the device."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    mk = lambda t, h: torch.randn((b, t, h, d), generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
+    return mk(tq, hq), mk(tk, hk), mk(tk, hk), mk(tq, hq)
+
+
+def _alibi_score(dev, b, h, tq, tk, seed=3):
+    """fp32 [B, H, Tq, Tk] = 2^(-8(h+1)/H) * (k - q) + N(0, 0.5^2)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    slopes = torch.tensor([2.0 ** (-8.0 * (i + 1) / h) for i in range(h)], device=dev).view(1, h, 1, 1)
+    rel = (torch.arange(tk, device=dev).view(1, 1, 1, tk) - torch.arange(tq, device=dev).view(1, 1, tq, 1)).float()
+    return slopes * rel + 0.5 * torch.randn((b, h, tq, tk), generator=g, device=dev)
+
+
+def _bernoulli_mask(dev, b, h, tq, tk, keep, seed=4):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    m = torch.rand((b, h, tq, tk), generator=g, device=dev) < keep
+    i = torch.arange(min(tq, tk), device=dev)
+    m[:, :, i, i] = True
+    return m
+
+
+def _packed_doc_mask(dev, b, t, lo=128, hi=1024, seed=2):
+    """[B, 1, T, T]: causal inside seeded documents of length U[lo, hi], False across."""
+    g = torch.Generator()
+    g.manual_seed(seed)
+    doc = torch.empty((b, t), dtype=torch.int32)
+    for bi in range(b):
+        s, n = 0, 0
+        while s < t:
+            ln = int(torch.randint(lo, hi + 1, (1,), generator=g))
+            doc[bi, s:s + ln] = n
+            s, n = s + ln, n + 1
+    doc = doc.to(dev)
+    same = doc[:, :, None] == doc[:, None, :]
+    causal = torch.ones((t, t), dtype=torch.bool, device=dev).tril()
+    return (same & causal).unsqueeze(1)
+
+
+def extra_measurements(_lib, dev, peaks):
+    """The other benchmark configurations, a few iterations each (context, not `value`)."""
+    out = {}
+    peak = peaks["bf16_tflops"]
+
+    def fb(b, tq, tk, hq, hk, d, causal_mode, mask=None, score=None, iters=5):
+        q, k, v, do = (x.transpose(1, 2) for x in _dev_inputs(dev, b, tq, tk, hq, hk, d, seed=3))
+        sc = d ** -0.5
+        tf = time_fn(lambda: _lib.forward(q, k, v, mask, score, sc, causal_mode), iters)
+        o, lse = _lib.forward(q, k, v, mask, score, sc, causal_mode)
+        tb = time_fn(lambda: _lib.backward(do, q, k, v, o, lse, mask, score, sc, causal_mode), iters)
+        return tf, tb
+
+    tf, tb = fb(B, T, T, HQ, HK, D, _lib.CAUSAL_TOP_LEFT)
+    ff, fbf = fwd_flops(B, HQ, T, T, D, True), fwd_bwd_flops(B, HQ, T, T, D, True)
+    out["cfg2_causal"] = {"fwd_ms": round(tf, 4), "fwd_tflops": round(ff / tf / 1e9, 1),
+                          "fwd_bwd_ms": round(tf + tb, 4), "fwd_bwd_tflops": round(fbf / (tf + tb) / 1e9, 1),
+                          "fwd_frac": round(ff / tf / 1e9 / peak, 4),
+                          "fwd_bwd_frac": round(fbf / (tf + tb) / 1e9 / peak, 4)}
+    # cfg4: ALiBi-style fp32 score + Bernoulli(0.9) bool mask, MHA, non-causal (HBM-bound)
+    b4, t4, h4 = 1, 4096, 16
+    score = _alibi_score(dev, b4, h4, t4, t4)
+    mask = _bernoulli_mask(dev, b4, h4, t4, t4, 0.9)
+    tf, tb = fb(b4, t4, t4, h4, h4, D, _lib.CAUSAL_NONE, mask=mask, score=score, iters=3)
+    bytes_fwd = score.numel() * 4 + mask.numel() + 4 * b4 * t4 * h4 * D * 2
+    out["cfg4_score_mask"] = {"fwd_ms": round(tf, 4), "fwd_gbs": round(bytes_fwd / tf / 1e6, 1),
+                              "fwd_frac_hbm": round(bytes_fwd / tf / 1e6 / peaks["hbm_gbs"], 4),
+                              "fwd_bwd_ms": round(tf + tb, 4),
+                              "algorithmic_fwd_bytes": bytes_fwd}
+    del score, mask
+    # cfg3: packed-document [B,1,T,T] mask
+    b3, t3 = 2, 4096
+    mask = _packed_doc_mask(dev, b3, t3)
+    tf, tb = fb(b3, t3, t3, HQ, HK, D, _lib.CAUSAL_NONE, mask=mask.expand(b3, HQ, t3, t3), iters=3)
+    ff, fbf = fwd_flops(b3, HQ, t3, t3, D, False), fwd_bwd_flops(b3, HQ, t3, t3, D, False)
+    out["cfg3_packed_docs"] = {"fwd_ms": round(tf, 4), "fwd_bwd_ms": round(tf + tb, 4),
+                               "fwd_dense_equiv_tflops": round(ff / tf / 1e9, 1),
+                               "fwd_bwd_dense_equiv_tflops": round(fbf / (tf + tb) / 1e9, 1)}
+    del mask
+    # cfg5: MQA, bshd, bottom-right causal, one GPU's shard of 16 (B=2)
+    tf, tb = fb(2, 1024, 4096, 64, 1, 64, _lib.CAUSAL_BOTTOM_RIGHT, iters=3)
+    ff, fbf = fwd_flops(2, 64, 1024, 4096, 64, True), fwd_bwd_flops(2, 64, 1024, 4096, 64, True)
+    out["cfg5_mqa_shard_b2"] = {"fwd_ms": round(tf, 4), "fwd_bwd_ms": round(tf + tb, 4),
+                                "fwd_bwd_tflops_convention": round(fbf / (tf + tb) / 1e9, 1)}
+    return out
+
+
+def run_e2e(api, dev, args):
+    """Same metric through the public API with pinned host buffers: each step copies
+    q/k/v/dO host->device, runs forward + autograd backward and copies O, dQ, dK, dV
+    device->host."""
+    g = torch.Generator()
+    g.manual_seed(77)
+    host = lambda shape: torch.randn(shape, generator=g).to(torch.bfloat16).pin_memory()
+    hq, hk, hv, hdo = host((B, T, HQ, D)), host((B, T, HK, D)), host((B, T, HK, D)), host((B, T, HQ, D))
+    outs = [torch.empty((B, T, HQ, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)] + \
+           [torch.empty((B, T, HK, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hdo))
+    d2h = sum(x.numel() * x.element_size() for x in outs)
+
+    def step():
+        q = hq.to(dev, non_blocking=True).transpose(1, 2).requires_grad_(True)
+        k = hk.to(dev, non_blocking=True).transpose(1, 2).requires_grad_(True)
+        v = hv.to(dev, non_blocking=True).transpose(1, 2).requires_grad_(True)
+        do = hdo.to(dev, non_blocking=True).transpose(1, 2)
+        o = api.tilelang_flash_attention(q, k, v)
+        o.backward(do)
+        for dst, src in zip(outs, (o, q.grad, k.grad, v.grad)):
+            dst.copy_(src.detach().transpose(1, 2), non_blocking=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.e2e_steps):
+        step()
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / args.e2e_steps
+    return {"value": round(fwd_bwd_flops(B, HQ, T, T, D, False) / (ms * 1e-3) / 1e12, 2), "unit": UNIT,
+            "ms_per_step": round(ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": "tilelang_flash_attention + autograd backward, pinned host in/out"}
+
+
+# --------------------------------------------------------------------------- CPU arms
+def cpu_sample_step(hq_sample):
+    """One fwd+bwd of the reference's eager fp32 attention on the host: query heads
+    0..hq_sample-1 of the workload with their KV head (T=8192, D=128)."""
+    from oracle import inputs as I
+    from oracle.eager import attention_ref_grads
+
+    hk_sample = max(1, hq_sample // (HQ // HK))
+    q, k, v, do = I.qkv(1, T, T, hq_sample, hk_sample, D, seed=5)
+    t0 = time.perf_counter()
+    attention_ref_grads(q, k, v, do, None, None, scale=D ** -0.5, is_causal=False)
+    return time.perf_counter() - t0, fwd_bwd_flops(1, hq_sample, T, T, D, False)
+
+
+def cpu_baseline(args):
+    torch.set_num_threads(os.cpu_count() or 1)
+    cpu_sample_step(1)  # warm-up
+    secs, flops = [], 0.0
+    for _ in range(3):
+        s, flops = cpu_sample_step(4)
+        secs.append(s)
+    s = statistics.median(secs)
+    return {"value": round(flops / s / 1e12, 5), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": "oracle/eager.py (restated eager_ref, fp32) fwd+bwd on one GQA group "
+                      "(4 query heads, 1 KV head) of the workload, median of 3 after 1 warm-up"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return None
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        cpu_sample_step(1)
+    secs, flops = [], 0.0
+    for _ in range(args.steps):
+        s, flops = cpu_sample_step(1)
+        secs.append(s)
+    ms = 1e3 * sum(secs) / len(secs)
+    value = flops / (ms * 1e-3) / 1e12
+    sample = ("reference eager fp32 attention (oracle/eager.py restatement of "
+              "benchmark/precision_check.py:133-180) fwd+bwd on query head 0 and its KV head of the workload "
+              "(T=8192, D=128) per step, on the host cores")
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 5),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic N(0,1) inputs, seeded",
+        "config": {"workload": WORKLOAD, "global_batch": world * B, "seq_len": T,
+                   "parallelism": "host CPU, rank 0 only"},
+        "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-extra", dest="extra", action="store_false")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        line = run_reference(args)
+    else:
+        import tilelang_fa2_4d_mask  # noqa: F401  (registers fa2_with_4d_mask_b200)
+
+        line = run_ours(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -38,6 +38,9 @@ EXPORTED_SYMBOLS = (
     "fa4d_bwd_workspace_size",
     "fa4d_fwd",
     "fa4d_bwd",
+    "fa4d_bwd_preprocess",
+    "fa4d_bwd_main",
+    "fa4d_bwd_dq_convert",
     "fa4d_last_error",
     "fa4d_device_status",
     "fa4d_abi_version",
@@ -137,11 +140,13 @@ def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
     lib.fa4d_bwd_workspace_size.restype = ctypes.c_size_t
     lib.fa4d_fwd.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
     lib.fa4d_fwd.restype = ctypes.c_int
-    lib.fa4d_bwd.argtypes = [ctypes.POINTER(BwdArgs), ctypes.c_void_p]
-    lib.fa4d_bwd.restype = ctypes.c_int
+    for name in ("fa4d_bwd", "fa4d_bwd_preprocess", "fa4d_bwd_main", "fa4d_bwd_dq_convert"):
+        fn = getattr(lib, name)
+        fn.argtypes = [ctypes.POINTER(BwdArgs), ctypes.c_void_p]
+        fn.restype = ctypes.c_int
     lib.fa4d_last_error.argtypes = []
     lib.fa4d_last_error.restype = ctypes.c_char_p
-    lib.fa4d_device_status.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    lib.fa4d_device_status.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_int]
     lib.fa4d_device_status.restype = ctypes.c_int
     lib.fa4d_abi_version.argtypes = []
     lib.fa4d_abi_version.restype = ctypes.c_int
@@ -267,9 +272,15 @@ def backward(
     score: Optional[torch.Tensor],
     scale: float,
     causal: int,
+    stages=None,
 ) -> tuple:
     """Runs fa4d_bwd on [B, T, H, D] views.  Returns (dQ, dK, dV) contiguous in the
-    input dtype, dK/dV summed over the GQA group."""
+    input dtype, dK/dV summed over the GQA group.
+
+    ``stages`` optionally replaces the single fa4d_bwd call by a list of callables
+    ``f(name, launch)``; each receives the stage name ("preprocess", "main",
+    "dq_convert") and a zero-argument function that enqueues that stage, so a caller
+    can bracket each stage (e.g. with CUDA events)."""
     lib = load_library()
     B, Tq, Hq, D = q.shape
     Tk, Hk = k.shape[1], k.shape[2]
@@ -302,18 +313,32 @@ def backward(
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws_bytes
     with torch.cuda.device(q.device):
-        rc = lib.fa4d_bwd(ctypes.byref(a), _stream_ptr(q.device))
-    if rc != FA4D_OK:
-        _raise(lib, rc, "fa4d_bwd")
+        stream = _stream_ptr(q.device)
+        if stages is None:
+            rc = lib.fa4d_bwd(ctypes.byref(a), stream)
+            if rc != FA4D_OK:
+                _raise(lib, rc, "fa4d_bwd")
+        else:
+            for name in ("preprocess", "main", "dq_convert"):
+                fn = getattr(lib, "fa4d_bwd_" + name)
+
+                def launch(fn=fn, name=name):
+                    rc = fn(ctypes.byref(a), stream)
+                    if rc != FA4D_OK:
+                        _raise(lib, rc, "fa4d_bwd_" + name)
+
+                stages(name, launch)
     return dq, dk, dv
 
 
 def device_status(device: Optional[torch.device] = None, clear: bool = True) -> int:
     """Synchronises the current stream and returns the kernels' timeout bits (0 = none)."""
     lib = load_library()
-    device = device or torch.device("cuda", torch.cuda.current_device())
+    device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
     with torch.cuda.device(device):
-        rc = lib.fa4d_device_status(_stream_ptr(device), 1 if clear else 0)
+        rc = lib.fa4d_device_status(device.index, _stream_ptr(device), 1 if clear else 0)
     if rc < 0:
         _raise(lib, rc, "fa4d_device_status")
     return rc

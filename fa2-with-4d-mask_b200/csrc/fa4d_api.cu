@@ -64,6 +64,25 @@ int* status_word_ptr() {
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Makes the device that owns `ptr` current for this library on the calling thread.
+// The library links its own CUDA runtime, so the caller's current-device setting
+// is not visible here; the driver calls below (tensor-map encoding) need the
+// owning device's context current on this thread (autograd runs backward on a
+// worker thread of its own).
+int bind_device_of(const void* ptr, const char* name) {
+  cudaPointerAttributes at;
+  cudaError_t e = cudaPointerGetAttributes(&at, ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FA4D_ERR_INVALID, "%s: not a CUDA pointer (%s)", name, cudaGetErrorString(e));
+  }
+  if (at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged)
+    return fail(FA4D_ERR_INVALID, "%s: not device memory", name);
+  if ((e = cudaSetDevice(at.device)) != cudaSuccess)
+    return fail(FA4D_ERR_CUDA, "cudaSetDevice(%d) failed: %s", at.device, cudaGetErrorString(e));
+  return FA4D_OK;
+}
+
 // Tensor map over a [B, T, H, D] 16-bit tensor given element strides (b, t, h):
 // dims (D, T, H, B), box (64, rows, 1, 1), 128-B swizzle, zero fill out of bounds.
 int encode_bthd(CUtensorMap* m, const void* ptr, int B, int T, int H, int D, const int64_t st[3], int rows,
@@ -140,7 +159,9 @@ const char* fa4d_last_error(void) { return g_last_error.c_str(); }
 
 int fa4d_abi_version(void) { return FA4D_ABI_VERSION; }
 
-int fa4d_device_status(void* stream, int clear) {
+int fa4d_device_status(int device, void* stream, int clear) {
+  cudaError_t se = cudaSetDevice(device);
+  if (se != cudaSuccess) return fail(FA4D_ERR_CUDA, "cudaSetDevice(%d) failed: %s", device, cudaGetErrorString(se));
   int* word = status_word_ptr();
   if (!word) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -161,6 +182,7 @@ int fa4d_fwd(const fa4d_fwd_args* a, void* stream) {
   if (rc) return rc;
   if (!a->q || !a->k || !a->v || !a->o || !a->lse) return fail(FA4D_ERR_INVALID, "q, k, v, o and lse are required");
   if ((rc = check_rows16(a->o, a->o_stride, "o"))) return rc;
+  if ((rc = bind_device_of(a->q, "q"))) return rc;
   const bool bf16 = a->dtype == FA4D_BF16;
   fa4d::FwdParams p;
   memset(&p, 0, sizeof(p));
@@ -197,7 +219,21 @@ int fa4d_fwd(const fa4d_fwd_args* a, void* stream) {
   return ok();
 }
 
-int fa4d_bwd(const fa4d_bwd_args* a, void* stream) {
+}  // extern "C"
+
+namespace {
+
+struct BwdPlan {
+  fa4d::BwdParams main;
+  fa4d::PrepParams prep;
+  fa4d::ConvertParams convert;
+  bool bf16;
+  int D;
+  bool has_mask, has_score;
+};
+
+// Validates a backward call and fills the parameter blocks of its three stages.
+int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   if (!a) return fail(FA4D_ERR_INVALID, "args is NULL");
   int rc = check_common(a->B, a->Tq, a->Tk, a->Hq, a->Hk, a->D, a->dtype, a->causal, a->scale);
   if (rc) return rc;
@@ -208,21 +244,26 @@ int fa4d_bwd(const fa4d_bwd_args* a, void* stream) {
   if ((rc = check_rows16(a->dk, a->dk_stride, "dk"))) return rc;
   if ((rc = check_rows16(a->dv, a->dv_stride, "dv"))) return rc;
   if ((rc = check_rows16(a->o, a->o_stride, "o"))) return rc;
+  if ((rc = check_rows16(a->dout, a->do_stride, "dout"))) return rc;
   const size_t need = fa4d_bwd_workspace_size(a->B, a->Tq, a->Hq, a->D);
   if (!a->workspace || a->workspace_bytes < need || !aligned(a->workspace, 256))
     return fail(FA4D_ERR_WORKSPACE, "workspace must be 256-B aligned and hold %zu bytes (got %zu)", need,
                 a->workspace_bytes);
+  if ((rc = bind_device_of(a->q, "q"))) return rc;
   const bool bf16 = a->dtype == FA4D_BF16;
   const int64_t lse_ld = lse_ld_of(a->Tq);
   float* dq_acc = static_cast<float*>(a->workspace);
   const size_t dq_bytes = static_cast<size_t>(a->B) * a->Tq * a->Hq * a->D * sizeof(float);
   float* delta = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + (dq_bytes + 255) / 256 * 256);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* status = status_word_ptr();
   if (!status) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
 
-  fa4d::BwdParams p;
-  memset(&p, 0, sizeof(p));
+  memset(plan, 0, sizeof(*plan));
+  plan->bf16 = bf16;
+  plan->D = a->D;
+  plan->has_mask = a->mask != nullptr;
+  plan->has_score = a->score != nullptr;
+  fa4d::BwdParams& p = plan->main;
   if ((rc = encode_bthd(&p.tm_q, a->q, a->B, a->Tq, a->Hq, a->D, a->q_stride, 64, bf16, "q"))) return rc;
   if ((rc = encode_bthd(&p.tm_do, a->dout, a->B, a->Tq, a->Hq, a->D, a->do_stride, 64, bf16, "dout"))) return rc;
   if ((rc = encode_bthd(&p.tm_k, a->k, a->B, a->Tk, a->Hk, a->D, a->k_stride, 128, bf16, "k"))) return rc;
@@ -252,8 +293,7 @@ int fa4d_bwd(const fa4d_bwd_args* a, void* stream) {
   p.scale = a->scale;
   p.status = status;
 
-  fa4d::PrepParams pp;
-  memset(&pp, 0, sizeof(pp));
+  fa4d::PrepParams& pp = plan->prep;
   pp.o = a->o;
   pp.dout = a->dout;
   pp.delta = delta;
@@ -268,8 +308,7 @@ int fa4d_bwd(const fa4d_bwd_args* a, void* stream) {
   pp.D = a->D;
   pp.lse_ld = static_cast<int32_t>(lse_ld);
 
-  fa4d::ConvertParams cp;
-  memset(&cp, 0, sizeof(cp));
+  fa4d::ConvertParams& cp = plan->convert;
   cp.dq_acc = dq_acc;
   cp.dq = a->dq;
   for (int i = 0; i < 3; ++i) cp.dq_stride[i] = a->dq_stride[i];
@@ -277,14 +316,43 @@ int fa4d_bwd(const fa4d_bwd_args* a, void* stream) {
   cp.Tq = a->Tq;
   cp.Hq = a->Hq;
   cp.D = a->D;
+  return FA4D_OK;
+}
 
-  cudaError_t e = fa4d::launch_bwd_prep(pp, bf16, s);
-  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "backward preprocess launch failed: %s", cudaGetErrorString(e));
-  e = fa4d::launch_bwd(p, a->D, bf16, a->mask != nullptr, a->score != nullptr, s);
-  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "backward launch failed: %s", cudaGetErrorString(e));
-  e = fa4d::launch_dq_convert(cp, bf16, s);
-  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "dQ convert launch failed: %s", cudaGetErrorString(e));
+int run_stage(const BwdPlan& plan, int stage, cudaStream_t s) {
+  cudaError_t e = cudaSuccess;
+  const char* what = "";
+  if (stage == 0) {
+    e = fa4d::launch_bwd_prep(plan.prep, plan.bf16, s);
+    what = "backward preprocess";
+  } else if (stage == 1) {
+    e = fa4d::launch_bwd(plan.main, plan.D, plan.bf16, plan.has_mask, plan.has_score, s);
+    what = "backward main";
+  } else {
+    e = fa4d::launch_dq_convert(plan.convert, plan.bf16, s);
+    what = "dQ convert";
+  }
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+  return FA4D_OK;
+}
+
+int bwd_stages(const fa4d_bwd_args* a, int first, int last, void* stream) {
+  BwdPlan plan;
+  int rc = plan_bwd(a, &plan);
+  if (rc) return rc;
+  for (int st = first; st <= last; ++st)
+    if ((rc = run_stage(plan, st, static_cast<cudaStream_t>(stream)))) return rc;
   return ok();
 }
 
+}  // namespace
+
+extern "C" {
+
+int fa4d_bwd(const fa4d_bwd_args* a, void* stream) { return bwd_stages(a, 0, 2, stream); }
+int fa4d_bwd_preprocess(const fa4d_bwd_args* a, void* stream) { return bwd_stages(a, 0, 0, stream); }
+int fa4d_bwd_main(const fa4d_bwd_args* a, void* stream) { return bwd_stages(a, 1, 1, stream); }
+int fa4d_bwd_dq_convert(const fa4d_bwd_args* a, void* stream) { return bwd_stages(a, 2, 2, stream); }
+
 }  // extern "C"
+

@@ -120,15 +120,30 @@ int fa4d_fwd(const fa4d_fwd_args* args, void* stream);
  * sums at python/fa2.py:508-549 (kernels python/fa2.py:142-426). */
 int fa4d_bwd(const fa4d_bwd_args* args, void* stream);
 
+/* The three stages fa4d_bwd enqueues, callable one by one (same args, same
+ * stream order required: preprocess, main, dq_convert).
+ *  - fa4d_bwd_preprocess: Delta = rowsum(O * dO) into the workspace and zeroing
+ *    of the fp32 dQ accumulator; replaces bwd_preprocess (python/fa2.py:142-179,
+ *    launched at :509-513) and the torch.zeros of dQ at :527 / :540.
+ *  - fa4d_bwd_main: dK, dV (written) and dQ (accumulated in the workspace);
+ *    replaces flash_attention_bwd_with_4d_mask_atomic (python/fa2.py:182-302,
+ *    launched at :530-534) and _reduce (:306-426, launched at :543-547).
+ *  - fa4d_bwd_dq_convert: dQ in the input dtype from the accumulator; replaces the
+ *    autograd engine's cast of the fp32 dQ the reference returns (:556). */
+int fa4d_bwd_preprocess(const fa4d_bwd_args* args, void* stream);
+int fa4d_bwd_main(const fa4d_bwd_args* args, void* stream);
+int fa4d_bwd_dq_convert(const fa4d_bwd_args* args, void* stream);
+
 /* Message for the last non-zero return on this thread ("" if none). */
 const char* fa4d_last_error(void);
 
-/* Reads (and with clear != 0 resets) the device status word after synchronising
- * the stream: 0 = no kernel gave up a bounded wait; otherwise a bit set of
- * FA4D_DEV_* flags.  Returns a negative FA4D_ERR_* code if the read fails. */
+/* Reads (and with clear != 0 resets) the status word of CUDA device `device`
+ * after synchronising `stream`: 0 = no kernel gave up a bounded wait; otherwise a
+ * bit set of FA4D_DEV_* flags.  Returns a negative FA4D_ERR_* code if the read
+ * fails.  No counterpart in the reference (its kernels have no bounded waits). */
 #define FA4D_DEV_TIMEOUT_FWD 1
 #define FA4D_DEV_TIMEOUT_BWD 2
-int fa4d_device_status(void* stream, int clear);
+int fa4d_device_status(int device, void* stream, int clear);
 
 /* FA4D_ABI_VERSION of the loaded library. */
 int fa4d_abi_version(void);
