@@ -42,7 +42,7 @@ struct BwdLayout {
   static constexpr int kLSE = kDSb + 2 * kDS;   // 2 stages x 64 floats
   static constexpr int kDelta = kLSE + 2 * 256; // 2 stages x 64 floats
   static constexpr int kBar = kDelta + 2 * 256;
-  static constexpr int kNumBars = 16;
+  static constexpr int kNumBars = 18;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   uint64_t* q_empty = bars + 3;   // [2]
   uint64_t* s_full = bars + 5;    // [2]
   uint64_t* dp_full = bars + 7;
-  uint64_t* p_full = bars + 8;
+  uint64_t* p_full = bars + 16;  // [2], one per S^T buffer
   uint64_t* ds_full = bars + 9;
   uint64_t* ds_empty = bars + 10; // [2]
   uint64_t* dq_full = bars + 12;
@@ -136,7 +136,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       mbar_init(&ds_empty[i], 1);
     }
     mbar_init(dp_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(&p_full[0], 128);
+    mbar_init(&p_full[1], 128);
     mbar_init(ds_full, 128);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
           issue_kt<D, kBF16>(tmem + kColS + 64 * nx, sK, sQ + nx * L::kQT);
           tc_commit(&s_full[nx]);
         }
-        ok = mbar_wait(p_full, it & 1, abort_flag);
+        ok = mbar_wait(&p_full[st], (it >> 1) & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
         issue_dv<D, kBF16>(tmem + kColDV, tmem + kColS + 64 * st, sDO + st * L::kQT, it > 0);
@@ -272,24 +273,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       const float* lse = sLSE + st * 64;
       const bool need_causal = p.causal && (k0 + 127 > q0 + p.causal_off);
       const bool need_bounds = (q0 + 64 > p.Tq) || (k0 + 128 > p.Tk);
+      // Mask/score are read at clamped (always in-bounds) addresses and applied with
+      // selects, so lanes never branch apart before the warp-collective TMEM store.
+      const int kc = min(k, p.Tk - 1);
       const float* score_col = nullptr;
       const uint8_t* mask_col = nullptr;
-      if (kScore) score_col = p.score + b * p.score_stride[0] + h * p.score_stride[1] + k;
-      if (kMask) mask_col = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + k;
+      if (kScore) score_col = p.score + b * p.score_stride[0] + h * p.score_stride[1] + kc;
+      if (kMask) mask_col = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + kc;
       float pv[64];
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
         const int q = q0 + c;
+        const int64_t qc = min(q, p.Tq - 1);
         bool keep = true;
         if (need_bounds) keep = k_valid && (q < p.Tq);
         if (need_causal) keep = keep && (k <= q + p.causal_off);
         float x = __uint_as_float(sr[c]);
-        if constexpr (kScore) {
-          if (keep) x += __ldg(score_col + static_cast<int64_t>(q) * p.score_stride[2]);
-        }
-        if constexpr (kMask) {
-          if (keep) keep = __ldg(mask_col + static_cast<int64_t>(q) * p.mask_stride[2]) != 0;
-        }
+        if constexpr (kScore) x += __ldg(score_col + qc * p.score_stride[2]);
+        if constexpr (kMask) keep = keep && (__ldg(mask_col + qc * p.mask_stride[2]) != 0);
         const float e = ex2(x * p.scale_log2 - lse[c]);
         pv[c] = keep ? e : 0.f;
       }
@@ -304,7 +305,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full);
+      // One barrier per S^T buffer: a warp that finishes P for the next iteration
+      // early must not count toward this iteration's 128 arrivals.
+      mbar_arrive(&p_full[st]);
 
       ok = __all_sync(0xffffffffu, mbar_wait(dp_full, it & 1, abort_flag));
       if (!ok) break;

@@ -245,12 +245,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     const uint32_t tO = tmem + lane_base + 256 + D * t;
     const int n = n_slot[t];
 
+    // Rows past Tq read row Tq-1 (always in bounds) and are never stored: the loads
+    // below carry no per-lane branch, so the warp stays converged for the TMEM ops.
+    const int64_t qc = min(q, p.Tq - 1);
     const float* score_row = nullptr;
     const uint8_t* mask_row = nullptr;
-    if (kScore && q_valid)
-      score_row = p.score + b * p.score_stride[0] + h * p.score_stride[1] + static_cast<int64_t>(q) * p.score_stride[2];
-    if (kMask && q_valid)
-      mask_row = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + static_cast<int64_t>(q) * p.mask_stride[2];
+    if (kScore) score_row = p.score + b * p.score_stride[0] + h * p.score_stride[1] + qc * p.score_stride[2];
+    if (kMask) mask_row = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + qc * p.mask_stride[2];
 
     float m_run = kNegInf;
     float l_run = 0.f;
@@ -274,30 +275,27 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         const int k4 = kbase + 4 * c4;
         float add[4] = {0.f, 0.f, 0.f, 0.f};
         uint32_t keep_bits = 0xFu;
+        // k4 is the same for every lane, so these branches are warp-uniform.
         if constexpr (kScore) {
-          if (q_valid) {
-            if (p.score_vec && k4 + 3 < p.Tk) {
-              const float4 v = __ldg(reinterpret_cast<const float4*>(score_row + k4));
-              add[0] = v.x; add[1] = v.y; add[2] = v.z; add[3] = v.w;
-            } else {
+          if (p.score_vec && k4 + 3 < p.Tk) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(score_row + k4));
+            add[0] = v.x; add[1] = v.y; add[2] = v.z; add[3] = v.w;
+          } else {
 #pragma unroll
-              for (int e = 0; e < 4; ++e)
-                if (k4 + e < p.Tk) add[e] = __ldg(score_row + k4 + e);
-            }
+            for (int e = 0; e < 4; ++e)
+              if (k4 + e < p.Tk) add[e] = __ldg(score_row + k4 + e);
           }
         }
         if constexpr (kMask) {
           keep_bits = 0u;
-          if (q_valid) {
-            if (p.mask_vec && k4 + 3 < p.Tk) {
-              const uint32_t w = __ldg(reinterpret_cast<const unsigned int*>(mask_row + k4));
+          if (p.mask_vec && k4 + 3 < p.Tk) {
+            const uint32_t w = __ldg(reinterpret_cast<const unsigned int*>(mask_row + k4));
 #pragma unroll
-              for (int e = 0; e < 4; ++e) keep_bits |= (((w >> (8 * e)) & 0xFFu) != 0u ? 1u : 0u) << e;
-            } else {
+            for (int e = 0; e < 4; ++e) keep_bits |= (((w >> (8 * e)) & 0xFFu) != 0u ? 1u : 0u) << e;
+          } else {
 #pragma unroll
-              for (int e = 0; e < 4; ++e)
-                if (k4 + e < p.Tk) keep_bits |= (__ldg(mask_row + k4 + e) != 0 ? 1u : 0u) << e;
-            }
+            for (int e = 0; e < 4; ++e)
+              if (k4 + e < p.Tk) keep_bits |= (__ldg(mask_row + k4 + e) != 0 ? 1u : 0u) << e;
           }
         }
 #pragma unroll
