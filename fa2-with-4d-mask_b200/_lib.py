@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "fa4d_bwd_preprocess",
     "fa4d_bwd_main",
     "fa4d_bwd_dq_convert",
+    "fa4d_bwd_noalloc",
     "fa4d_last_error",
     "fa4d_device_status",
     "fa4d_abi_version",
@@ -140,7 +141,7 @@ def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
     lib.fa4d_bwd_workspace_size.restype = ctypes.c_size_t
     lib.fa4d_fwd.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
     lib.fa4d_fwd.restype = ctypes.c_int
-    for name in ("fa4d_bwd", "fa4d_bwd_preprocess", "fa4d_bwd_main", "fa4d_bwd_dq_convert"):
+    for name in ("fa4d_bwd", "fa4d_bwd_preprocess", "fa4d_bwd_main", "fa4d_bwd_dq_convert", "fa4d_bwd_noalloc"):
         fn = getattr(lib, name)
         fn.argtypes = [ctypes.POINTER(BwdArgs), ctypes.c_void_p]
         fn.restype = ctypes.c_int

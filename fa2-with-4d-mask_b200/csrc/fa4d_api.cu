@@ -356,3 +356,72 @@ int fa4d_bwd_dq_convert(const fa4d_bwd_args* a, void* stream) { return bwd_stage
 
 }  // extern "C"
 
+
+// ---------------------------------------------------------------------------------
+// Backward without any allocation by anyone.
+//
+// Some callers cannot hand the library a workspace: hosts that only own the input
+// and output buffers (a plugin or FFI boundary with no device allocator of its own),
+// and processes whose device memory is fully reserved by another pool, where a fresh
+// cudaMalloc would fail and cudaFree would synchronise the device.  For them the
+// backward's scratch (fp32 dQ accumulator + Delta) lives in this fixed array, which
+// every GPU that loads the library holds until the process exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = FA4D_BWD_NOALLOC_MAX_WORKSPACE;  // per device
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// symbol is only a stand-in, so the address is looked up once per device (with that
+// device current) and cached.
+void* noalloc_scratch_ptr(int* err) {
+  static std::mutex mu;
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = fail(FA4D_ERR_CUDA, "no current device for the scratch lookup");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      *err = fail(FA4D_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed on device %d: %s", dev,
+                  cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa4d_bwd_noalloc(const fa4d_bwd_args* a, void* stream) {
+  if (!a) return fail(FA4D_ERR_INVALID, "args is NULL");
+  int rc = check_common(a->B, a->Tq, a->Tk, a->Hq, a->Hk, a->D, a->dtype, a->causal, a->scale);
+  if (rc) return rc;
+  const size_t need = fa4d_bwd_workspace_size(a->B, a->Tq, a->Hq, a->D);
+  if (need > kNoAllocScratchBytes)
+    return fail(FA4D_ERR_WORKSPACE,
+                "fa4d_bwd_noalloc: this problem needs %zu bytes of scratch but the built-in buffer holds %zu "
+                "(B*Tq*Hq*D*4 plus Delta); use fa4d_bwd with a caller-owned workspace",
+                need, kNoAllocScratchBytes);
+  if (!a->q) return fail(FA4D_ERR_INVALID, "q is NULL");
+  if ((rc = bind_device_of(a->q, "q"))) return rc;
+  void* scratch = noalloc_scratch_ptr(&rc);
+  if (!scratch) return rc;
+  fa4d_bwd_args b = *a;
+  b.workspace = scratch;
+  b.workspace_bytes = kNoAllocScratchBytes;
+  // The preprocess stage zeroes the dQ accumulator and writes every Delta entry, so
+  // nothing left in the buffer by an earlier call reaches this one's results.
+  return bwd_stages(&b, 0, 2, stream);
+}
+
+}  // extern "C"

@@ -134,6 +134,25 @@ int fa4d_bwd_preprocess(const fa4d_bwd_args* args, void* stream);
 int fa4d_bwd_main(const fa4d_bwd_args* args, void* stream);
 int fa4d_bwd_dq_convert(const fa4d_bwd_args* args, void* stream);
 
+/* Backward for callers that cannot allocate device memory — no counterpart in the
+ * reference.  Some hosts own only the input and output buffers (a plugin or FFI
+ * boundary with no device allocator of its own), or run with device memory fully
+ * reserved by another pool, where cudaMalloc would fail and cudaFree would
+ * synchronise the device.  This call takes the same arguments as fa4d_bwd but ignores
+ * args->workspace / workspace_bytes: the scratch (fp32 dQ accumulator and Delta) is a
+ * fixed buffer of FA4D_BWD_NOALLOC_MAX_WORKSPACE bytes inside the library, which every
+ * GPU that loads the library keeps until the process exits.  Nothing is allocated.
+ *  - Problems whose fa4d_bwd_workspace_size() exceeds the buffer are rejected with
+ *    FA4D_ERR_WORKSPACE (e.g. B=1, Hq=32, D=128 fits up to Tq = 4064).
+ *  - The first call on a device looks up the buffer's device address (no
+ *    allocation); make that first call before any stream capture.
+ *  - All calls share the one buffer and it keeps the previous call's contents; the
+ *    first stage clears what must start at zero.  Calls whose work overlaps on the
+ *    GPU (different streams, or different host threads on one device) race on it:
+ *    order them on one stream. */
+#define FA4D_BWD_NOALLOC_MAX_WORKSPACE ((size_t)64 << 20)
+int fa4d_bwd_noalloc(const fa4d_bwd_args* args, void* stream);
+
 /* Message for the last non-zero return on this thread ("" if none). */
 const char* fa4d_last_error(void);
 
