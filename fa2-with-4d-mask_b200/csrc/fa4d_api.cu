@@ -149,7 +149,7 @@ extern "C" {
 int64_t fa4d_lse_row_stride(int32_t Tq) { return lse_ld_of(Tq); }
 
 size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D) {
-  const size_t dq = static_cast<size_t>(B) * Tq * Hq * D * sizeof(float);
+  const size_t dq = static_cast<size_t>(B) * Hq * lse_ld_of(Tq) * D * sizeof(float);
   const size_t dq_al = (dq + 255) / 256 * 256;
   const size_t delta = static_cast<size_t>(B) * Hq * lse_ld_of(Tq) * sizeof(float);
   return dq_al + (delta + 255) / 256 * 256;
@@ -253,7 +253,7 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   const bool bf16 = a->dtype == FA4D_BF16;
   const int64_t lse_ld = lse_ld_of(a->Tq);
   float* dq_acc = static_cast<float*>(a->workspace);
-  const size_t dq_bytes = static_cast<size_t>(a->B) * a->Tq * a->Hq * a->D * sizeof(float);
+  const size_t dq_bytes = static_cast<size_t>(a->B) * a->Hq * lse_ld * a->D * sizeof(float);
   float* delta = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + (dq_bytes + 255) / 256 * 256);
   int* status = status_word_ptr();
   if (!status) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
@@ -316,6 +316,7 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   cp.Tq = a->Tq;
   cp.Hq = a->Hq;
   cp.D = a->D;
+  cp.lse_ld = static_cast<int32_t>(lse_ld);
   return FA4D_OK;
 }
 

@@ -7,14 +7,16 @@
 // every query head of its GQA group, so dK/dV are summed in tensor memory and
 // stored once in the input dtype (the reference sums the group with fp32 atomics,
 // python/fa2.py:299-302, or with a bf16 host-side sum, python/fa2.py:548-549).
-// dQ is accumulated in fp32 with coalesced red.global.add and cast afterwards.
+// Each 64-query dQ tile is staged in shared memory and added to an fp32
+// accumulator with one bulk reduction (cp.reduce.async.bulk ... add.f32).
 //
-// CTA = 128 keys x one (batch, KV head); 384 threads:
-//   warp 0      TMA producer (K/V once; Q, dO, LSE, Delta per 64-row query tile)
-//   warp 1      tcgen05.mma issuer
-//   warp 2      TMEM allocator
-//   warps 4-7   P / dS computation (one thread per key row) and the dK/dV epilogue
-//   warps 8-11  dQ drain (one thread per head-dim lane) into the fp32 accumulator
+// CTA = 128 keys x one (batch, KV head); 512 threads:
+//   warp 0       TMA producer (K/V once; Q, dO, LSE, Delta per 64-row query tile)
+//   warp 1       tcgen05.mma issuer
+//   warp 2       TMEM allocator
+//   warps 4-7    P / dS for query columns 0-31 (one thread per key row), then dV out
+//   warps 8-11   P / dS for query columns 32-63, then dK out
+//   warps 12-15  dQ drain: TMEM -> shared staging -> bulk reduce-add into global
 // TMEM: S^T x2 [0,64) [64,128), dP^T [128,192), dQ^T [192,256), dV [256,256+D),
 // dK [256+D, 256+2D).  All MMAs are kind::f16 with fp32 accumulation.
 #include <cfloat>
@@ -27,22 +29,24 @@ namespace fa4d {
 
 namespace {
 
-constexpr int kBwdThreads = 384;
+constexpr int kBwdThreads = 512;
 
 template <int D>
 struct BwdLayout {
-  static constexpr int kKV = 128 * D * 2;  // K or V tile (128 keys)
-  static constexpr int kQT = 64 * D * 2;   // Q or dO tile (64 queries)
-  static constexpr int kDS = 128 * 64 * 2; // dS^T tile (128 keys x 64 queries, 16-bit)
+  static constexpr int kKV = 128 * D * 2;   // K or V tile (128 keys)
+  static constexpr int kQT = 64 * D * 2;    // Q or dO tile (64 queries)
+  static constexpr int kDS = 128 * 64 * 2;  // dS^T tile (128 keys x 64 queries, 16-bit)
+  static constexpr int kDQS = 64 * D * 4;   // dQ staging tile (64 queries x D, fp32)
   static constexpr int kK = 0;
   static constexpr int kV = kK + kKV;
-  static constexpr int kQ = kV + kKV;        // 2 stages
-  static constexpr int kDO = kQ + 2 * kQT;   // 2 stages
-  static constexpr int kDSb = kDO + 2 * kQT; // 2 buffers
-  static constexpr int kLSE = kDSb + 2 * kDS;   // 2 stages x 64 floats
-  static constexpr int kDelta = kLSE + 2 * 256; // 2 stages x 64 floats
+  static constexpr int kQ = kV + kKV;         // 2 stages
+  static constexpr int kDO = kQ + 2 * kQT;    // 2 stages
+  static constexpr int kDSb = kDO + 2 * kQT;  // 2 buffers
+  static constexpr int kDQs = kDSb + 2 * kDS;
+  static constexpr int kLSE = kDQs + kDQS;       // 2 stages x 64 floats
+  static constexpr int kDelta = kLSE + 2 * 256;  // 2 stages x 64 floats
   static constexpr int kBar = kDelta + 2 * 256;
-  static constexpr int kNumBars = 18;
+  static constexpr int kNumBars = 22;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -100,13 +104,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   uint64_t* q_empty = bars + 3;   // [2]
   uint64_t* s_full = bars + 5;    // [2]
   uint64_t* dp_full = bars + 7;
-  uint64_t* p_full = bars + 16;  // [2], one per S^T buffer
-  uint64_t* ds_full = bars + 9;
-  uint64_t* ds_empty = bars + 10; // [2]
-  uint64_t* dq_full = bars + 12;
-  uint64_t* dq_empty = bars + 13;
-  uint64_t* dkv_full = bars + 14;
-  uint64_t* mma_drain = bars + 15;
+  uint64_t* ds_full = bars + 8;
+  uint64_t* ds_empty = bars + 9;  // [2]
+  uint64_t* dq_full = bars + 11;
+  uint64_t* dq_empty = bars + 12;
+  uint64_t* dkv_full = bars + 13;
+  uint64_t* mma_drain = bars + 14;
+  uint64_t* p_full = bars + 15;   // [2], one per S^T buffer
+  uint64_t* s_read = bars + 17;   // [2], both P/dS warpgroups have read S^T
+  uint64_t* stage_free = bars + 19;
+  uint64_t* stage_full = bars + 20;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -134,11 +141,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&ds_empty[i], 1);
+      // One barrier per S^T buffer: a warp that finishes P for the next iteration
+      // early must not count toward this iteration's arrivals.
+      mbar_init(&p_full[i], 256);
+      mbar_init(&s_read[i], 256);
     }
+    mbar_init(stage_free, 1);
+    mbar_init(stage_full, 128);
     mbar_init(dp_full, 1);
-    mbar_init(&p_full[0], 128);
-    mbar_init(&p_full[1], 128);
-    mbar_init(ds_full, 128);
+    mbar_init(ds_full, 256);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
     mbar_init(dkv_full, 1);
@@ -201,8 +212,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       const uint32_t sQ = smem_u32(smem + L::kQ);
       const uint32_t sDO = smem_u32(smem + L::kDO);
       const uint32_t sDS = smem_u32(smem + L::kDSb);
-      bool ok = mbar_wait(kv_full, 0, abort_flag) &&
-                mbar_wait(&q_full[0], 0, abort_flag);
+      bool ok = mbar_wait(kv_full, 0, abort_flag) && mbar_wait(&q_full[0], 0, abort_flag);
       if (ok) {
         tc_fence_after();
         issue_kt<D, kBF16>(tmem + kColS, sK, sQ);
@@ -245,14 +255,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       mbar_wait(mma_drain, 0, abort_flag);
     }
     __syncwarp();
-  } else if (warp >= 4 && warp < 8) {
+  } else if (warp >= 4 && warp < 12) {
     // ------------------------------------------------------------ P, dS and dK/dV epilogue
+    const int wg = (warp - 4) >> 2;  // 0: query columns 0-31, 1: columns 32-63
+    const int cb = 32 * wg;
     const int r = (warp & 3) * 32 + lane;
     const int k = k0 + r;
     const bool k_valid = k < p.Tk;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const float* sLSE = reinterpret_cast<const float*>(smem + L::kLSE);
     const float* sDelta = reinterpret_cast<const float*>(smem + L::kDelta);
+    // Mask/score are read at clamped (always in-bounds) addresses and applied with
+    // selects, so lanes never branch apart before the warp-collective TMEM ops.
+    const int kc = min(k, p.Tk - 1);
     bool ok = true;
     for (int it = 0; it < N; ++it) {
       const int st = it & 1;
@@ -265,25 +280,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       if (!ok) break;
       tc_fence_after();
       const uint32_t tS = tmem + lane_base + kColS + 64 * st;
-      uint32_t sr[64];
-      tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      uint32_t sr[32];
+      tmem_ld32(tS + cb, sr);
       tmem_wait_ld();
+      // Both warpgroups must have read their S^T columns before either overwrites
+      // columns 0-31 of this buffer with P^T.  (No run-ahead: reaching this buffer's
+      // next use needs every thread's P of this iteration.)
+      mbar_arrive(&s_read[st]);
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_read[st], par, abort_flag));
+      if (!ok) break;
 
-      const float* lse = sLSE + st * 64;
+      const float* lse = sLSE + st * 64 + cb;
       const bool need_causal = p.causal && (k0 + 127 > q0 + p.causal_off);
       const bool need_bounds = (q0 + 64 > p.Tq) || (k0 + 128 > p.Tk);
-      // Mask/score are read at clamped (always in-bounds) addresses and applied with
-      // selects, so lanes never branch apart before the warp-collective TMEM store.
-      const int kc = min(k, p.Tk - 1);
       const float* score_col = nullptr;
       const uint8_t* mask_col = nullptr;
       if (kScore) score_col = p.score + b * p.score_stride[0] + h * p.score_stride[1] + kc;
       if (kMask) mask_col = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + kc;
-      float pv[64];
+      float pv[32];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const int q = q0 + c;
+      for (int c = 0; c < 32; ++c) {
+        const int q = q0 + cb + c;
         const int64_t qc = min(q, p.Tq - 1);
         bool keep = true;
         if (need_bounds) keep = k_valid && (q < p.Tq);
@@ -297,93 +314,81 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       {
         uint32_t pk[16];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = pack2<kBF16>(pv[32 * half + 2 * i], pv[32 * half + 2 * i + 1]);
-          tmem_st16(tS + 16 * half, pk);
-        }
+        for (int i = 0; i < 16; ++i) pk[i] = pack2<kBF16>(pv[2 * i], pv[2 * i + 1]);
+        tmem_st16(tS + 16 * wg, pk);
       }
       tmem_wait_st();
       tc_fence_before();
-      // One barrier per S^T buffer: a warp that finishes P for the next iteration
-      // early must not count toward this iteration's 128 arrivals.
       mbar_arrive(&p_full[st]);
 
       ok = __all_sync(0xffffffffu, mbar_wait(dp_full, it & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t tDP = tmem + lane_base + kColDP;
-      tmem_ld32(tDP, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld32(tDP + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_ld32(tmem + lane_base + kColDP + cb, sr);
       tmem_wait_ld();
-      const float* delta = sDelta + st * 64;
-      uint32_t dsk[32];
+      const float* delta = sDelta + st * 64 + cb;
+      uint32_t dsk[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         const float d0 = pv[2 * i] * (__uint_as_float(sr[2 * i]) - delta[2 * i]) * p.scale;
         const float d1 = pv[2 * i + 1] * (__uint_as_float(sr[2 * i + 1]) - delta[2 * i + 1]) * p.scale;
         dsk[i] = pack2<kBF16>(d0, d1);
       }
       ok = __all_sync(0xffffffffu, mbar_wait(&ds_empty[st], par ^ 1, abort_flag));
       if (!ok) break;
-      // Row r of the dS^T tile: 128 B in 8 chunks of 16 B, 128-B swizzled (chunk ^ (row % 8)).
+      // Row r of the dS^T tile: 128 B in 8 chunks of 16 B, 128-B swizzled (chunk ^ (row % 8));
+      // this warpgroup owns chunks 4*wg .. 4*wg+3.
       uint8_t* ds_row = smem + L::kDSb + st * L::kDS + r * 128;
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc)
-        *reinterpret_cast<uint4*>(ds_row + ((cc ^ (r & 7)) << 4)) =
+      for (int cc = 0; cc < 4; ++cc)
+        *reinterpret_cast<uint4*>(ds_row + (((4 * wg + cc) ^ (r & 7)) << 4)) =
             make_uint4(dsk[4 * cc], dsk[4 * cc + 1], dsk[4 * cc + 2], dsk[4 * cc + 3]);
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
     }
 
-    // dK / dV epilogue (zeros when no query interacts with this key tile).
-    uint16_t* dv_row = nullptr;
-    uint16_t* dk_row = nullptr;
+    // Epilogue: warpgroup 0 writes dV, warpgroup 1 writes dK (zeros when no query
+    // interacts with this key tile).
+    uint16_t* dst_row = nullptr;
     if (k_valid) {
-      dv_row = reinterpret_cast<uint16_t*>(p.dv) + b * p.dv_stride[0] + static_cast<int64_t>(k) * p.dv_stride[1] +
-               hk * p.dv_stride[2];
-      dk_row = reinterpret_cast<uint16_t*>(p.dk) + b * p.dk_stride[0] + static_cast<int64_t>(k) * p.dk_stride[1] +
-               hk * p.dk_stride[2];
+      const int64_t* st3 = wg == 0 ? p.dv_stride : p.dk_stride;
+      dst_row = reinterpret_cast<uint16_t*>(wg == 0 ? p.dv : p.dk) + b * st3[0] + static_cast<int64_t>(k) * st3[1] +
+                hk * st3[2];
     }
     if (N > 0 && ok) {
       ok = __all_sync(0xffffffffu, mbar_wait(dkv_full, 0, abort_flag));
       tc_fence_after();
+      const uint32_t tA = tmem + lane_base + (wg == 0 ? kColDV : kColDK);
 #pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const uint32_t tA = tmem + lane_base + (which == 0 ? kColDV : kColDK);
-        uint16_t* dst_row = which == 0 ? dv_row : dk_row;
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tA + 32 * c, v);
+        tmem_wait_ld();
+        if (k_valid) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tA + 32 * c, v);
-          tmem_wait_ld();
-          if (k_valid) {
-            uint32_t pk[16];
+          for (int i = 0; i < 16; ++i) pk[i] = pack2<kBF16>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+          uint4* dst = reinterpret_cast<uint4*>(dst_row + 32 * c);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) pk[i] = pack2<kBF16>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-            uint4* dst = reinterpret_cast<uint4*>(dst_row + 32 * c);
-#pragma unroll
-            for (int u = 0; u < 4; ++u) dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-          }
+          for (int u = 0; u < 4; ++u) dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         }
       }
     } else if (k_valid && N == 0) {
 #pragma unroll
-      for (int u = 0; u < D / 8; ++u) {
-        reinterpret_cast<uint4*>(dv_row)[u] = make_uint4(0, 0, 0, 0);
-        reinterpret_cast<uint4*>(dk_row)[u] = make_uint4(0, 0, 0, 0);
-      }
+      for (int u = 0; u < D / 8; ++u) reinterpret_cast<uint4*>(dst_row)[u] = make_uint4(0, 0, 0, 0);
     }
     tc_fence_before();
-  } else if (warp >= 8) {
+  } else if (warp >= 12) {
     // ------------------------------------------------------------ dQ drain
     const int wq = warp & 3;
     // M = D accumulator layout: D=128 uses all 128 lanes; D=64 (M=64) puts rows
     // 16*wq .. 16*wq+15 in lanes 0-15 of each 32-lane quadrant.
     const int d = (D == 128) ? (wq * 32 + lane) : (wq * 16 + lane);
     const bool d_valid = (D == 128) || (lane < 16);
+    const bool leader = (warp == 12 && lane == 0);
     const uint32_t tDQ = tmem + (static_cast<uint32_t>(wq * 32) << 16) + kColDQ;
+    float* stage = reinterpret_cast<float*>(smem + L::kDQs);  // [64 queries][D]
     for (int it = 0; it < N; ++it) {
       const int g = it / nq;
       const int h = hk * G + g;
@@ -397,15 +402,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(dq_empty);
+      // The previous tile's bulk reduction must have finished reading the staging tile.
+      if (leader) {
+        bulk_wait_read_all();
+        mbar_arrive(stage_free);
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait(stage_free, it & 1, abort_flag))) break;
       if (d_valid) {
-        float* base = p.dq_acc + ((static_cast<int64_t>(b) * p.Tq + q0) * p.Hq + h) * D + d;
-        const int64_t qstride = static_cast<int64_t>(p.Hq) * D;
-        const int qn = min(64, p.Tq - q0);
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (c < qn) red_add_f32(base + c * qstride, __uint_as_float(v[c]));
+        for (int c = 0; c < 64; ++c) stage[c * D + d] = __uint_as_float(v[c]);
+      }
+      fence_async_smem();
+      mbar_arrive(stage_full);
+      if (leader && mbar_wait(stage_full, it & 1, abort_flag)) {
+        // Rows q0..q0+63 of head h are contiguous in the [B, Hq, Tq_pad, D] accumulator
+        // (rows past Tq land in the padding and are never read).
+        float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + q0) * D;
+        bulk_reduce_add_f32(dst, stage, 64 * D * 4);
+        bulk_commit();
       }
     }
+    if (leader) bulk_wait_all();
     tc_fence_before();
   }
 
@@ -417,7 +434,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   }
 }
 
-// Delta[b, h, t] = sum_d O * dO (0 for padding rows) and dq_acc row = 0.
+// Delta[b, h, t] = sum_d O * dO (0 for padding rows) and zeroing of the dQ accumulator
+// row (b, h, t), layout [B, Hq, lse_ld, D].  One warp per (b, t, h).
 template <int D, bool kBF16>
 __global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
   const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -427,9 +445,9 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
   const int h = static_cast<int>(w % p.Hq);
   const int t = static_cast<int>((w / p.Hq) % p.lse_ld);
   const int b = static_cast<int>(w / (static_cast<int64_t>(p.Hq) * p.lse_ld));
+  constexpr int E = D / 32;  // elements per lane (2 or 4)
   float acc = 0.f;
   if (t < p.Tq) {
-    constexpr int E = D / 32;  // elements per lane (2 or 4)
     const uint16_t* o = reinterpret_cast<const uint16_t*>(p.o) + b * p.o_stride[0] +
                         static_cast<int64_t>(t) * p.o_stride[1] + h * p.o_stride[2] + lane * E;
     const uint16_t* g = reinterpret_cast<const uint16_t*>(p.dout) + b * p.do_stride[0] +
@@ -448,7 +466,7 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    float* dq = p.dq_acc + ((static_cast<int64_t>(b) * p.Tq + t) * p.Hq + h) * D + lane * E;
+    float* dq = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t) * D + lane * E;
     if constexpr (E == 4)
       *reinterpret_cast<float4*>(dq) = make_float4(0.f, 0.f, 0.f, 0.f);
     else
@@ -457,7 +475,7 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
   if (lane == 0) p.delta[(static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t] = acc;
 }
 
-// dQ (input dtype) = dq_acc, 8 elements per thread.
+// dQ (input dtype, caller strides) = dq_acc [B, Hq, lse_ld, D], 8 elements per thread.
 template <bool kBF16>
 __global__ void __launch_bounds__(256) dq_convert_kernel(const ConvertParams p) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -465,11 +483,12 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const ConvertParams p) 
   const int64_t total = static_cast<int64_t>(p.B) * p.Tq * p.Hq * per_row;
   if (i >= total) return;
   const int d8 = static_cast<int>(i % per_row);
-  const int64_t row = i / per_row;
+  const int64_t row = i / per_row;  // (b, t, h) with h fastest
   const int h = static_cast<int>(row % p.Hq);
   const int t = static_cast<int>((row / p.Hq) % p.Tq);
   const int b = static_cast<int>(row / (static_cast<int64_t>(p.Hq) * p.Tq));
-  const float4* src = reinterpret_cast<const float4*>(p.dq_acc + row * p.D + d8 * 8);
+  const float4* src = reinterpret_cast<const float4*>(
+      p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t) * p.D + d8 * 8);
   const float4 a = src[0], c = src[1];
   uint4 out = make_uint4(pack2<kBF16>(a.x, a.y), pack2<kBF16>(a.z, a.w), pack2<kBF16>(c.x, c.y),
                          pack2<kBF16>(c.z, c.w));

@@ -41,7 +41,7 @@ struct BwdParams {
   CUtensorMap tm_v;
   const float* lse;     // [B, Hq, lse_ld]
   const float* delta;   // [B, Hq, lse_ld]
-  float* dq_acc;        // [B, Tq, Hq, D] fp32, zeroed by the preprocess kernel
+  float* dq_acc;        // [B, Hq, lse_ld, D] fp32, zeroed by the preprocess kernel
   void* dk;
   void* dv;
   const uint8_t* mask;
@@ -71,12 +71,13 @@ struct PrepParams {
   int32_t lse_ld;
 };
 
-// dQ (input dtype, caller strides) = dQ accumulator.
+// dQ (input dtype, caller strides) = dQ accumulator [B, Hq, lse_ld, D].
 struct ConvertParams {
   const float* dq_acc;
   void* dq;
   int64_t dq_stride[3];
   int32_t B, Tq, Hq, D;
+  int32_t lse_ld;
 };
 
 cudaError_t launch_fwd(const FwdParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);

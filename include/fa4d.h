@@ -106,8 +106,9 @@ typedef struct fa4d_bwd_args {
  * The LSE buffer holds B * Hq * fa4d_lse_row_stride(Tq) floats. */
 int64_t fa4d_lse_row_stride(int32_t Tq);
 
-/* Bytes of device scratch fa4d_bwd needs: an fp32 dQ accumulator [B, Tq, Hq, D]
- * and the fp32 row dot products Delta [B, Hq, fa4d_lse_row_stride(Tq)]. */
+/* Bytes of device scratch fa4d_bwd needs: an fp32 dQ accumulator
+ * [B, Hq, fa4d_lse_row_stride(Tq), D] and the fp32 row dot products
+ * Delta [B, Hq, fa4d_lse_row_stride(Tq)]. */
 size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D);
 
 /* Forward: O = softmax(((Q K^T + score) * scale) masked) V and LSE.
@@ -143,7 +144,7 @@ int fa4d_bwd_dq_convert(const fa4d_bwd_args* args, void* stream);
  * fixed buffer of FA4D_BWD_NOALLOC_MAX_WORKSPACE bytes inside the library, which every
  * GPU that loads the library keeps until the process exits.  Nothing is allocated.
  *  - Problems whose fa4d_bwd_workspace_size() exceeds the buffer are rejected with
- *    FA4D_ERR_WORKSPACE (e.g. B=1, Hq=32, D=128 fits up to Tq = 4064).
+ *    FA4D_ERR_WORKSPACE (e.g. B=1, Hq=32, D=128 fits up to Tq = 3968).
  *  - The first call on a device looks up the buffer's device address (no
  *    allocation); make that first call before any stream capture.
  *  - All calls share the one buffer and it keeps the previous call's contents; the
