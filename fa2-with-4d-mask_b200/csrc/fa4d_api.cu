@@ -317,6 +317,7 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   cp.Hq = a->Hq;
   cp.D = a->D;
   cp.lse_ld = static_cast<int32_t>(lse_ld);
+  cp.scale = a->scale;
   return FA4D_OK;
 }
 

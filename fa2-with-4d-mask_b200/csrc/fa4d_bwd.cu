@@ -3,6 +3,8 @@
 // Math follows the reference backward (python/fa2.py:181-302): P is recomputed from
 // the saved log2-domain LSE, dV = P^T dO, dP = dO V^T, dS = P (dP - Delta) scale,
 // dK = dS^T Q, dQ = dS K, with Delta = rowsum(O * dO) (python/fa2.py:142-179).
+// The kernels carry dS without the factor `scale` and apply it once to the dK
+// tile in its epilogue and to dQ when the accumulator is converted.
 // Unlike the reference, one CTA owns a 128-key tile of one KV head and loops over
 // every query head of its GQA group, so dK/dV are summed in tensor memory and
 // stored once in the input dtype (the reference sums the group with fp32 atomics,
@@ -30,6 +32,9 @@ namespace fa4d {
 namespace {
 
 constexpr int kBwdThreads = 512;
+// Depth of the Q / dO / LSE / Delta ring: the load for query tile it+2 is issued
+// while tile it is still being consumed, which hides its L2/HBM latency.
+constexpr int kQStages = 3;
 
 template <int D>
 struct BwdLayout {
@@ -39,17 +44,18 @@ struct BwdLayout {
   static constexpr int kDQS = 64 * D * 4;   // dQ staging tile (64 queries x D, fp32)
   static constexpr int kK = 0;
   static constexpr int kV = kK + kKV;
-  static constexpr int kQ = kV + kKV;         // 2 stages
-  static constexpr int kDO = kQ + 2 * kQT;    // 2 stages
-  static constexpr int kDSb = kDO + 2 * kQT;  // 2 buffers
+  static constexpr int kQ = kV + kKV;                 // kQStages stages
+  static constexpr int kDO = kQ + kQStages * kQT;     // kQStages stages
+  static constexpr int kDSb = kDO + kQStages * kQT;   // 2 buffers
   static constexpr int kDQs = kDSb + 2 * kDS;
-  static constexpr int kLSE = kDQs + kDQS;       // 2 stages x 64 floats
-  static constexpr int kDelta = kLSE + 2 * 256;  // 2 stages x 64 floats
-  static constexpr int kBar = kDelta + 2 * 256;
-  static constexpr int kNumBars = 22;
+  static constexpr int kLSE = kDQs + kDQS;               // kQStages x 64 floats
+  static constexpr int kDelta = kLSE + kQStages * 256;   // kQStages x 64 floats
+  static constexpr int kBar = kDelta + kQStages * 256;
+  static constexpr int kNumBars = 24;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
+  static_assert(kAlloc <= 232448, "shared memory beyond the 227 KB per-block limit");
 };
 
 // S^T = K Q^T (or dP^T = V dO^T): M=128 keys, N=64 queries, K=D; both K-major.
@@ -100,20 +106,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;    // [2]
-  uint64_t* q_empty = bars + 3;   // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* dp_full = bars + 7;
-  uint64_t* ds_full = bars + 8;
-  uint64_t* ds_empty = bars + 9;  // [2]
-  uint64_t* dq_full = bars + 11;
-  uint64_t* dq_empty = bars + 12;
-  uint64_t* dkv_full = bars + 13;
-  uint64_t* mma_drain = bars + 14;
-  uint64_t* p_full = bars + 15;   // [2], one per S^T buffer
-  uint64_t* s_read = bars + 17;   // [2], both P/dS warpgroups have read S^T
-  uint64_t* stage_free = bars + 19;
-  uint64_t* stage_full = bars + 20;
+  uint64_t* s_full = bars + 1;    // [2]
+  uint64_t* dp_full = bars + 3;
+  uint64_t* ds_full = bars + 4;
+  uint64_t* ds_empty = bars + 5;  // [2]
+  uint64_t* dq_full = bars + 7;
+  uint64_t* dq_empty = bars + 8;
+  uint64_t* dkv_full = bars + 9;
+  uint64_t* mma_drain = bars + 10;
+  uint64_t* p_full = bars + 11;   // [2], one per S^T buffer
+  uint64_t* s_read = bars + 13;   // [2], both P/dS warpgroups have read S^T
+  uint64_t* stage_free = bars + 15;
+  uint64_t* stage_full = bars + 16;
+  uint64_t* q_full = bars + 17;   // [kQStages]
+  uint64_t* q_empty = bars + 20;  // [kQStages]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -136,9 +142,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kQStages; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&ds_empty[i], 1);
       // One barrier per S^T buffer: a warp that finishes P for the next iteration
@@ -182,25 +190,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       }
       int issued = 0;
       for (int it = 0; it < N; ++it) {
-        const int st = it & 1;
+        const int qs = it % kQStages;
         const int g = it / nq;
         const int h = hk * G + g;
         const int q0 = (first_qt + it % nq) * 64;
-        if (!mbar_wait(&q_empty[st], ((it >> 1) & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&q_full[st], 2 * L::kQT + 512);
+        if (!mbar_wait(&q_empty[qs], ((it / kQStages) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&q_full[qs], 2 * L::kQT + 512);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(smem + L::kQ + st * L::kQT + c * 8192, &p.tm_q, &q_full[st], c * 64, q0, h, b);
-          tma_load_4d(smem + L::kDO + st * L::kQT + c * 8192, &p.tm_do, &q_full[st], c * 64, q0, h, b);
+          tma_load_4d(smem + L::kQ + qs * L::kQT + c * 8192, &p.tm_q, &q_full[qs], c * 64, q0, h, b);
+          tma_load_4d(smem + L::kDO + qs * L::kQT + c * 8192, &p.tm_do, &q_full[qs], c * 64, q0, h, b);
         }
         const int64_t row = (static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + q0;
-        bulk_load(smem + L::kLSE + st * 256, p.lse + row, 256, &q_full[st]);
-        bulk_load(smem + L::kDelta + st * 256, p.delta + row, 256, &q_full[st]);
+        bulk_load(smem + L::kLSE + qs * 256, p.lse + row, 256, &q_full[qs]);
+        bulk_load(smem + L::kDelta + qs * 256, p.delta + row, 256, &q_full[qs]);
         issued = it + 1;
       }
       if (*reinterpret_cast<volatile int*>(abort_flag)) {
         mbar_wait_short(kv_full, 0);
-        for (int it = max(0, issued - 2); it < issued; ++it) mbar_wait_short(&q_full[it & 1], (it >> 1) & 1);
+        for (int it = max(0, issued - kQStages); it < issued; ++it)
+          mbar_wait_short(&q_full[it % kQStages], (it / kQStages) & 1);
       }
     }
     __syncwarp();
@@ -221,32 +230,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         tc_commit(dp_full);
       }
       for (int it = 0; ok && it < N; ++it) {
-        const int st = it & 1;
+        const int st = it & 1;         // S^T / P^T and dS^T buffers
         const int nx = (it + 1) & 1;
+        const int qs = it % kQStages;  // Q / dO stage of this tile
+        const int qn = (it + 1) % kQStages;
         if (it + 1 < N) {
-          ok = mbar_wait(&q_full[nx], ((it + 1) >> 1) & 1, abort_flag);
+          ok = mbar_wait(&q_full[qn], ((it + 1) / kQStages) & 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
-          issue_kt<D, kBF16>(tmem + kColS + 64 * nx, sK, sQ + nx * L::kQT);
+          issue_kt<D, kBF16>(tmem + kColS + 64 * nx, sK, sQ + qn * L::kQT);
           tc_commit(&s_full[nx]);
         }
         ok = mbar_wait(&p_full[st], (it >> 1) & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
-        issue_dv<D, kBF16>(tmem + kColDV, tmem + kColS + 64 * st, sDO + st * L::kQT, it > 0);
+        issue_dv<D, kBF16>(tmem + kColDV, tmem + kColS + 64 * st, sDO + qs * L::kQT, it > 0);
         ok = mbar_wait(ds_full, it & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
-        issue_dk<D, kBF16>(tmem + kColDK, sDS + st * L::kDS, sQ + st * L::kQT, it > 0);
+        issue_dk<D, kBF16>(tmem + kColDK, sDS + st * L::kDS, sQ + qs * L::kQT, it > 0);
         ok = mbar_wait(dq_empty, (it & 1) ^ 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
         issue_dq<D, kBF16>(tmem + kColDQ, sK, sDS + st * L::kDS);
         tc_commit(dq_full);
-        tc_commit(&q_empty[st]);
+        tc_commit(&q_empty[qs]);
         tc_commit(&ds_empty[st]);
         if (it + 1 < N) {
-          issue_kt<D, kBF16>(tmem + kColDP, sV, sDO + nx * L::kQT);
+          issue_kt<D, kBF16>(tmem + kColDP, sV, sDO + qn * L::kQT);
           tc_commit(dp_full);
         }
       }
@@ -275,8 +286,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       const int h = hk * G + g;
       const int q0 = (first_qt + it % nq) * 64;
       const uint32_t par = (it >> 1) & 1;
+      const int qs = it % kQStages;
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], par, abort_flag) &&
-                                       mbar_wait(&q_full[st], par, abort_flag));
+                                       mbar_wait(&q_full[qs], (it / kQStages) & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
       const uint32_t tS = tmem + lane_base + kColS + 64 * st;
@@ -290,26 +302,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       ok = __all_sync(0xffffffffu, mbar_wait(&s_read[st], par, abort_flag));
       if (!ok) break;
 
-      const float* lse = sLSE + st * 64 + cb;
+      float lsev[32];
+      {
+        const float4* l4 = reinterpret_cast<const float4*>(sLSE + qs * 64 + cb);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 t = l4[i];
+          lsev[4 * i] = t.x; lsev[4 * i + 1] = t.y; lsev[4 * i + 2] = t.z; lsev[4 * i + 3] = t.w;
+        }
+      }
       const bool need_causal = p.causal && (k0 + 127 > q0 + p.causal_off);
       const bool need_bounds = (q0 + 64 > p.Tq) || (k0 + 128 > p.Tk);
-      const float* score_col = nullptr;
-      const uint8_t* mask_col = nullptr;
-      if (kScore) score_col = p.score + b * p.score_stride[0] + h * p.score_stride[1] + kc;
-      if (kMask) mask_col = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + kc;
       float pv[32];
+      if (!kMask && !kScore && !need_causal && !need_bounds) {
+        // Interior tile (warp-uniform): P = exp2(S * scale * log2(e) - LSE).
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int q = q0 + cb + c;
-        const int64_t qc = min(q, p.Tq - 1);
-        bool keep = true;
-        if (need_bounds) keep = k_valid && (q < p.Tq);
-        if (need_causal) keep = keep && (k <= q + p.causal_off);
-        float x = __uint_as_float(sr[c]);
-        if constexpr (kScore) x += __ldg(score_col + qc * p.score_stride[2]);
-        if constexpr (kMask) keep = keep && (__ldg(mask_col + qc * p.mask_stride[2]) != 0);
-        const float e = ex2(x * p.scale_log2 - lse[c]);
-        pv[c] = keep ? e : 0.f;
+        for (int c = 0; c < 32; ++c) pv[c] = ex2(fmaf(__uint_as_float(sr[c]), p.scale_log2, -lsev[c]));
+      } else {
+        const float* score_col = nullptr;
+        const uint8_t* mask_col = nullptr;
+        if (kScore) score_col = p.score + b * p.score_stride[0] + h * p.score_stride[1] + kc;
+        if (kMask) mask_col = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + kc;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int q = q0 + cb + c;
+          const int64_t qc = min(q, p.Tq - 1);
+          bool keep = true;
+          if (need_bounds) keep = k_valid && (q < p.Tq);
+          if (need_causal) keep = keep && (k <= q + p.causal_off);
+          float x = __uint_as_float(sr[c]);
+          if constexpr (kScore) x += __ldg(score_col + qc * p.score_stride[2]);
+          if constexpr (kMask) keep = keep && (__ldg(mask_col + qc * p.mask_stride[2]) != 0);
+          const float e = ex2(fmaf(x, p.scale_log2, -lsev[c]));
+          pv[c] = keep ? e : 0.f;
+        }
       }
       {
         uint32_t pk[16];
@@ -326,13 +352,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       tc_fence_after();
       tmem_ld32(tmem + lane_base + kColDP + cb, sr);
       tmem_wait_ld();
-      const float* delta = sDelta + st * 64 + cb;
+      // dS without the softmax scale: dK and dQ are scaled once at their outputs.
       uint32_t dsk[16];
+      {
+        const float4* d4 = reinterpret_cast<const float4*>(sDelta + qs * 64 + cb);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float d0 = pv[2 * i] * (__uint_as_float(sr[2 * i]) - delta[2 * i]) * p.scale;
-        const float d1 = pv[2 * i + 1] * (__uint_as_float(sr[2 * i + 1]) - delta[2 * i + 1]) * p.scale;
-        dsk[i] = pack2<kBF16>(d0, d1);
+        for (int i = 0; i < 8; ++i) {
+          const float4 t = d4[i];
+          const float e0 = pv[4 * i] * (__uint_as_float(sr[4 * i]) - t.x);
+          const float e1 = pv[4 * i + 1] * (__uint_as_float(sr[4 * i + 1]) - t.y);
+          const float e2 = pv[4 * i + 2] * (__uint_as_float(sr[4 * i + 2]) - t.z);
+          const float e3 = pv[4 * i + 3] * (__uint_as_float(sr[4 * i + 3]) - t.w);
+          dsk[2 * i] = pack2<kBF16>(e0, e1);
+          dsk[2 * i + 1] = pack2<kBF16>(e2, e3);
+        }
       }
       ok = __all_sync(0xffffffffu, mbar_wait(&ds_empty[st], par ^ 1, abort_flag));
       if (!ok) break;
@@ -360,6 +393,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       ok = __all_sync(0xffffffffu, mbar_wait(dkv_full, 0, abort_flag));
       tc_fence_after();
       const uint32_t tA = tmem + lane_base + (wg == 0 ? kColDV : kColDK);
+      const float out_scale = wg == 0 ? 1.f : p.scale;  // dK = scale * dS^T Q
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t v[32];
@@ -368,7 +402,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         if (k_valid) {
           uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = pack2<kBF16>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+          for (int i = 0; i < 16; ++i)
+            pk[i] = pack2<kBF16>(__uint_as_float(v[2 * i]) * out_scale, __uint_as_float(v[2 * i + 1]) * out_scale);
           uint4* dst = reinterpret_cast<uint4*>(dst_row + 32 * c);
 #pragma unroll
           for (int u = 0; u < 4; ++u) dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
@@ -475,7 +510,7 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
   if (lane == 0) p.delta[(static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t] = acc;
 }
 
-// dQ (input dtype, caller strides) = dq_acc [B, Hq, lse_ld, D], 8 elements per thread.
+// dQ (input dtype, caller strides) = scale * dq_acc [B, Hq, lse_ld, D], 8 elements per thread.
 template <bool kBF16>
 __global__ void __launch_bounds__(256) dq_convert_kernel(const ConvertParams p) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -490,8 +525,9 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const ConvertParams p) 
   const float4* src = reinterpret_cast<const float4*>(
       p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t) * p.D + d8 * 8);
   const float4 a = src[0], c = src[1];
-  uint4 out = make_uint4(pack2<kBF16>(a.x, a.y), pack2<kBF16>(a.z, a.w), pack2<kBF16>(c.x, c.y),
-                         pack2<kBF16>(c.z, c.w));
+  const float sc = p.scale;  // dQ = scale * dS K (dS is accumulated without the scale)
+  uint4 out = make_uint4(pack2<kBF16>(a.x * sc, a.y * sc), pack2<kBF16>(a.z * sc, a.w * sc),
+                         pack2<kBF16>(c.x * sc, c.y * sc), pack2<kBF16>(c.z * sc, c.w * sc));
   uint16_t* dst = reinterpret_cast<uint16_t*>(p.dq) + b * p.dq_stride[0] + static_cast<int64_t>(t) * p.dq_stride[1] +
                   h * p.dq_stride[2] + d8 * 8;
   *reinterpret_cast<uint4*>(dst) = out;

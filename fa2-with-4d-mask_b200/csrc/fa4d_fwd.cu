@@ -44,6 +44,7 @@ struct FwdLayout {
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
+  static_assert(kAlloc <= 232448, "shared memory beyond the 227 KB per-block limit");
 };
 
 // S[slot] = Q[slot] K^T : M=128, N=128, K=D; both operands K-major, 128-B swizzled.

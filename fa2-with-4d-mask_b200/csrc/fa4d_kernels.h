@@ -78,6 +78,7 @@ struct ConvertParams {
   int64_t dq_stride[3];
   int32_t B, Tq, Hq, D;
   int32_t lse_ld;
+  float scale;
 };
 
 cudaError_t launch_fwd(const FwdParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);

@@ -45,6 +45,21 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint64_t* bar, uint32_t parity
   return done;
 }
 
+// As mbar_try_wait, but lets the hardware suspend the warp (up to `hint_ns`) until
+// the phase completes instead of returning at once, so waiting warps do not take
+// issue slots from working warps.
+__device__ __forceinline__ uint32_t mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done;
+}
+
 // Waits for the phase with the given parity.  Returns false if it did not complete
 // within kWaitLimitCycles (the CTA's abort flag is then raised; the kernel reports
 // it in the device status word before exiting) or if another role of the CTA
@@ -52,14 +67,11 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint64_t* bar, uint32_t parity
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  uint32_t n = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if ((++n & 255u) == 0u) {
-      if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
-      if (clock64() - t0 > kWaitLimitCycles) {
-        *reinterpret_cast<volatile int*>(abort_flag) = 1;
-        return false;
-      }
+  while (!mbar_try_wait_sleep(bar, parity, 1000000u)) {
+    if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      *reinterpret_cast<volatile int*>(abort_flag) = 1;
+      return false;
     }
   }
   return true;
