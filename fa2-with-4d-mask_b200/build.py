@@ -10,6 +10,7 @@ from __future__ import annotations
 import argparse
 import concurrent.futures as cf
 import os
+import re
 import shutil
 import subprocess
 import sys
@@ -45,13 +46,32 @@ def _stale(target: Path, inputs: list[Path]) -> bool:
     return any(p.stat().st_mtime > t for p in inputs)
 
 
+# Kernels that rebalance registers with setmaxnreg assume this exact allocation per
+# thread at launch; fewer would make a setmaxnreg.inc wait forever.
+LAUNCH_REGS = {"bwd_kernel": 128}
+
+
+def _check_launch_regs(src: Path, log: str) -> None:
+    entry = None
+    for line in log.splitlines():
+        m = re.search(r"Compiling entry function '(\S+)'", line)
+        if m:
+            entry = m.group(1)
+            continue
+        m = re.search(r"Used (\d+) registers", line)
+        if m and entry:
+            for name, regs in LAUNCH_REGS.items():
+                if name in entry and int(m.group(1)) != regs:
+                    raise RuntimeError(f"{src.name}: {entry} uses {m.group(1)} registers, expected {regs}")
+            entry = None
+
+
 def _compile(nvcc: str, src: Path, obj: Path, ptxas_info: bool) -> str:
-    cmd = [nvcc, *ARCH, *CFLAGS, f"-I{INCLUDE}", f"-I{CSRC}", "-c", str(src), "-o", str(obj)]
-    if ptxas_info:
-        cmd += ["-Xptxas", "-v"]
+    cmd = [nvcc, *ARCH, *CFLAGS, f"-I{INCLUDE}", f"-I{CSRC}", "-c", str(src), "-o", str(obj), "-Xptxas", "-v"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src.name}:\n{res.stdout}\n{res.stderr}")
+    _check_launch_regs(src, res.stdout + res.stderr)
     return res.stdout + res.stderr
 
 

@@ -13,14 +13,17 @@
 // accumulator with one bulk reduction (cp.reduce.async.bulk ... add.f32).
 //
 // CTA = 128 keys x one (batch, KV head); 512 threads:
-//   warp 0       TMA producer (K/V once; Q, dO, LSE, Delta per 64-row query tile)
-//   warp 1       tcgen05.mma issuer
+//   warp 0       TMA producer (K/V once; Q, dO, LSE, Delta per 64-row query tile,
+//                3-stage ring)
+//   warp 1       tcgen05.mma issuer, two query tiles ahead of the P/dS warpgroups
 //   warp 2       TMEM allocator
-//   warps 4-7    P / dS for query columns 0-31 (one thread per key row), then dV out
-//   warps 8-11   P / dS for query columns 32-63, then dK out
+//   warps 4-7    P / dS of the even query tiles (one thread per key row), then dV out
+//   warps 8-11   P / dS of the odd query tiles, then dK out
 //   warps 12-15  dQ drain: TMEM -> shared staging -> bulk reduce-add into global
-// TMEM: S^T x2 [0,64) [64,128), dP^T [128,192), dQ^T [192,256), dV [256,256+D),
-// dK [256+D, 256+2D).  All MMAs are kind::f16 with fp32 accumulation.
+// The two P/dS warpgroups ping-pong, so the hand-off latency of one tile (MMA
+// completion -> P -> MMA -> dS -> MMA) overlaps the other tile's work.
+// TMEM (512 columns): S^T x2 [0,128), X x2 [128,256) (a tile's dP^T, later its
+// dQ^T), dV [256,256+D), dK [256+D,256+2D).  All MMAs are kind::f16, fp32 accumulate.
 #include <cfloat>
 
 #include "fa4d.h"
@@ -35,6 +38,11 @@ constexpr int kBwdThreads = 512;
 // Depth of the Q / dO / LSE / Delta ring: the load for query tile it+2 is issued
 // while tile it is still being consumed, which hides its L2/HBM latency.
 constexpr int kQStages = 3;
+// Register split (launch: 512 threads x 128 = 65536): producer/MMA warpgroup 88,
+// P/dS warpgroups 152, dQ drain 112 -> 128*88 + 256*152 + 128*112 = 64512.
+constexpr uint32_t kRegsLaunch = 128, kRegsCtl = 88, kRegsSoftmax = 152, kRegsDrain = 112;
+static_assert(128 * kRegsCtl + 256 * kRegsSoftmax + 128 * kRegsDrain <= kBwdThreads * kRegsLaunch,
+              "register split exceeds the launch allocation");
 
 template <int D>
 struct BwdLayout {
@@ -51,7 +59,7 @@ struct BwdLayout {
   static constexpr int kLSE = kDQs + kDQS;               // kQStages x 64 floats
   static constexpr int kDelta = kLSE + kQStages * 256;   // kQStages x 64 floats
   static constexpr int kBar = kDelta + kQStages * 256;
-  static constexpr int kNumBars = 24;
+  static constexpr int kNumBars = 25;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -106,20 +114,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* kv_full = bars + 0;
-  uint64_t* s_full = bars + 1;    // [2]
-  uint64_t* dp_full = bars + 3;
-  uint64_t* ds_full = bars + 4;
-  uint64_t* ds_empty = bars + 5;  // [2]
-  uint64_t* dq_full = bars + 7;
-  uint64_t* dq_empty = bars + 8;
-  uint64_t* dkv_full = bars + 9;
-  uint64_t* mma_drain = bars + 10;
-  uint64_t* p_full = bars + 11;   // [2], one per S^T buffer
-  uint64_t* s_read = bars + 13;   // [2], both P/dS warpgroups have read S^T
-  uint64_t* stage_free = bars + 15;
-  uint64_t* stage_full = bars + 16;
-  uint64_t* q_full = bars + 17;   // [kQStages]
-  uint64_t* q_empty = bars + 20;  // [kQStages]
+  uint64_t* dkv_full = bars + 1;
+  uint64_t* mma_drain = bars + 2;
+  uint64_t* stage_free = bars + 3;
+  uint64_t* stage_full = bars + 4;
+  // Per tile parity (tile it uses buffer it & 1; each is owned by one P/dS warpgroup).
+  uint64_t* s_full = bars + 5;     // [2] S^T of the tile is in TMEM
+  uint64_t* p_full = bars + 7;     // [2] P^T written to TMEM (128 arrivals)
+  uint64_t* dp_full = bars + 9;    // [2] dP^T of the tile is in TMEM
+  uint64_t* ds_full = bars + 11;   // [2] dS^T written to smem (128 arrivals)
+  uint64_t* ds_empty = bars + 13;  // [2] dS^T smem buffer free again
+  uint64_t* dq_full = bars + 15;   // [2] dQ^T of the tile is in TMEM
+  uint64_t* dq_empty = bars + 17;  // [2] drain has read dQ^T (128 arrivals)
+  uint64_t* q_full = bars + 19;    // [kQStages]
+  uint64_t* q_empty = bars + 22;   // [kQStages]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -142,26 +150,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
+    mbar_init(dkv_full, 1);
+    mbar_init(mma_drain, 1);
+    mbar_init(stage_free, 1);
+    mbar_init(stage_full, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&dp_full[i], 1);
+      mbar_init(&ds_full[i], 128);
+      mbar_init(&ds_empty[i], 1);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_empty[i], 128);
+    }
     for (int i = 0; i < kQStages; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&ds_empty[i], 1);
-      // One barrier per S^T buffer: a warp that finishes P for the next iteration
-      // early must not count toward this iteration's arrivals.
-      mbar_init(&p_full[i], 256);
-      mbar_init(&s_read[i], 256);
-    }
-    mbar_init(stage_free, 1);
-    mbar_init(stage_full, 128);
-    mbar_init(dp_full, 1);
-    mbar_init(ds_full, 256);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 128);
-    mbar_init(dkv_full, 1);
-    mbar_init(mma_drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -173,9 +178,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 192, kColDV = 256, kColDK = 256 + D;
+  // S^T x2, then X x2 (dP^T of a tile, later overwritten by its dQ^T), dV, dK.
+  constexpr uint32_t kColS = 0, kColX = 128, kColDV = 256, kColDK = 256 + D;
 
-  if (warp == 0) {
+  if (warp < 4) {
+    // Each role starts with its register budget so the compiler allocates that
+    // role's code under it.
+    regs_dec<kRegsCtl>();
+    if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && N > 0) {
       prefetch_tmap(&p.tm_q);
@@ -213,52 +223,57 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
+    } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Runs two tiles ahead: S and dP of tile it+2 are issued while the P/dS
+    // warpgroups work on tiles it and it+1.
     if (lane == 0 && N > 0) {
       const uint32_t sK = smem_u32(smem + L::kK);
       const uint32_t sV = smem_u32(smem + L::kV);
       const uint32_t sQ = smem_u32(smem + L::kQ);
       const uint32_t sDO = smem_u32(smem + L::kDO);
       const uint32_t sDS = smem_u32(smem + L::kDSb);
-      bool ok = mbar_wait(kv_full, 0, abort_flag) && mbar_wait(&q_full[0], 0, abort_flag);
-      if (ok) {
+      bool ok = mbar_wait(kv_full, 0, abort_flag);
+      for (int j = 0; ok && j < min(2, N); ++j) {
+        ok = mbar_wait(&q_full[j], 0, abort_flag);
+        if (!ok) break;
         tc_fence_after();
-        issue_kt<D, kBF16>(tmem + kColS, sK, sQ);
-        tc_commit(&s_full[0]);
-        issue_kt<D, kBF16>(tmem + kColDP, sV, sDO);
-        tc_commit(dp_full);
+        issue_kt<D, kBF16>(tmem + kColS + 64 * j, sK, sQ + j * L::kQT);
+        tc_commit(&s_full[j]);
+        issue_kt<D, kBF16>(tmem + kColX + 64 * j, sV, sDO + j * L::kQT);
+        tc_commit(&dp_full[j]);
       }
       for (int it = 0; ok && it < N; ++it) {
-        const int st = it & 1;         // S^T / P^T and dS^T buffers
-        const int nx = (it + 1) & 1;
-        const int qs = it % kQStages;  // Q / dO stage of this tile
-        const int qn = (it + 1) % kQStages;
-        if (it + 1 < N) {
-          ok = mbar_wait(&q_full[qn], ((it + 1) / kQStages) & 1, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          issue_kt<D, kBF16>(tmem + kColS + 64 * nx, sK, sQ + qn * L::kQT);
-          tc_commit(&s_full[nx]);
-        }
-        ok = mbar_wait(&p_full[st], (it >> 1) & 1, abort_flag);
+        const int st = it & 1;
+        const uint32_t par = (it >> 1) & 1;
+        const int qs = it % kQStages;
+        ok = mbar_wait(&p_full[st], par, abort_flag);
         if (!ok) break;
         tc_fence_after();
         issue_dv<D, kBF16>(tmem + kColDV, tmem + kColS + 64 * st, sDO + qs * L::kQT, it > 0);
-        ok = mbar_wait(ds_full, it & 1, abort_flag);
+        ok = mbar_wait(&ds_full[st], par, abort_flag);
         if (!ok) break;
         tc_fence_after();
         issue_dk<D, kBF16>(tmem + kColDK, sDS + st * L::kDS, sQ + qs * L::kQT, it > 0);
-        ok = mbar_wait(dq_empty, (it & 1) ^ 1, abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-        issue_dq<D, kBF16>(tmem + kColDQ, sK, sDS + st * L::kDS);
-        tc_commit(dq_full);
         tc_commit(&q_empty[qs]);
+        // dQ^T overwrites this tile's dP^T (read before ds_full).
+        issue_dq<D, kBF16>(tmem + kColX + 64 * st, sK, sDS + st * L::kDS);
+        tc_commit(&dq_full[st]);
         tc_commit(&ds_empty[st]);
-        if (it + 1 < N) {
-          issue_kt<D, kBF16>(tmem + kColDP, sV, sDO + qn * L::kQT);
-          tc_commit(dp_full);
+        const int jn = it + 2;
+        if (jn < N) {
+          const int qn = jn % kQStages;
+          ok = mbar_wait(&q_full[qn], (jn / kQStages) & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          issue_kt<D, kBF16>(tmem + kColS + 64 * st, sK, sQ + qn * L::kQT);
+          tc_commit(&s_full[st]);
+          // dP of tile it+2 reuses X[st] once the drain has read dQ^T of tile it.
+          ok = mbar_wait(&dq_empty[st], par, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          issue_kt<D, kBF16>(tmem + kColX + 64 * st, sV, sDO + qn * L::kQT);
+          tc_commit(&dp_full[st]);
         }
       }
       if (ok) tc_commit(dkv_full);
@@ -266,10 +281,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       mbar_wait(mma_drain, 0, abort_flag);
     }
     __syncwarp();
-  } else if (warp >= 4 && warp < 12) {
+    }
+  } else if (warp < 12) {
+    regs_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ P, dS and dK/dV epilogue
-    const int wg = (warp - 4) >> 2;  // 0: query columns 0-31, 1: columns 32-63
-    const int cb = 32 * wg;
+    const int wg = (warp - 4) >> 2;  // this warpgroup takes tiles it with it % 2 == wg
     const int r = (warp & 3) * 32 + lane;
     const int k = k0 + r;
     const bool k_valid = k < p.Tk;
@@ -280,105 +296,100 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     // selects, so lanes never branch apart before the warp-collective TMEM ops.
     const int kc = min(k, p.Tk - 1);
     bool ok = true;
-    for (int it = 0; it < N; ++it) {
-      const int st = it & 1;
+    for (int it = wg; it < N; it += 2) {
+      const int st = wg;
+      const uint32_t par = (it >> 1) & 1;
+      const int qs = it % kQStages;
       const int g = it / nq;
       const int h = hk * G + g;
       const int q0 = (first_qt + it % nq) * 64;
-      const uint32_t par = (it >> 1) & 1;
-      const int qs = it % kQStages;
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], par, abort_flag) &&
                                        mbar_wait(&q_full[qs], (it / kQStages) & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
       const uint32_t tS = tmem + lane_base + kColS + 64 * st;
-      uint32_t sr[32];
-      tmem_ld32(tS + cb, sr);
-      tmem_wait_ld();
-      // Both warpgroups must have read their S^T columns before either overwrites
-      // columns 0-31 of this buffer with P^T.  (No run-ahead: reaching this buffer's
-      // next use needs every thread's P of this iteration.)
-      mbar_arrive(&s_read[st]);
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_read[st], par, abort_flag));
-      if (!ok) break;
-
-      float lsev[32];
-      {
-        const float4* l4 = reinterpret_cast<const float4*>(sLSE + qs * 64 + cb);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 t = l4[i];
-          lsev[4 * i] = t.x; lsev[4 * i + 1] = t.y; lsev[4 * i + 2] = t.z; lsev[4 * i + 3] = t.w;
-        }
-      }
       const bool need_causal = p.causal && (k0 + 127 > q0 + p.causal_off);
       const bool need_bounds = (q0 + 64 > p.Tq) || (k0 + 128 > p.Tk);
-      float pv[32];
-      if (!kMask && !kScore && !need_causal && !need_bounds) {
-        // Interior tile (warp-uniform): P = exp2(S * scale * log2(e) - LSE).
+      const bool fast = !kMask && !kScore && !need_causal && !need_bounds;  // warp-uniform
+      const float4* l4 = reinterpret_cast<const float4*>(sLSE + qs * 64);
+      const float* score_col = nullptr;
+      const uint8_t* mask_col = nullptr;
+      if (kScore) score_col = p.score + b * p.score_stride[0] + h * p.score_stride[1] + kc;
+      if (kMask) mask_col = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + kc;
+      float pv[64];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) pv[c] = ex2(fmaf(__uint_as_float(sr[c]), p.scale_log2, -lsev[c]));
-      } else {
-        const float* score_col = nullptr;
-        const uint8_t* mask_col = nullptr;
-        if (kScore) score_col = p.score + b * p.score_stride[0] + h * p.score_stride[1] + kc;
-        if (kMask) mask_col = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + kc;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sr[32];
+        tmem_ld32(tS + 32 * half, sr);
+        tmem_wait_ld();
+        if (fast) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int q = q0 + cb + c;
-          const int64_t qc = min(q, p.Tq - 1);
-          bool keep = true;
-          if (need_bounds) keep = k_valid && (q < p.Tq);
-          if (need_causal) keep = keep && (k <= q + p.causal_off);
-          float x = __uint_as_float(sr[c]);
-          if constexpr (kScore) x += __ldg(score_col + qc * p.score_stride[2]);
-          if constexpr (kMask) keep = keep && (__ldg(mask_col + qc * p.mask_stride[2]) != 0);
-          const float e = ex2(fmaf(x, p.scale_log2, -lsev[c]));
-          pv[c] = keep ? e : 0.f;
+          for (int i = 0; i < 8; ++i) {
+            const float4 l = l4[8 * half + i];
+            const int c = 32 * half + 4 * i;
+            pv[c] = ex2(fmaf(__uint_as_float(sr[4 * i]), p.scale_log2, -l.x));
+            pv[c + 1] = ex2(fmaf(__uint_as_float(sr[4 * i + 1]), p.scale_log2, -l.y));
+            pv[c + 2] = ex2(fmaf(__uint_as_float(sr[4 * i + 2]), p.scale_log2, -l.z));
+            pv[c + 3] = ex2(fmaf(__uint_as_float(sr[4 * i + 3]), p.scale_log2, -l.w));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int c = 32 * half + i;
+            const int q = q0 + c;
+            const int64_t qc = min(q, p.Tq - 1);
+            bool keep = true;
+            if (need_bounds) keep = k_valid && (q < p.Tq);
+            if (need_causal) keep = keep && (k <= q + p.causal_off);
+            float x = __uint_as_float(sr[i]);
+            if constexpr (kScore) x += __ldg(score_col + qc * p.score_stride[2]);
+            if constexpr (kMask) keep = keep && (__ldg(mask_col + qc * p.mask_stride[2]) != 0);
+            const float e = ex2(fmaf(x, p.scale_log2, -sLSE[qs * 64 + c]));
+            pv[c] = keep ? e : 0.f;
+          }
         }
-      }
-      {
+        // P^T (16-bit) for these 32 queries goes to columns 16*half .. 16*half+15,
+        // which hold S^T values this thread has already read.
         uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = pack2<kBF16>(pv[2 * i], pv[2 * i + 1]);
-        tmem_st16(tS + 16 * wg, pk);
+        for (int i = 0; i < 16; ++i) pk[i] = pack2<kBF16>(pv[32 * half + 2 * i], pv[32 * half + 2 * i + 1]);
+        tmem_st16(tS + 16 * half, pk);
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[st]);
 
-      ok = __all_sync(0xffffffffu, mbar_wait(dp_full, it & 1, abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(&dp_full[st], par, abort_flag) &&
+                                       mbar_wait(&ds_empty[st], par ^ 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      tmem_ld32(tmem + lane_base + kColDP + cb, sr);
-      tmem_wait_ld();
-      // dS without the softmax scale: dK and dQ are scaled once at their outputs.
-      uint32_t dsk[16];
-      {
-        const float4* d4 = reinterpret_cast<const float4*>(sDelta + qs * 64 + cb);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 t = d4[i];
-          const float e0 = pv[4 * i] * (__uint_as_float(sr[4 * i]) - t.x);
-          const float e1 = pv[4 * i + 1] * (__uint_as_float(sr[4 * i + 1]) - t.y);
-          const float e2 = pv[4 * i + 2] * (__uint_as_float(sr[4 * i + 2]) - t.z);
-          const float e3 = pv[4 * i + 3] * (__uint_as_float(sr[4 * i + 3]) - t.w);
-          dsk[2 * i] = pack2<kBF16>(e0, e1);
-          dsk[2 * i + 1] = pack2<kBF16>(e2, e3);
-        }
-      }
-      ok = __all_sync(0xffffffffu, mbar_wait(&ds_empty[st], par ^ 1, abort_flag));
-      if (!ok) break;
-      // Row r of the dS^T tile: 128 B in 8 chunks of 16 B, 128-B swizzled (chunk ^ (row % 8));
-      // this warpgroup owns chunks 4*wg .. 4*wg+3.
+      const float4* d4 = reinterpret_cast<const float4*>(sDelta + qs * 64);
       uint8_t* ds_row = smem + L::kDSb + st * L::kDS + r * 128;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc)
-        *reinterpret_cast<uint4*>(ds_row + (((4 * wg + cc) ^ (r & 7)) << 4)) =
-            make_uint4(dsk[4 * cc], dsk[4 * cc + 1], dsk[4 * cc + 2], dsk[4 * cc + 3]);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sr[32];
+        tmem_ld32(tmem + lane_base + kColX + 64 * st + 32 * half, sr);
+        tmem_wait_ld();
+        // dS without the softmax scale: dK and dQ are scaled once at their outputs.
+        uint32_t dsk[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 t = d4[8 * half + i];
+          const int c = 32 * half + 4 * i;
+          dsk[2 * i] = pack2<kBF16>(pv[c] * (__uint_as_float(sr[4 * i]) - t.x),
+                                    pv[c + 1] * (__uint_as_float(sr[4 * i + 1]) - t.y));
+          dsk[2 * i + 1] = pack2<kBF16>(pv[c + 2] * (__uint_as_float(sr[4 * i + 2]) - t.z),
+                                        pv[c + 3] * (__uint_as_float(sr[4 * i + 3]) - t.w));
+        }
+        // Row r of the dS^T tile: 128 B in 8 chunks of 16 B, 128-B swizzled (chunk ^ (row % 8)).
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+          *reinterpret_cast<uint4*>(ds_row + (((4 * half + cc) ^ (r & 7)) << 4)) =
+              make_uint4(dsk[4 * cc], dsk[4 * cc + 1], dsk[4 * cc + 2], dsk[4 * cc + 3]);
+      }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(ds_full);
+      mbar_arrive(&ds_full[st]);
     }
 
     // Epilogue: warpgroup 0 writes dV, warpgroup 1 writes dK (zeros when no query
@@ -414,7 +425,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       for (int u = 0; u < D / 8; ++u) reinterpret_cast<uint4*>(dst_row)[u] = make_uint4(0, 0, 0, 0);
     }
     tc_fence_before();
-  } else if (warp >= 12) {
+  } else {
+    regs_dec<kRegsDrain>();
     // ------------------------------------------------------------ dQ drain
     const int wq = warp & 3;
     // M = D accumulator layout: D=128 uses all 128 lanes; D=64 (M=64) puts rows
@@ -422,21 +434,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     const int d = (D == 128) ? (wq * 32 + lane) : (wq * 16 + lane);
     const bool d_valid = (D == 128) || (lane < 16);
     const bool leader = (warp == 12 && lane == 0);
-    const uint32_t tDQ = tmem + (static_cast<uint32_t>(wq * 32) << 16) + kColDQ;
     float* stage = reinterpret_cast<float*>(smem + L::kDQs);  // [64 queries][D]
     for (int it = 0; it < N; ++it) {
+      const int st = it & 1;
       const int g = it / nq;
       const int h = hk * G + g;
       const int q0 = (first_qt + it % nq) * 64;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, abort_flag));
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&dq_full[st], (it >> 1) & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
+      const uint32_t tDQ = tmem + (static_cast<uint32_t>(wq * 32) << 16) + kColX + 64 * st;
       uint32_t v[64];
       tmem_ld32(tDQ, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
       tmem_ld32(tDQ + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(dq_empty);
+      mbar_arrive(&dq_empty[st]);
       // The previous tile's bulk reduction must have finished reading the staging tile.
       if (leader) {
         bulk_wait_read_all();

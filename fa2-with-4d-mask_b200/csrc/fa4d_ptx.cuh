@@ -221,6 +221,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+// Per-warp register budget change (all warps of a warpgroup execute it).  The
+// increases are satisfied from registers released by decreases, so the sum over
+// warpgroups must stay within the block's launch allocation (threads x registers).
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 // ------------------------------------------------------------------ descriptors
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand (tile base
 // 1024-B aligned).  K-major: lbo is unused (16), sbo = 1024 (8 rows of 128 B).
