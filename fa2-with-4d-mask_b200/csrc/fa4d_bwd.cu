@@ -226,61 +226,80 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     // Runs two tiles ahead: S and dP of tile it+2 are issued while the P/dS
-    // warpgroups work on tiles it and it+1.
-    if (lane == 0 && N > 0) {
+    // warpgroups work on tiles it and it+1.  The whole warp runs the loop (waits
+    // included); each group of MMAs and its commits is issued by one elected lane.
+    if (N > 0) {
       const uint32_t sK = smem_u32(smem + L::kK);
       const uint32_t sV = smem_u32(smem + L::kV);
       const uint32_t sQ = smem_u32(smem + L::kQ);
       const uint32_t sDO = smem_u32(smem + L::kDO);
       const uint32_t sDS = smem_u32(smem + L::kDSb);
-      bool ok = mbar_wait(kv_full, 0, abort_flag);
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+      };
+      bool ok = wait(kv_full, 0);
       for (int j = 0; ok && j < min(2, N); ++j) {
-        ok = mbar_wait(&q_full[j], 0, abort_flag);
+        ok = wait(&q_full[j], 0);
         if (!ok) break;
         tc_fence_after();
-        issue_kt<D, kBF16>(tmem + kColS + 64 * j, sK, sQ + j * L::kQT);
-        tc_commit(&s_full[j]);
-        issue_kt<D, kBF16>(tmem + kColX + 64 * j, sV, sDO + j * L::kQT);
-        tc_commit(&dp_full[j]);
+        if (elect_one()) {
+          issue_kt<D, kBF16>(tmem + kColS + 64 * j, sK, sQ + j * L::kQT);
+          tc_commit(&s_full[j]);
+          issue_kt<D, kBF16>(tmem + kColX + 64 * j, sV, sDO + j * L::kQT);
+          tc_commit(&dp_full[j]);
+        }
+        __syncwarp();
       }
       for (int it = 0; ok && it < N; ++it) {
         const int st = it & 1;
         const uint32_t par = (it >> 1) & 1;
         const int qs = it % kQStages;
-        ok = mbar_wait(&p_full[st], par, abort_flag);
+        ok = wait(&p_full[st], par);
         if (!ok) break;
         tc_fence_after();
-        issue_dv<D, kBF16>(tmem + kColDV, tmem + kColS + 64 * st, sDO + qs * L::kQT, it > 0);
-        ok = mbar_wait(&ds_full[st], par, abort_flag);
+        if (elect_one()) issue_dv<D, kBF16>(tmem + kColDV, tmem + kColS + 64 * st, sDO + qs * L::kQT, it > 0);
+        __syncwarp();
+        ok = wait(&ds_full[st], par);
         if (!ok) break;
         tc_fence_after();
-        issue_dk<D, kBF16>(tmem + kColDK, sDS + st * L::kDS, sQ + qs * L::kQT, it > 0);
-        tc_commit(&q_empty[qs]);
-        // dQ^T overwrites this tile's dP^T (read before ds_full).
-        issue_dq<D, kBF16>(tmem + kColX + 64 * st, sK, sDS + st * L::kDS);
-        tc_commit(&dq_full[st]);
-        tc_commit(&ds_empty[st]);
+        if (elect_one()) {
+          issue_dk<D, kBF16>(tmem + kColDK, sDS + st * L::kDS, sQ + qs * L::kQT, it > 0);
+          tc_commit(&q_empty[qs]);
+          // dQ^T overwrites this tile's dP^T (read before ds_full).
+          issue_dq<D, kBF16>(tmem + kColX + 64 * st, sK, sDS + st * L::kDS);
+          tc_commit(&dq_full[st]);
+          tc_commit(&ds_empty[st]);
+        }
+        __syncwarp();
         const int jn = it + 2;
         if (jn < N) {
           const int qn = jn % kQStages;
-          ok = mbar_wait(&q_full[qn], (jn / kQStages) & 1, abort_flag);
+          ok = wait(&q_full[qn], (jn / kQStages) & 1);
           if (!ok) break;
           tc_fence_after();
-          issue_kt<D, kBF16>(tmem + kColS + 64 * st, sK, sQ + qn * L::kQT);
-          tc_commit(&s_full[st]);
+          if (elect_one()) {
+            issue_kt<D, kBF16>(tmem + kColS + 64 * st, sK, sQ + qn * L::kQT);
+            tc_commit(&s_full[st]);
+          }
+          __syncwarp();
           // dP of tile it+2 reuses X[st] once the drain has read dQ^T of tile it.
-          ok = mbar_wait(&dq_empty[st], par, abort_flag);
+          ok = wait(&dq_empty[st], par);
           if (!ok) break;
           tc_fence_after();
-          issue_kt<D, kBF16>(tmem + kColX + 64 * st, sV, sDO + qn * L::kQT);
-          tc_commit(&dp_full[st]);
+          if (elect_one()) {
+            issue_kt<D, kBF16>(tmem + kColX + 64 * st, sV, sDO + qn * L::kQT);
+            tc_commit(&dp_full[st]);
+          }
+          __syncwarp();
         }
       }
-      if (ok) tc_commit(dkv_full);
-      tc_commit(mma_drain);
-      mbar_wait(mma_drain, 0, abort_flag);
+      if (elect_one()) {
+        if (ok) tc_commit(dkv_full);
+        tc_commit(mma_drain);
+      }
+      __syncwarp();
+      wait(mma_drain, 0);
     }
-    __syncwarp();
     }
   } else if (warp < 12) {
     regs_inc<kRegsSoftmax>();

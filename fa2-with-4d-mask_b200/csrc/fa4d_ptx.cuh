@@ -233,6 +233,19 @@ __device__ __forceinline__ void regs_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
 }
 
+// True in exactly one lane of a converged warp (elect.sync).  MMA issue loops run
+// on the whole warp and issue from the elected lane, so the compiler keeps the
+// loop's values in uniform registers.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // ------------------------------------------------------------------ descriptors
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand (tile base
 // 1024-B aligned).  K-major: lbo is unused (16), sbo = 1024 (8 rows of 128 B).
