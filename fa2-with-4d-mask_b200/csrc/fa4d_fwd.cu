@@ -182,56 +182,70 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n_max > 0) {
+    // The whole warp runs the loop (waits included); each group of MMAs and its
+    // commits is issued by one elected lane, keeping the issue state uniform.
+    if (n_max > 0) {
       const uint32_t sQ = smem_u32(smem + L::kQ);
       const uint32_t sK = smem_u32(smem + L::kK);
       const uint32_t sV = smem_u32(smem + L::kV);
-      bool ok = mbar_wait(q_full, 0, abort_flag) &&
-                mbar_wait(&k_full[0], 0, abort_flag);
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+      };
+      bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
       if (ok) {
         tc_fence_after();
+        if (elect_one()) {
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (n_slot[t] > 0) {
-            issue_qk<D, kBF16>(tmem + 128 * t, sQ + t * L::kTile, sK);
-            tc_commit(&s_full[t]);
+          for (int t = 0; t < 2; ++t) {
+            if (n_slot[t] > 0) {
+              issue_qk<D, kBF16>(tmem + 128 * t, sQ + t * L::kTile, sK);
+              tc_commit(&s_full[t]);
+            }
           }
+          tc_commit(&k_empty[0]);
         }
-        tc_commit(&k_empty[0]);
+        __syncwarp();
       }
       for (int j = 0; ok && j < n_max; ++j) {
         const int sv = j & 1;
-        ok = mbar_wait(&v_full[sv], (j >> 1) & 1, abort_flag);
+        ok = wait(&v_full[sv], (j >> 1) & 1);
         if (!ok) break;
         const bool has_next = j + 1 < n_max;
         const int sk = (j + 1) & 1;
         if (has_next) {
-          ok = mbar_wait(&k_full[sk], ((j + 1) >> 1) & 1, abort_flag);
+          ok = wait(&k_full[sk], ((j + 1) >> 1) & 1);
           if (!ok) break;
         }
         tc_fence_after();
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (j < n_slot[t]) {
-            ok = mbar_wait(&p_full[t], j & 1, abort_flag);
+            ok = wait(&p_full[t], j & 1);
             if (!ok) break;
             tc_fence_after();
-            issue_pv<D, kBF16>(tmem + 256 + D * t, tmem + 128 * t, sV + sv * L::kTile, j > 0);
-            if (j + 1 < n_slot[t]) {
-              issue_qk<D, kBF16>(tmem + 128 * t, sQ + t * L::kTile, sK + sk * L::kTile);
-              tc_commit(&s_full[t]);
-            } else {
-              tc_commit(&o_full[t]);
+            if (elect_one()) {
+              issue_pv<D, kBF16>(tmem + 256 + D * t, tmem + 128 * t, sV + sv * L::kTile, j > 0);
+              if (j + 1 < n_slot[t]) {
+                issue_qk<D, kBF16>(tmem + 128 * t, sQ + t * L::kTile, sK + sk * L::kTile);
+                tc_commit(&s_full[t]);
+              } else {
+                tc_commit(&o_full[t]);
+              }
             }
+            __syncwarp();
           }
         }
         if (!ok) break;
-        tc_commit(&v_empty[sv]);
-        if (has_next) tc_commit(&k_empty[sk]);
+        if (elect_one()) {
+          tc_commit(&v_empty[sv]);
+          if (has_next) tc_commit(&k_empty[sk]);
+        }
+        __syncwarp();
       }
       // Every MMA must have completed before TMEM is released.
-      tc_commit(mma_drain);
-      mbar_wait(mma_drain, 0, abort_flag);
+      if (elect_one()) tc_commit(mma_drain);
+      __syncwarp();
+      wait(mma_drain, 0);
     }
     __syncwarp();
   } else if (warp >= 4) {
