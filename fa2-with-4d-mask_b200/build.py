@@ -48,7 +48,7 @@ def _stale(target: Path, inputs: list[Path]) -> bool:
 
 # Kernels that rebalance registers with setmaxnreg assume this exact allocation per
 # thread at launch; fewer would make a setmaxnreg.inc wait forever.
-LAUNCH_REGS = {"bwd_kernel": 128}
+LAUNCH_REGS = {"bwd_kernel": 128, "fwd_kernel": 168}
 
 
 def _check_launch_regs(src: Path, log: str) -> None:

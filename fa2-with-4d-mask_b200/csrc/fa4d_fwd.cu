@@ -28,6 +28,11 @@ namespace fa4d {
 namespace {
 
 constexpr int kFwdThreads = 384;
+// Register split (launch: 384 threads x 168 = 64512): producer/MMA warpgroup 112,
+// the two softmax warpgroups 192 -> 128*112 + 256*192 = 63488.
+constexpr uint32_t kFwdRegsLaunch = 168, kFwdRegsCtl = 112, kFwdRegsSoftmax = 192;
+static_assert(128 * kFwdRegsCtl + 256 * kFwdRegsSoftmax <= kFwdThreads * kFwdRegsLaunch,
+              "register split exceeds the launch allocation");
 constexpr float kNegInf = -INFINITY;
 // O is only rescaled when the running max grows by more than this (log2 units);
 // in between, P = exp2(s - stale max) stays <= 2^8, exact after the final 1/l.
@@ -139,7 +144,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp < 4) {
+    // Each role starts with its register budget so the compiler allocates that
+    // role's code under it.
+    regs_dec<kFwdRegsCtl>();
+    if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && n_max > 0) {
       prefetch_tmap(&p.tm_q);
@@ -180,7 +189,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
+    } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     // The whole warp runs the loop (waits included); each group of MMAs and its
     // commits is issued by one elected lane, keeping the issue state uniform.
@@ -248,7 +257,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       wait(mma_drain, 0);
     }
     __syncwarp();
-  } else if (warp >= 4) {
+    }
+  } else {
+    regs_inc<kFwdRegsSoftmax>();
     // ------------------------------------------------------------ softmax + epilogue
     const int t = (warp - 4) >> 2;
     const int row = (warp & 3) * 32 + lane;
@@ -284,7 +295,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       const int kbase = j * 128;
       const bool need_bounds = kbase + 128 > p.Tk;
       const bool need_causal = p.causal && (kbase + 127 > qs + p.causal_off);
+      // Interior tile (warp-uniform): nothing to add or mask, so the row max is taken
+      // on raw S and the scale is folded into the exponent's FMA below.
+      const bool fast = !kMask && !kScore && !need_bounds && !need_causal && p.scale_log2 > 0.f;
       float m_tile = kNegInf;
+      if (fast) {
+        float m4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
+#pragma unroll
+        for (int i = 0; i < 128; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(sr[i]));
+        m_tile = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
+      } else {
 #pragma unroll
       for (int c4 = 0; c4 < 32; ++c4) {
         const int k4 = kbase + 4 * c4;
@@ -328,6 +348,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
           m_tile = fmaxf(m_tile, x);
         }
       }
+      }
 
       // Online softmax with lazy rescaling of O.
       const float m_new = fmaxf(m_run, m_tile);
@@ -352,17 +373,36 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       }
       const float m_use = (m_run == kNegInf) ? 0.f : m_run;
       float rowsum = 0.f;
+      if (fast) {
+        // exp2(s * scale * log2(e) - m); one element in four on the FMA pipe
+        // (ex2_poly) so the MUFU unit is not the limit.
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2(__uint_as_float(sr[32 * c + 2 * i]) - m_use);
-          const float p1 = ex2(__uint_as_float(sr[32 * c + 2 * i + 1]) - m_use);
-          rowsum += p0 + p1;
-          pk[i] = pack2<kBF16>(p0, p1);
+          for (int i = 0; i < 16; ++i) {
+            const float a0 = fmaf(__uint_as_float(sr[32 * c + 2 * i]), p.scale_log2, -m_use);
+            const float a1 = fmaf(__uint_as_float(sr[32 * c + 2 * i + 1]), p.scale_log2, -m_use);
+            const float p0 = ex2(a0);
+            const float p1 = (i & 1) ? ex2_poly(a1) : ex2(a1);
+            rowsum += p0 + p1;
+            pk[i] = pack2<kBF16>(p0, p1);
+          }
+          tmem_st16(tS + 16 * c, pk);
         }
-        tmem_st16(tS + 16 * c, pk);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = ex2(__uint_as_float(sr[32 * c + 2 * i]) - m_use);
+            const float p1 = ex2(__uint_as_float(sr[32 * c + 2 * i + 1]) - m_use);
+            rowsum += p0 + p1;
+            pk[i] = pack2<kBF16>(p0, p1);
+          }
+          tmem_st16(tS + 16 * c, pk);
+        }
       }
       l_run += rowsum;
       tmem_wait_st();
