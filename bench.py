@@ -219,6 +219,8 @@ def _run_ours(args, _lib):
     per_rank = fwd_bwd_flops(B, HQ, T, T, D, False)
     value = world * per_rank / (t_step * 1e-3) / 1e12
     status = _lib.device_status(dev)
+    # End-to-end leg on every rank (each rank its own host batch element), max over ranks.
+    e2e = run_e2e(api, dev, args, dist, world) if args.e2e_steps > 0 else None
 
     if rank != 0:
         if dist:
@@ -275,8 +277,8 @@ def _run_ours(args, _lib):
     }
     if args.extra and world == 1:
         line["extra"] = extra_measurements(_lib, dev, peaks)
-    if args.e2e_steps > 0:
-        line["e2e"] = run_e2e(api, dev, args)
+    if e2e is not None:
+        line["e2e"] = e2e
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args)
     if dist:
@@ -390,10 +392,11 @@ def extra_measurements(_lib, dev, peaks):
     return out
 
 
-def run_e2e(api, dev, args):
+def run_e2e(api, dev, args, dist=None, world=1):
     """Same metric through the public API with pinned host buffers: each step copies
     q/k/v/dO host->device, runs forward + autograd backward and copies O, dQ, dK, dV
-    device->host."""
+    device->host.  Every rank runs it on its own batch element; the step time is the
+    max over ranks and the value is whole-job (all ranks' FLOPs)."""
     g = torch.Generator()
     g.manual_seed(77)
     host = lambda shape: torch.randn(shape, generator=g).to(torch.bfloat16).pin_memory()
@@ -413,8 +416,11 @@ def run_e2e(api, dev, args):
         for dst, src in zip(outs, (o, q.grad, k.grad, v.grad)):
             dst.copy_(src.detach().transpose(1, 2), non_blocking=True)
 
-    for _ in range(2):
+    for _ in range(3):
         step()
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
     torch.cuda.synchronize(dev)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
@@ -422,9 +428,12 @@ def run_e2e(api, dev, args):
         step()
     b.record()
     torch.cuda.synchronize(dev)
-    ms = a.elapsed_time(b) / args.e2e_steps
-    return {"value": round(fwd_bwd_flops(B, HQ, T, T, D, False) / (ms * 1e-3) / 1e12, 2), "unit": UNIT,
-            "ms_per_step": round(ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+    t = torch.tensor([a.elapsed_time(b) / args.e2e_steps], device=dev, dtype=torch.float64)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"value": round(world * fwd_bwd_flops(B, HQ, T, T, D, False) / (ms * 1e-3) / 1e12, 2), "unit": UNIT,
+            "ms_per_step": round(ms, 4), "h2d_bytes_per_step": world * h2d, "d2h_bytes_per_step": world * d2h,
             "path": "tilelang_flash_attention + autograd backward, pinned host in/out"}
 
 

@@ -45,6 +45,7 @@ EXPORTED_SYMBOLS = (
     "fa4d_last_error",
     "fa4d_device_status",
     "fa4d_abi_version",
+    "fa4d_check_exp2",
 )
 
 _i64x3 = ctypes.c_int64 * 3
@@ -151,6 +152,8 @@ def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
     lib.fa4d_device_status.restype = ctypes.c_int
     lib.fa4d_abi_version.argtypes = []
     lib.fa4d_abi_version.restype = ctypes.c_int
+    lib.fa4d_check_exp2.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_float, ctypes.c_float, ctypes.c_void_p]
+    lib.fa4d_check_exp2.restype = ctypes.c_int
     if path is None:
         _LIB = lib
     return lib

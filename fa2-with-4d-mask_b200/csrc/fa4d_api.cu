@@ -159,6 +159,15 @@ const char* fa4d_last_error(void) { return g_last_error.c_str(); }
 
 int fa4d_abi_version(void) { return FA4D_ABI_VERSION; }
 
+int fa4d_check_exp2(float* out, int32_t n, float lo, float hi, void* stream) {
+  if (!out || n < 2) return fail(FA4D_ERR_INVALID, "out must be a device buffer of n >= 2 floats");
+  int rc = bind_device_of(out, "out");
+  if (rc) return rc;
+  cudaError_t e = fa4d::launch_exp2_check(out, n, lo, hi, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "exp2 check launch failed: %s", cudaGetErrorString(e));
+  return ok();
+}
+
 int fa4d_device_status(int device, void* stream, int clear) {
   cudaError_t se = cudaSetDevice(device);
   if (se != cudaSuccess) return fail(FA4D_ERR_CUDA, "cudaSetDevice(%d) failed: %s", device, cudaGetErrorString(se));

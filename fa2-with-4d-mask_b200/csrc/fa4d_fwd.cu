@@ -486,3 +486,22 @@ cudaError_t launch_fwd(const FwdParams& p, int D, bool bf16, bool has_mask, bool
 }
 
 }  // namespace fa4d
+
+namespace {
+
+// out[i] = ex2_poly(x_i) / exp2f(x_i) - 1 on an even grid x_i over [lo, hi].
+__global__ void exp2_check_kernel(float* out, int n, float lo, float hi) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float x = lo + (hi - lo) * (static_cast<float>(i) / static_cast<float>(n - 1));
+  out[i] = fa4d::ex2_poly(x) / exp2f(x) - 1.0f;
+}
+
+}  // namespace
+
+namespace fa4d {
+cudaError_t launch_exp2_check(float* out, int n, float lo, float hi, cudaStream_t s) {
+  exp2_check_kernel<<<(n + 255) / 256, 256, 0, s>>>(out, n, lo, hi);
+  return cudaGetLastError();
+}
+}  // namespace fa4d

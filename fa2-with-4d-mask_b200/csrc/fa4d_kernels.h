@@ -85,5 +85,6 @@ cudaError_t launch_fwd(const FwdParams& p, int D, bool bf16, bool has_mask, bool
 cudaError_t launch_bwd(const BwdParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);
 cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s);
+cudaError_t launch_exp2_check(float* out, int n, float lo, float hi, cudaStream_t s);
 
 }  // namespace fa4d

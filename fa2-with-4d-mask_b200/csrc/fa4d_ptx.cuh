@@ -279,8 +279,9 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x evaluated on the FMA pipe, for finite x <= ~64 (arguments below -126 return
-// 2^-126 instead of 0, so callers use it only where no argument is -inf).
+// 2^x evaluated on the FMA pipe, for finite x <= ~64.  Arguments below -126 are
+// clamped and results under ~2^-120 are only approximately tiny (no exact zero), so
+// callers use it only where no argument is -inf and such values are negligible.
 // Cody-Waite split x = n + f with n = round(x) (the 1.5 * 2^23 addition rounds to
 // an integer held in the low mantissa bits) and f in [-1/2, 1/2]; 2^f is a degree-3
 // polynomial whose coefficients were fitted for this library (relative-error-weighted

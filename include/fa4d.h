@@ -168,6 +168,12 @@ int fa4d_device_status(int device, void* stream, int clear);
 /* FA4D_ABI_VERSION of the loaded library. */
 int fa4d_abi_version(void);
 
+/* Diagnostic (no counterpart in the reference): writes out[i] = e(x_i)/exp2f(x_i) - 1
+ * for n points x_i evenly spaced over [lo, hi], where e is the polynomial exp2 the
+ * forward kernel evaluates on the FMA pipe for part of its exponentials.  `out` is a
+ * device buffer of n floats. */
+int fa4d_check_exp2(float* out, int32_t n, float lo, float hi, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
