@@ -351,12 +351,18 @@ def extra_measurements(_lib, dev, peaks):
     peak = peaks["bf16_tflops"]
 
     def fb(b, tq, tk, hq, hk, d, causal_mode, mask=None, score=None, iters=5):
+        """(fwd ms, bwd ms) with the mask's block map built once beforehand (as the op
+        caches it per mask); the map pass itself is timed by map_ms()."""
         q, k, v, do = (x.transpose(1, 2) for x in _dev_inputs(dev, b, tq, tk, hq, hk, d, seed=3))
         sc = d ** -0.5
-        tf = time_fn(lambda: _lib.forward(q, k, v, mask, score, sc, causal_mode), iters)
-        o, lse = _lib.forward(q, k, v, mask, score, sc, causal_mode)
-        tb = time_fn(lambda: _lib.backward(do, q, k, v, o, lse, mask, score, sc, causal_mode), iters)
+        bm = _lib.mask_blocks(mask) if mask is not None else None
+        tf = time_fn(lambda: _lib.forward(q, k, v, mask, score, sc, causal_mode, blocks=bm), iters)
+        o, lse = _lib.forward(q, k, v, mask, score, sc, causal_mode, blocks=bm)
+        tb = time_fn(lambda: _lib.backward(do, q, k, v, o, lse, mask, score, sc, causal_mode, blocks=bm), iters)
         return tf, tb
+
+    def map_ms(mask):
+        return round(time_fn(lambda: _lib.mask_blocks(mask), 5), 4)
 
     tf, tb = fb(B, T, T, HQ, HK, D, _lib.CAUSAL_TOP_LEFT)
     ff, fbf = fwd_flops(B, HQ, T, T, D, True), fwd_bwd_flops(B, HQ, T, T, D, True)
@@ -373,17 +379,25 @@ def extra_measurements(_lib, dev, peaks):
     out["cfg4_score_mask"] = {"fwd_ms": round(tf, 4), "fwd_gbs": round(bytes_fwd / tf / 1e6, 1),
                               "fwd_frac_hbm": round(bytes_fwd / tf / 1e6 / peaks["hbm_gbs"], 4),
                               "fwd_bwd_ms": round(tf + tb, 4),
-                              "algorithmic_fwd_bytes": bytes_fwd}
+                              "algorithmic_fwd_bytes": bytes_fwd,
+                              "block_map_ms": map_ms(mask)}
     del score, mask
     # cfg3: packed-document [B,1,T,T] mask
     b3, t3 = 2, 4096
     mask = _packed_doc_mask(dev, b3, t3)
-    tf, tb = fb(b3, t3, t3, HQ, HK, D, _lib.CAUSAL_NONE, mask=mask.expand(b3, HQ, t3, t3), iters=3)
+    mview = mask.expand(b3, HQ, t3, t3)
+    tf, tb = fb(b3, t3, t3, HQ, HK, D, _lib.CAUSAL_NONE, mask=mview, iters=3)
     ff, fbf = fwd_flops(b3, HQ, t3, t3, D, False), fwd_bwd_flops(b3, HQ, t3, t3, D, False)
+    counts = _lib.mask_blocks(mview).counts()
+    live = (counts["partial"] + counts["full"]) / sum(counts.values())
     out["cfg3_packed_docs"] = {"fwd_ms": round(tf, 4), "fwd_bwd_ms": round(tf + tb, 4),
                                "fwd_dense_equiv_tflops": round(ff / tf / 1e9, 1),
-                               "fwd_bwd_dense_equiv_tflops": round(fbf / (tf + tb) / 1e9, 1)}
-    del mask
+                               "fwd_bwd_dense_equiv_tflops": round(fbf / (tf + tb) / 1e9, 1),
+                               "blocks": counts,
+                               "fwd_live_block_tflops": round(live * ff / tf / 1e9, 1),
+                               "fwd_bwd_live_block_tflops": round(live * fbf / (tf + tb) / 1e9, 1),
+                               "block_map_ms": map_ms(mview)}
+    del mask, mview
     # cfg5: MQA, bshd, bottom-right causal, one GPU's shard of 16 (B=2)
     tf, tb = fb(2, 1024, 4096, 64, 1, 64, _lib.CAUSAL_BOTTOM_RIGHT, iters=3)
     ff, fbf = fwd_flops(2, 64, 1024, 4096, 64, True), fwd_bwd_flops(2, 64, 1024, 4096, 64, True)

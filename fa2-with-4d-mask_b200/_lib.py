@@ -46,7 +46,13 @@ EXPORTED_SYMBOLS = (
     "fa4d_device_status",
     "fa4d_abi_version",
     "fa4d_check_exp2",
+    "fa4d_mask_blocks",
+    "fa4d_mask_blocks_size",
 )
+
+ABI_VERSION = 2
+BLOCK = 128  # rows / keys per block of the mask's block map
+BLOCK_EMPTY, BLOCK_PARTIAL, BLOCK_FULL = 0, 1, 2
 
 _i64x3 = ctypes.c_int64 * 3
 
@@ -78,6 +84,8 @@ class FwdArgs(ctypes.Structure):
         ("causal", ctypes.c_int32),
         ("scale", ctypes.c_float),
         ("reserved", ctypes.c_int32 * 3),
+        ("mask_blocks", ctypes.c_void_p),
+        ("mask_blocks_stride", ctypes.c_int64 * 2),
     ]
 
 
@@ -118,6 +126,8 @@ class BwdArgs(ctypes.Structure):
         ("deterministic", ctypes.c_int32),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("mask_blocks", ctypes.c_void_p),
+        ("mask_blocks_stride", ctypes.c_int64 * 2),
     ]
 
 
@@ -154,6 +164,22 @@ def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
     lib.fa4d_abi_version.restype = ctypes.c_int
     lib.fa4d_check_exp2.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_float, ctypes.c_float, ctypes.c_void_p]
     lib.fa4d_check_exp2.restype = ctypes.c_int
+    lib.fa4d_mask_blocks_size.argtypes = [ctypes.c_int32] * 4
+    lib.fa4d_mask_blocks_size.restype = ctypes.c_size_t
+    lib.fa4d_mask_blocks.argtypes = [
+        ctypes.c_void_p,
+        ctypes.POINTER(ctypes.c_int64),
+        ctypes.c_int32,
+        ctypes.c_int32,
+        ctypes.c_int32,
+        ctypes.c_int32,
+        ctypes.c_void_p,
+        ctypes.c_void_p,
+    ]
+    lib.fa4d_mask_blocks.restype = ctypes.c_int
+    version = lib.fa4d_abi_version()
+    if version != ABI_VERSION:
+        raise RuntimeError(f"{p}: ABI version {version}, expected {ABI_VERSION}; rebuild with build.py")
     if path is None:
         _LIB = lib
     return lib
@@ -220,6 +246,53 @@ def prepare_bias(x: Optional[torch.Tensor], dtype: torch.dtype) -> Optional[torc
     return x
 
 
+class BlockMap:
+    """Block map of one mask (``fa4d_mask_blocks``): ``blocks`` is a uint8 tensor
+    [Bm, Hm, ceil(Tq/128), ceil(Tk/128)] and ``strides`` the (batch, head) byte
+    strides the kernels index it with (0 where the mask broadcasts)."""
+
+    __slots__ = ("blocks", "strides")
+
+    def __init__(self, blocks: torch.Tensor, strides: tuple):
+        self.blocks = blocks
+        self.strides = strides
+
+    def counts(self) -> dict:
+        """Number of EMPTY / PARTIAL / FULL blocks (synchronises)."""
+        flat = self.blocks.flatten().to(torch.int64)
+        c = torch.bincount(flat, minlength=3).tolist()
+        return {"empty": c[0], "partial": c[1], "full": c[2]}
+
+
+def mask_blocks(mask: torch.Tensor) -> BlockMap:
+    """Runs the block-occupancy pre-pass over a [B|1, H|1, Tq, Tk] bool/uint8 mask view
+    with unit key stride (broadcast dimensions may have stride 0)."""
+    lib = load_library()
+    if mask.dim() != 4 or mask.element_size() != 1 or mask.stride(3) != 1:
+        raise ValueError("mask must be a 4D bool/uint8 tensor with unit key stride")
+    Bf, Hf, Tq, Tk = mask.shape
+    sb, sh, sr = _bias_strides(mask)
+    Bm = Bf if sb != 0 else 1
+    Hm = Hf if sh != 0 else 1
+    nqb, nkb = -(-Tq // BLOCK), -(-Tk // BLOCK)
+    blocks = torch.empty((Bm, Hm, nqb, nkb), dtype=torch.uint8, device=mask.device)
+    st = (ctypes.c_int64 * 3)(sb, sh, sr)
+    with torch.cuda.device(mask.device):
+        rc = lib.fa4d_mask_blocks(mask.data_ptr(), st, Bm, Hm, Tq, Tk, blocks.data_ptr(), _stream_ptr(mask.device))
+    if rc != FA4D_OK:
+        _raise(lib, rc, "fa4d_mask_blocks")
+    strides = (Hm * nqb * nkb if Bm > 1 else 0, nqb * nkb if Hm > 1 else 0)
+    return BlockMap(blocks, strides)
+
+
+def _set_blocks(a, mask: Optional[torch.Tensor], blocks: Optional[BlockMap]) -> None:
+    if mask is not None and blocks is not None:
+        a.mask_blocks = blocks.blocks.data_ptr()
+        a.mask_blocks_stride = (ctypes.c_int64 * 2)(*blocks.strides)
+    else:
+        a.mask_blocks = None
+
+
 def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
@@ -236,8 +309,9 @@ def forward(
     score: Optional[torch.Tensor],
     scale: float,
     causal: int,
+    blocks: Optional[BlockMap] = None,
 ) -> tuple:
-    """Runs fa4d_fwd.  q: [B, Tq, Hq, D] view, k/v: [B, Tk, Hk, D] views (TMA-friendly).
+    """Runs fa4d_fwd (with the mask's block map when given).  q: [B, Tq, Hq, D] view, k/v: [B, Tk, Hk, D] views (TMA-friendly).
     Returns (O [B, Tq, Hq, D] contiguous, LSE [B, Hq, lse_row_stride(Tq)] fp32)."""
     lib = load_library()
     B, Tq, Hq, D = q.shape
@@ -258,6 +332,7 @@ def forward(
     a.dtype = _dtype_code(q.dtype)
     a.causal = int(causal)
     a.scale = float(scale)
+    _set_blocks(a, mask, blocks)
     with torch.cuda.device(q.device):
         rc = lib.fa4d_fwd(ctypes.byref(a), _stream_ptr(q.device))
     if rc != FA4D_OK:
@@ -277,6 +352,7 @@ def backward(
     scale: float,
     causal: int,
     stages=None,
+    blocks: Optional[BlockMap] = None,
 ) -> tuple:
     """Runs fa4d_bwd on [B, T, H, D] views.  Returns (dQ, dK, dV) contiguous in the
     input dtype, dK/dV summed over the GQA group.
@@ -316,6 +392,7 @@ def backward(
     a.deterministic = 0
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws_bytes
+    _set_blocks(a, mask, blocks)
     with torch.cuda.device(q.device):
         stream = _stream_ptr(q.device)
         if stages is None:

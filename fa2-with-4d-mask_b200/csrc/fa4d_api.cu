@@ -114,6 +114,37 @@ int encode_bthd(CUtensorMap* m, const void* ptr, int B, int T, int H, int D, con
   return FA4D_OK;
 }
 
+// Tensor map over a [B or 1, H or 1, Tq, Tk] mask (1-byte) or score (4-byte) tensor
+// given element strides (b, h, row): dims (Tk, Tq, H', B') with a broadcast (stride
+// 0) dimension given extent 1, box (128 bytes of keys, 128 rows, 1, 1), 128-B swizzle,
+// zero fill out of bounds.  Returns false when the layout cannot be described by a
+// tensor map (unaligned base or strides); the kernels then load from global memory.
+bool encode_bias(CUtensorMap* m, const void* ptr, int B, int H, int Tq, int Tk, const int64_t st[3], int esize) {
+  auto enc = tensor_map_encoder();
+  if (!enc || !ptr || !aligned(ptr, 16)) return false;
+  const int64_t row = st[2] * esize;
+  if (row <= 0 || row % 16 != 0 || row >= (int64_t(1) << 40)) return false;
+  const int64_t ext_h = st[1] == 0 ? 1 : H, ext_b = st[0] == 0 ? 1 : B;
+  int64_t sh = st[1] * esize, sb = st[0] * esize;
+  // A size-1 dimension is never stepped over; give it a stride past the whole tensor.
+  const int64_t span = row * Tq * ext_h * ext_b;
+  if (ext_h == 1) sh = span;
+  if (ext_b == 1) sb = span;
+  if (sh <= 0 || sh % 16 != 0 || sh >= (int64_t(1) << 40) || sb <= 0 || sb % 16 != 0 || sb >= (int64_t(1) << 40))
+    return false;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(Tk), static_cast<cuuint64_t>(Tq), static_cast<cuuint64_t>(ext_h),
+                        static_cast<cuuint64_t>(ext_b)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(row), static_cast<cuuint64_t>(sh), static_cast<cuuint64_t>(sb)};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / esize), 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, esize == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
+                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int nblocks(int T) { return (T + 127) / 128; }
+
 int check_common(int B, int Tq, int Tk, int Hq, int Hk, int D, int dtype, int causal, float scale) {
   if (B < 1 || Tq < 1 || Tk < 1 || Hq < 1 || Hk < 1)
     return fail(FA4D_ERR_INVALID, "sizes must be positive (B=%d Tq=%d Tk=%d Hq=%d Hk=%d)", B, Tq, Tk, Hq, Hk);
@@ -158,6 +189,40 @@ size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D) {
 const char* fa4d_last_error(void) { return g_last_error.c_str(); }
 
 int fa4d_abi_version(void) { return FA4D_ABI_VERSION; }
+
+size_t fa4d_mask_blocks_size(int32_t Bm, int32_t Hm, int32_t Tq, int32_t Tk) {
+  if (Bm < 1 || Hm < 1 || Tq < 1 || Tk < 1) return 0;
+  return static_cast<size_t>(Bm) * Hm * nblocks(Tq) * nblocks(Tk);
+}
+
+int fa4d_mask_blocks(const uint8_t* mask, const int64_t mask_stride[3], int32_t Bm, int32_t Hm, int32_t Tq,
+                     int32_t Tk, uint8_t* blocks, void* stream) {
+  if (!mask || !mask_stride || !blocks) return fail(FA4D_ERR_INVALID, "mask, mask_stride and blocks are required");
+  if (Bm < 1 || Hm < 1 || Tq < 1 || Tk < 1)
+    return fail(FA4D_ERR_INVALID, "sizes must be positive (Bm=%d Hm=%d Tq=%d Tk=%d)", Bm, Hm, Tq, Tk);
+  if (static_cast<int64_t>(Bm) * Hm > 65535 || nblocks(Tq) > 65535)
+    return fail(FA4D_ERR_UNSUPPORTED, "Bm*Hm and ceil(Tq/128) must be <= 65535");
+  if (mask_stride[0] < 0 || mask_stride[1] < 0 || mask_stride[2] < 0)
+    return fail(FA4D_ERR_INVALID, "mask strides must be non-negative");
+  int rc = bind_device_of(mask, "mask");
+  if (rc) return rc;
+  fa4d::MaskBlocksParams p;
+  memset(&p, 0, sizeof(p));
+  p.mask = mask;
+  for (int i = 0; i < 3; ++i) p.stride[i] = mask_stride[i];
+  p.Bm = Bm;
+  p.Hm = Hm;
+  p.Tq = Tq;
+  p.Tk = Tk;
+  p.nqb = nblocks(Tq);
+  p.nkb = nblocks(Tk);
+  p.vec = aligned(mask, 16) && Tk % 16 == 0 && mask_stride[0] % 16 == 0 && mask_stride[1] % 16 == 0 &&
+          mask_stride[2] % 16 == 0;
+  p.blocks = blocks;
+  cudaError_t e = fa4d::launch_mask_blocks(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "mask block pass launch failed: %s", cudaGetErrorString(e));
+  return ok();
+}
 
 int fa4d_check_exp2(float* out, int32_t n, float lo, float hi, void* stream) {
   if (!out || n < 2) return fail(FA4D_ERR_INVALID, "out must be a device buffer of n >= 2 floats");
@@ -222,6 +287,16 @@ int fa4d_fwd(const fa4d_fwd_args* a, void* stream) {
                 a->score_stride[2] % 4 == 0;
   p.status = status_word_ptr();
   if (!p.status) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
+  p.nkb = nblocks(a->Tk);
+  if (a->mask && a->mask_blocks) {
+    p.mask_blocks = a->mask_blocks;
+    p.mb_stride[0] = a->mask_blocks_stride[0];
+    p.mb_stride[1] = a->mask_blocks_stride[1];
+  }
+  if (a->mask || a->score) {
+    p.bias_tma = (!a->mask || encode_bias(&p.tm_mask, a->mask, a->B, a->Hq, a->Tq, a->Tk, a->mask_stride, 1)) &&
+                 (!a->score || encode_bias(&p.tm_score, a->score, a->B, a->Hq, a->Tq, a->Tk, a->score_stride, 4));
+  }
   cudaError_t e = fa4d::launch_fwd(p, a->D, bf16, a->mask != nullptr, a->score != nullptr,
                                    static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "forward launch failed: %s", cudaGetErrorString(e));
@@ -301,6 +376,12 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   p.scale_log2 = static_cast<float>(static_cast<double>(a->scale) * 1.4426950408889634);
   p.scale = a->scale;
   p.status = status;
+  p.nkb = nblocks(a->Tk);
+  if (a->mask && a->mask_blocks) {
+    p.mask_blocks = a->mask_blocks;
+    p.mb_stride[0] = a->mask_blocks_stride[0];
+    p.mb_stride[1] = a->mask_blocks_stride[1];
+  }
 
   fa4d::PrepParams& pp = plan->prep;
   pp.o = a->o;

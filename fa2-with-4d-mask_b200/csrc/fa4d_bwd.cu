@@ -107,6 +107,36 @@ __device__ __forceinline__ void issue_dq(uint32_t tD, uint32_t sK, uint32_t sDS)
            kk > 0 ? 1u : 0u);
 }
 
+// The (query head g of the GQA group, 64-row query tile) pairs a key tile visits, in
+// order g-major, minus those whose 128 x 128 block the mask's block map marks EMPTY
+// (block-sparse skipping; the reference visits every pair, python/fa2.py:242).
+template <bool kMask>
+struct QTiles {
+  const uint8_t* map;  // block map at (head 0 of the group, query block 0, this key block), or null
+  int64_t head_stride, row_stride;
+  int nq, first_qt, N;  // N = G * nq pairs before skipping
+  int lin;              // current pair g * nq + qi; lin >= N past the end
+  __device__ __forceinline__ int g() const { return lin / nq; }
+  __device__ __forceinline__ int q0() const { return (first_qt + lin % nq) * 64; }
+  // 0: skip; 1: visit and apply the mask; 2: visit, the mask keeps every pair.
+  __device__ __forceinline__ int state() const {
+    if (!kMask) return 2;
+    if (!map) return 1;
+    const int gg = lin / nq;
+    const int v = __ldg(map + gg * head_stride + ((first_qt + lin - gg * nq) >> 1) * row_stride);
+    return v == 0 ? 0 : (v == 2 ? 2 : 1);
+  }
+  __device__ __forceinline__ bool valid() const { return lin < N; }
+  __device__ __forceinline__ void skip_empty() {
+    if (kMask && map)
+      while (lin < N && state() == 0) ++lin;
+  }
+  __device__ __forceinline__ void advance() {
+    ++lin;
+    skip_empty();
+  }
+};
+
 template <int D, bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_constant__ BwdParams p) {
   using L = BwdLayout<D>;
@@ -146,7 +176,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   }
   const int num_qt_total = (p.Tq + 63) / 64;
   const int nq = max(0, num_qt_total - first_qt);
-  const int N = G * nq;
+  QTiles<kMask> first;
+  first.map = (kMask && p.mask_blocks)
+                  ? p.mask_blocks + b * p.mb_stride[0] + static_cast<int64_t>(hk) * G * p.mb_stride[1] + blockIdx.x
+                  : nullptr;
+  first.head_stride = p.mb_stride[1];
+  first.row_stride = p.nkb;
+  first.nq = max(nq, 1);
+  first.first_qt = first_qt;
+  first.N = G * nq;
+  first.lin = 0;
+  first.skip_empty();
+  const bool any_work = first.valid();
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -187,7 +228,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     regs_dec<kRegsCtl>();
     if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && N > 0) {
+    if (lane == 0 && any_work) {
       prefetch_tmap(&p.tm_q);
       prefetch_tmap(&p.tm_do);
       prefetch_tmap(&p.tm_k);
@@ -199,11 +240,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         tma_load_4d(smem + L::kV + c * 16384, &p.tm_v, kv_full, c * 64, k0, hk, b);
       }
       int issued = 0;
-      for (int it = 0; it < N; ++it) {
+      QTiles<kMask> cur = first;
+      for (int it = 0; cur.valid(); ++it, cur.advance()) {
         const int qs = it % kQStages;
-        const int g = it / nq;
-        const int h = hk * G + g;
-        const int q0 = (first_qt + it % nq) * 64;
+        const int h = hk * G + cur.g();
+        const int q0 = cur.q0();
         if (!mbar_wait(&q_empty[qs], ((it / kQStages) & 1) ^ 1, abort_flag)) break;
         mbar_arrive_expect_tx(&q_full[qs], 2 * L::kQT + 512);
 #pragma unroll
@@ -228,7 +269,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     // Runs two tiles ahead: S and dP of tile it+2 are issued while the P/dS
     // warpgroups work on tiles it and it+1.  The whole warp runs the loop (waits
     // included); each group of MMAs and its commits is issued by one elected lane.
-    if (N > 0) {
+    if (any_work) {
       const uint32_t sK = smem_u32(smem + L::kK);
       const uint32_t sV = smem_u32(smem + L::kV);
       const uint32_t sQ = smem_u32(smem + L::kQ);
@@ -238,7 +279,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
       };
       bool ok = wait(kv_full, 0);
-      for (int j = 0; ok && j < min(2, N); ++j) {
+      // `ahead` walks the pair list two entries in front of `it`; n_known counts the
+      // pairs whose S and dP have been issued.
+      QTiles<kMask> ahead = first;
+      int n_known = 0;
+      for (int j = 0; ok && j < 2 && ahead.valid(); ++j, ahead.advance(), ++n_known) {
         ok = wait(&q_full[j], 0);
         if (!ok) break;
         tc_fence_after();
@@ -250,7 +295,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         }
         __syncwarp();
       }
-      for (int it = 0; ok && it < N; ++it) {
+      for (int it = 0; ok && it < n_known; ++it) {
         const int st = it & 1;
         const uint32_t par = (it >> 1) & 1;
         const int qs = it % kQStages;
@@ -272,7 +317,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         }
         __syncwarp();
         const int jn = it + 2;
-        if (jn < N) {
+        if (ahead.valid()) {
+          ahead.advance();
+          ++n_known;
           const int qn = jn % kQStages;
           ok = wait(&q_full[qn], (jn / kQStages) & 1);
           if (!ok) break;
@@ -315,13 +362,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     // selects, so lanes never branch apart before the warp-collective TMEM ops.
     const int kc = min(k, p.Tk - 1);
     bool ok = true;
-    for (int it = wg; it < N; it += 2) {
+    QTiles<kMask> cur = first;
+    if (wg == 1) cur.advance();
+    for (int it = wg; cur.valid(); it += 2, cur.advance(), cur.advance()) {
       const int st = wg;
       const uint32_t par = (it >> 1) & 1;
       const int qs = it % kQStages;
-      const int g = it / nq;
-      const int h = hk * G + g;
-      const int q0 = (first_qt + it % nq) * 64;
+      const int h = hk * G + cur.g();
+      const int q0 = cur.q0();
+      const bool use_mask = kMask && cur.state() == 1;  // warp-uniform
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], par, abort_flag) &&
                                        mbar_wait(&q_full[qs], (it / kQStages) & 1, abort_flag));
       if (!ok) break;
@@ -329,7 +378,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       const uint32_t tS = tmem + lane_base + kColS + 64 * st;
       const bool need_causal = p.causal && (k0 + 127 > q0 + p.causal_off);
       const bool need_bounds = (q0 + 64 > p.Tq) || (k0 + 128 > p.Tk);
-      const bool fast = !kMask && !kScore && !need_causal && !need_bounds;  // warp-uniform
+      const bool fast = !use_mask && !kScore && !need_causal && !need_bounds;  // warp-uniform
       const float4* l4 = reinterpret_cast<const float4*>(sLSE + qs * 64);
       const float* score_col = nullptr;
       const uint8_t* mask_col = nullptr;
@@ -362,7 +411,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             if (need_causal) keep = keep && (k <= q + p.causal_off);
             float x = __uint_as_float(sr[i]);
             if constexpr (kScore) x += __ldg(score_col + qc * p.score_stride[2]);
-            if constexpr (kMask) keep = keep && (__ldg(mask_col + qc * p.mask_stride[2]) != 0);
+            if (use_mask) keep = keep && (__ldg(mask_col + qc * p.mask_stride[2]) != 0);
             const float e = ex2(fmaf(x, p.scale_log2, -sLSE[qs * 64 + c]));
             pv[c] = keep ? e : 0.f;
           }
@@ -419,7 +468,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       dst_row = reinterpret_cast<uint16_t*>(wg == 0 ? p.dv : p.dk) + b * st3[0] + static_cast<int64_t>(k) * st3[1] +
                 hk * st3[2];
     }
-    if (N > 0 && ok) {
+    if (any_work && ok) {
       ok = __all_sync(0xffffffffu, mbar_wait(dkv_full, 0, abort_flag));
       tc_fence_after();
       const uint32_t tA = tmem + lane_base + (wg == 0 ? kColDV : kColDK);
@@ -439,7 +488,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
           for (int u = 0; u < 4; ++u) dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         }
       }
-    } else if (k_valid && N == 0) {
+    } else if (k_valid && !any_work) {
 #pragma unroll
       for (int u = 0; u < D / 8; ++u) reinterpret_cast<uint4*>(dst_row)[u] = make_uint4(0, 0, 0, 0);
     }
@@ -454,11 +503,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     const bool d_valid = (D == 128) || (lane < 16);
     const bool leader = (warp == 12 && lane == 0);
     float* stage = reinterpret_cast<float*>(smem + L::kDQs);  // [64 queries][D]
-    for (int it = 0; it < N; ++it) {
+    QTiles<kMask> cur = first;
+    for (int it = 0; cur.valid(); ++it, cur.advance()) {
       const int st = it & 1;
-      const int g = it / nq;
-      const int h = hk * G + g;
-      const int q0 = (first_qt + it % nq) * 64;
+      const int h = hk * G + cur.g();
+      const int q0 = cur.q0();
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&dq_full[st], (it >> 1) & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();

@@ -10,11 +10,18 @@
 // as softmax over an all -inf row does in the oracle.
 //
 // CTA = 2 query slots x 128 rows of one (batch, query head); 384 threads:
-//   warp 0      TMA producer (Q once, then K/V tiles into a 2-stage ring each)
-//   warp 1      tcgen05.mma issuer (one thread)
-//   warp 2      TMEM allocator
+//   warp 0      TMA producer (Q once, then K/V tiles into a 1- or 2-stage ring each)
+//   warp 1      tcgen05.mma issuer (whole warp, one elected lane issues)
+//   warp 2      TMEM allocator, then mask/score staging for query slot 1
+//   warp 3      mask/score staging for query slot 0
 //   warps 4-7   softmax + epilogue for query slot 0 (one thread per row)
 //   warps 8-11  softmax + epilogue for query slot 1
+// The key tiles visited are the union of the two slots' tiles: those below the
+// causal / key-length limit minus the blocks the mask's block map marks EMPTY
+// (block-sparse skipping; the reference visits every tile, python/fa2.py:95).
+// Mask tiles (PARTIAL blocks only) and score chunks reach shared memory by TMA
+// through a per-slot ring, so the softmax threads read them with 16-B shared loads
+// instead of waiting on global memory.
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
 // P (16-bit) overwrites the first 64 columns of S and feeds the PV MMA from TMEM.
 #include <cfloat>
@@ -37,19 +44,29 @@ constexpr float kNegInf = -INFINITY;
 // O is only rescaled when the running max grows by more than this (log2 units);
 // in between, P = exp2(s - stale max) stays <= 2^8, exact after the final 1/l.
 constexpr float kRescaleThreshold = 8.0f;
+// One staged mask tile (128 rows x 128 keys, 1 B) or score chunk (128 rows x 32
+// keys, fp32): 128 B per row, 128-B swizzled.
+constexpr int kRingEntry = 16384;
 
-template <int D>
+template <int D, bool kMask, bool kScore>
 struct FwdLayout {
   static constexpr int kTile = 128 * D * 2;  // one 128-row tile of 16-bit elements
-  static constexpr int kQ = 0;               // 2 query slots
-  static constexpr int kK = kQ + 2 * kTile;  // 2 stages
-  static constexpr int kV = kK + 2 * kTile;  // 2 stages
-  static constexpr int kBar = kV + 2 * kTile;
-  static constexpr int kNumBars = 16;
+  // With a score at D=128 the staging rings take the room of one K/V stage.
+  static constexpr int kKVStages = (kScore && D == 128) ? 1 : 2;
+  static constexpr int kQ = 0;  // 2 query slots
+  static constexpr int kK = kQ + 2 * kTile;
+  static constexpr int kV = kK + kKVStages * kTile;
+  static constexpr int kRing = kV + kKVStages * kTile;  // [2 slots][kRingDepth] entries
+  static constexpr int kRingRoom = 232448 - 1024 - 512 - kRing;
+  static constexpr int kRingFit = kRingRoom / (2 * kRingEntry);
+  static constexpr int kRingDepth = (kMask || kScore) ? (kRingFit < 4 ? kRingFit : 4) : 0;
+  static constexpr int kBar = kRing + 2 * kRingDepth * kRingEntry;
+  static constexpr int kNumBars = 16 + 4 * kRingDepth;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
   static_assert(kAlloc <= 232448, "shared memory beyond the 227 KB per-block limit");
+  static_assert(!(kMask || kScore) || kRingDepth >= 1, "no room for the mask/score staging ring");
 };
 
 // S[slot] = Q[slot] K^T : M=128, N=128, K=D; both operands K-major, 128-B swizzled.
@@ -85,9 +102,49 @@ __device__ __forceinline__ int kv_tiles_for(int qs, int qe, const FwdParams& p) 
   return kv_end > 0 ? (kv_end + 127) / 128 : 0;
 }
 
+// The 128-key tiles one 128-row query slot visits: the tiles below n (key bounds and
+// the causal limit) minus the EMPTY blocks of the mask's block map.
+template <bool kMask>
+struct SlotTiles {
+  const uint8_t* map;  // this slot's row of the block map, or null
+  int n;
+  // 0: skip; 1: visit and apply the mask; 2: visit, the mask keeps every key.
+  __device__ __forceinline__ int state(int kt) const {
+    if (kt >= n) return 0;
+    if (!kMask) return 2;
+    if (!map) return 1;
+    const int v = __ldg(map + kt);
+    return v == 0 ? 0 : (v == 2 ? 2 : 1);
+  }
+  __device__ __forceinline__ int next(int kt) const {
+    while (kt < n && state(kt) == 0) ++kt;
+    return kt;
+  }
+  __device__ __forceinline__ int last() const {
+    int kt = n - 1;
+    while (kt >= 0 && state(kt) == 0) --kt;
+    return kt;
+  }
+};
+
+// First tile at or after kt that either slot visits (n_max if none).
+template <bool kMask>
+__device__ __forceinline__ int next_union(const SlotTiles<kMask>& s0, const SlotTiles<kMask>& s1, int kt, int n_max) {
+  while (kt < n_max && s0.state(kt) == 0 && s1.state(kt) == 0) ++kt;
+  return kt;
+}
+
+// Bit e (e = 0..3) is set when byte e of w is nonzero.
+__device__ __forceinline__ uint32_t nonzero_bits4(uint32_t w) {
+  return ((__vcmpne4(w, 0u) & 0x01010101u) * 0x01020408u) >> 24;
+}
+
 template <int D, bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_constant__ FwdParams p) {
-  using L = FwdLayout<D>;
+  using L = FwdLayout<D, kMask, kScore>;
+  constexpr bool kBias = kMask || kScore;
+  constexpr int R = L::kRingDepth;
+  constexpr int KVS = L::kKVStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
@@ -100,6 +157,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
   uint64_t* p_full = bars + 11;  // [2] per slot
   uint64_t* o_full = bars + 13;  // [2] per slot
   uint64_t* mma_drain = bars + 15;
+  uint64_t* ring_full = bars + 16;          // [2 slots][R]
+  uint64_t* ring_empty = bars + 16 + 2 * R;  // [2 slots][R], 128 arrivals
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -111,14 +170,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
   const int hk = h / (p.Hq / p.Hk);
   const int q0 = qblk * 256;
 
-  int n_slot[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int qs = q0 + 128 * t;
-    const int qe = min(qs + 128, p.Tq);
-    n_slot[t] = kv_tiles_for(qs, qe, p);
+  SlotTiles<kMask> tiles0, tiles1;
+  {
+    const uint8_t* row = nullptr;
+    if (kMask && p.mask_blocks) row = p.mask_blocks + b * p.mb_stride[0] + h * p.mb_stride[1];
+    tiles0.n = kv_tiles_for(q0, min(q0 + 128, p.Tq), p);
+    tiles1.n = kv_tiles_for(q0 + 128, min(q0 + 256, p.Tq), p);
+    tiles0.map = (row && tiles0.n > 0) ? row + static_cast<int64_t>(q0 / 128) * p.nkb : nullptr;
+    tiles1.map = (row && tiles1.n > 0) ? row + static_cast<int64_t>(q0 / 128 + 1) * p.nkb : nullptr;
   }
-  const int n_max = max(n_slot[0], n_slot[1]);
+  const int n_max = max(tiles0.n, tiles1.n);
+  const int kt_first = next_union(tiles0, tiles1, 0, n_max);
+  const bool any_work = kt_first < n_max;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -132,6 +195,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       mbar_init(&o_full[i], 1);
     }
     mbar_init(mma_drain, 1);
+    for (int i = 0; i < 2 * R; ++i) {
+      mbar_init(&ring_full[i], 1);
+      mbar_init(&ring_empty[i], 128);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -150,7 +217,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     regs_dec<kFwdRegsCtl>();
     if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && n_max > 0) {
+    if (lane == 0 && any_work) {
       prefetch_tmap(&p.tm_q);
       prefetch_tmap(&p.tm_k);
       prefetch_tmap(&p.tm_v);
@@ -163,29 +230,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
           tma_load_4d(sQ + t * L::kTile + c * 16384, &p.tm_q, q_full, c * 64, q0 + 128 * t, h, b);
-      int issued = 0;
-      for (int j = 0; j < n_max; ++j) {
-        const int s = j & 1;
-        const uint32_t par = ((j >> 1) & 1) ^ 1;
+      int u = 0;              // union entries whose K and V loads were issued
+      bool k_pending = false;  // K of entry u issued, its V not
+      for (int kt = kt_first; kt < n_max; kt = next_union(tiles0, tiles1, kt + 1, n_max), ++u) {
+        const int s = u % KVS;
+        const uint32_t par = ((u / KVS) & 1) ^ 1;
         if (!mbar_wait(&k_empty[s], par, abort_flag)) break;
         mbar_arrive_expect_tx(&k_full[s], L::kTile);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(sK + s * L::kTile + c * 16384, &p.tm_k, &k_full[s], c * 64, j * 128, hk, b);
-        if (!mbar_wait(&v_empty[s], par, abort_flag)) break;
+          tma_load_4d(sK + s * L::kTile + c * 16384, &p.tm_k, &k_full[s], c * 64, kt * 128, hk, b);
+        if (!mbar_wait(&v_empty[s], par, abort_flag)) {
+          k_pending = true;
+          break;
+        }
         mbar_arrive_expect_tx(&v_full[s], L::kTile);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(sV + s * L::kTile + c * 16384, &p.tm_v, &v_full[s], c * 64, j * 128, hk, b);
-        issued = j + 1;
+          tma_load_4d(sV + s * L::kTile + c * 16384, &p.tm_v, &v_full[s], c * 64, kt * 128, hk, b);
       }
       // Abort path only: make sure no copy is still writing shared memory.
       if (*reinterpret_cast<volatile int*>(abort_flag)) {
         mbar_wait_short(q_full, 0);
-        for (int j = max(0, issued - 2); j < issued; ++j) {
-          mbar_wait_short(&k_full[j & 1], (j >> 1) & 1);
-          mbar_wait_short(&v_full[j & 1], (j >> 1) & 1);
+        for (int j = max(0, u - KVS); j < u; ++j) {
+          mbar_wait_short(&k_full[j % KVS], (j / KVS) & 1);
+          mbar_wait_short(&v_full[j % KVS], (j / KVS) & 1);
         }
+        if (k_pending) mbar_wait_short(&k_full[u % KVS], (u / KVS) & 1);
       }
     }
     __syncwarp();
@@ -193,56 +264,68 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     // ------------------------------------------------------------ MMA issuer
     // The whole warp runs the loop (waits included); each group of MMAs and its
     // commits is issued by one elected lane, keeping the issue state uniform.
-    if (n_max > 0) {
+    if (any_work) {
       const uint32_t sQ = smem_u32(smem + L::kQ);
       const uint32_t sK = smem_u32(smem + L::kK);
       const uint32_t sV = smem_u32(smem + L::kV);
       auto wait = [&](uint64_t* bar, uint32_t parity) {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
       };
+      const int last0 = tiles0.last(), last1 = tiles1.last();
       bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
       if (ok) {
         tc_fence_after();
         if (elect_one()) {
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (n_slot[t] > 0) {
-              issue_qk<D, kBF16>(tmem + 128 * t, sQ + t * L::kTile, sK);
-              tc_commit(&s_full[t]);
-            }
+          if (tiles0.state(kt_first)) {
+            issue_qk<D, kBF16>(tmem, sQ, sK);
+            tc_commit(&s_full[0]);
+          }
+          if (tiles1.state(kt_first)) {
+            issue_qk<D, kBF16>(tmem + 128, sQ + L::kTile, sK);
+            tc_commit(&s_full[1]);
           }
           tc_commit(&k_empty[0]);
         }
         __syncwarp();
       }
-      for (int j = 0; ok && j < n_max; ++j) {
-        const int sv = j & 1;
-        ok = wait(&v_full[sv], (j >> 1) & 1);
+      int cnt0 = 0, cnt1 = 0;  // PV MMAs issued per slot
+      int u = 0;
+      for (int kt = kt_first; ok && kt < n_max; ++u) {
+        const int sv = u % KVS;
+        ok = wait(&v_full[sv], (u / KVS) & 1);
         if (!ok) break;
-        const bool has_next = j + 1 < n_max;
-        const int sk = (j + 1) & 1;
+        const int ktn = next_union(tiles0, tiles1, kt + 1, n_max);
+        const bool has_next = ktn < n_max;
+        const int sk = (u + 1) % KVS;
         if (has_next) {
-          ok = wait(&k_full[sk], ((j + 1) >> 1) & 1);
+          ok = wait(&k_full[sk], ((u + 1) / KVS) & 1);
           if (!ok) break;
         }
         tc_fence_after();
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
-          if (j < n_slot[t]) {
-            ok = wait(&p_full[t], j & 1);
+          const SlotTiles<kMask>& tl = t ? tiles1 : tiles0;
+          int& cnt = t ? cnt1 : cnt0;
+          const bool cur = tl.state(kt) != 0;
+          const bool nxt = has_next && tl.state(ktn) != 0;
+          if (cur) {
+            ok = wait(&p_full[t], cnt & 1);
             if (!ok) break;
             tc_fence_after();
-            if (elect_one()) {
-              issue_pv<D, kBF16>(tmem + 256 + D * t, tmem + 128 * t, sV + sv * L::kTile, j > 0);
-              if (j + 1 < n_slot[t]) {
-                issue_qk<D, kBF16>(tmem + 128 * t, sQ + t * L::kTile, sK + sk * L::kTile);
-                tc_commit(&s_full[t]);
-              } else {
-                tc_commit(&o_full[t]);
-              }
-            }
-            __syncwarp();
           }
+          if (elect_one()) {
+            if (cur) issue_pv<D, kBF16>(tmem + 256 + D * t, tmem + 128 * t, sV + sv * L::kTile, cnt > 0);
+            if (nxt) {
+              // S of the slot's next tile; the PV above (or an earlier one) has
+              // consumed the P that shares these TMEM columns.
+              issue_qk<D, kBF16>(tmem + 128 * t, sQ + t * L::kTile, sK + sk * L::kTile);
+              tc_commit(&s_full[t]);
+            } else if (cur && kt == (t ? last1 : last0)) {
+              tc_commit(&o_full[t]);
+            }
+          }
+          __syncwarp();
+          if (cur) ++cnt;
         }
         if (!ok) break;
         if (elect_one()) {
@@ -250,11 +333,56 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
           if (has_next) tc_commit(&k_empty[sk]);
         }
         __syncwarp();
+        kt = ktn;
       }
       // Every MMA must have completed before TMEM is released.
       if (elect_one()) tc_commit(mma_drain);
       __syncwarp();
       wait(mma_drain, 0);
+    }
+    __syncwarp();
+    } else if (kBias) {
+    // ------------------------------------------------------------ mask / score staging
+    // Warp 3 feeds query slot 0, warp 2 (after the TMEM allocation) slot 1: for each
+    // tile the slot visits, the mask tile (PARTIAL blocks only) and then the four
+    // 32-key score chunks, in that order, into the slot's ring.
+    const int t = warp == 3 ? 0 : 1;
+    const SlotTiles<kMask> tl = t ? tiles1 : tiles0;
+    if (lane == 0 && p.bias_tma && tl.n > 0) {
+      if (kMask) prefetch_tmap(&p.tm_mask);
+      if (kScore) prefetch_tmap(&p.tm_score);
+      const int qs = q0 + 128 * t;
+      const int hm = p.mask_stride[1] ? h : 0, bm = p.mask_stride[0] ? b : 0;
+      const int hs = p.score_stride[1] ? h : 0, bs = p.score_stride[0] ? b : 0;
+      uint8_t* ring = smem + L::kRing + t * R * kRingEntry;
+      uint64_t* full = ring_full + t * R;
+      uint64_t* empty = ring_empty + t * R;
+      int g = 0;
+      bool ok = true;
+      for (int kt = tl.next(0); ok && kt < tl.n; kt = tl.next(kt + 1)) {
+        if (kMask && tl.state(kt) == 1) {
+          const int e = g % R;
+          ok = mbar_wait(&empty[e], ((g / R) & 1) ^ 1, abort_flag);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&full[e], kRingEntry);
+          tma_load_4d(ring + e * kRingEntry, &p.tm_mask, &full[e], kt * 128, qs, hm, bm);
+          ++g;
+        }
+        if (kScore) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            const int e = g % R;
+            ok = mbar_wait(&empty[e], ((g / R) & 1) ^ 1, abort_flag);
+            if (!ok) break;
+            mbar_arrive_expect_tx(&full[e], kRingEntry);
+            tma_load_4d(ring + e * kRingEntry, &p.tm_score, &full[e], kt * 128 + 32 * c, qs, hs, bs);
+            ++g;
+          }
+        }
+      }
+      if (*reinterpret_cast<volatile int*>(abort_flag)) {
+        for (int j = max(0, g - R); j < g; ++j) mbar_wait_short(&full[j % R], (j / R) & 1);
+      }
     }
     __syncwarp();
     }
@@ -269,22 +397,47 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_base + 128 * t;
     const uint32_t tO = tmem + lane_base + 256 + D * t;
-    const int n = n_slot[t];
+    const SlotTiles<kMask> tl = t ? tiles1 : tiles0;
 
-    // Rows past Tq read row Tq-1 (always in bounds) and are never stored: the loads
-    // below carry no per-lane branch, so the warp stays converged for the TMEM ops.
+    // Global-memory fallback (bias_tma == 0): rows past Tq read row Tq-1 (always in
+    // bounds) and are never stored, so the loads carry no per-lane branch and the
+    // warp stays converged for the TMEM ops.
     const int64_t qc = min(q, p.Tq - 1);
     const float* score_row = nullptr;
     const uint8_t* mask_row = nullptr;
     if (kScore) score_row = p.score + b * p.score_stride[0] + h * p.score_stride[1] + qc * p.score_stride[2];
     if (kMask) mask_row = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + qc * p.mask_stride[2];
+    // Staged path: this thread's row of each ring entry (128 B, 16-B units swizzled by row % 8).
+    const uint8_t* ring_row = smem + L::kRing + t * R * kRingEntry + row * 128;
+    uint64_t* full = ring_full + t * R;
+    uint64_t* empty = ring_empty + t * R;
+    const int sw = row & 7;
+    int g = 0;
 
     float m_run = kNegInf;
     float l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
+    int i = 0;  // tiles processed by this slot
+    for (int kt = tl.next(0); kt < tl.n; kt = tl.next(kt + 1), ++i) {
+      const bool use_mask = kMask && tl.state(kt) == 1;  // warp-uniform
+      uint32_t mbits[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      if (kMask && use_mask && p.bias_tma) {
+        const int e = g % R;
+        ok = __all_sync(0xffffffffu, mbar_wait(&full[e], (g / R) & 1, abort_flag));
+        if (!ok) break;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 w0 = *reinterpret_cast<const uint4*>(ring_row + e * kRingEntry + (((2 * c) ^ sw) << 4));
+          const uint4 w1 = *reinterpret_cast<const uint4*>(ring_row + e * kRingEntry + (((2 * c + 1) ^ sw) << 4));
+          mbits[c] = nonzero_bits4(w0.x) | (nonzero_bits4(w0.y) << 4) | (nonzero_bits4(w0.z) << 8) |
+                     (nonzero_bits4(w0.w) << 12) | (nonzero_bits4(w1.x) << 16) | (nonzero_bits4(w1.y) << 20) |
+                     (nonzero_bits4(w1.z) << 24) | (nonzero_bits4(w1.w) << 28);
+        }
+        mbar_arrive(&empty[e]);
+        ++g;
+      }
       // Warp-uniform outcome: the tcgen05.ld below is warp-collective.
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], i & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
       uint32_t sr[128];
@@ -292,62 +445,82 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       for (int c = 0; c < 4; ++c) tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * c]));
       tmem_wait_ld();
 
-      const int kbase = j * 128;
+      const int kbase = kt * 128;
       const bool need_bounds = kbase + 128 > p.Tk;
       const bool need_causal = p.causal && (kbase + 127 > qs + p.causal_off);
-      // Interior tile (warp-uniform): nothing to add or mask, so the row max is taken
+      // Interior tile with nothing to add or mask (warp-uniform): the row max is taken
       // on raw S and the scale is folded into the exponent's FMA below.
-      const bool fast = !kMask && !kScore && !need_bounds && !need_causal && p.scale_log2 > 0.f;
+      const bool fast = !kScore && !use_mask && !need_bounds && !need_causal && p.scale_log2 > 0.f;
       float m_tile = kNegInf;
       if (fast) {
         float m4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
 #pragma unroll
-        for (int i = 0; i < 128; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(sr[i]));
+        for (int k = 0; k < 128; ++k) m4[k & 3] = fmaxf(m4[k & 3], __uint_as_float(sr[k]));
         m_tile = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
       } else {
 #pragma unroll
-      for (int c4 = 0; c4 < 32; ++c4) {
-        const int k4 = kbase + 4 * c4;
-        float add[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t keep_bits = 0xFu;
-        // k4 is the same for every lane, so these branches are warp-uniform.
-        if constexpr (kScore) {
-          if (p.score_vec && k4 + 3 < p.Tk) {
-            const float4 v = __ldg(reinterpret_cast<const float4*>(score_row + k4));
-            add[0] = v.x; add[1] = v.y; add[2] = v.z; add[3] = v.w;
-          } else {
+        for (int c = 0; c < 4; ++c) {
+          const int kc = kbase + 32 * c;
+          uint32_t mb = mbits[c];
+          if (kMask && use_mask && !p.bias_tma) {
+            mb = 0u;
+            // kc is the same for every lane, so these branches are warp-uniform.
+            if (p.mask_vec && kc + 31 < p.Tk) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (k4 + e < p.Tk) add[e] = __ldg(score_row + k4 + e);
+              for (int w = 0; w < 8; ++w)
+                mb |= nonzero_bits4(__ldg(reinterpret_cast<const unsigned int*>(mask_row + kc) + w)) << (4 * w);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (kc + e < p.Tk) mb |= (__ldg(mask_row + kc + e) != 0 ? 1u : 0u) << e;
+            }
+          }
+          float add[32];
+          if constexpr (kScore) {
+            if (p.bias_tma) {
+              const int e = g % R;
+              ok = __all_sync(0xffffffffu, mbar_wait(&full[e], (g / R) & 1, abort_flag));
+              if (!ok) break;
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const float4 v = *reinterpret_cast<const float4*>(ring_row + e * kRingEntry + ((u ^ sw) << 4));
+                add[4 * u] = v.x;
+                add[4 * u + 1] = v.y;
+                add[4 * u + 2] = v.z;
+                add[4 * u + 3] = v.w;
+              }
+              mbar_arrive(&empty[e]);
+              ++g;
+            } else if (p.score_vec && kc + 31 < p.Tk) {
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(score_row + kc) + u);
+                add[4 * u] = v.x;
+                add[4 * u + 1] = v.y;
+                add[4 * u + 2] = v.z;
+                add[4 * u + 3] = v.w;
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) add[e] = (kc + e < p.Tk) ? __ldg(score_row + kc + e) : 0.f;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int k = kc + e;
+            float x = __uint_as_float(sr[32 * c + e]);
+            if constexpr (kScore) x += add[e];
+            x *= p.scale_log2;
+            bool keep = true;
+            if constexpr (kMask) keep = (mb >> e) & 1u;
+            if (need_bounds) keep = keep && (k < p.Tk);
+            if (need_causal) keep = keep && (k <= q + p.causal_off);
+            x = keep ? x : kNegInf;
+            sr[32 * c + e] = __float_as_uint(x);
+            m_tile = fmaxf(m_tile, x);
           }
         }
-        if constexpr (kMask) {
-          keep_bits = 0u;
-          if (p.mask_vec && k4 + 3 < p.Tk) {
-            const uint32_t w = __ldg(reinterpret_cast<const unsigned int*>(mask_row + k4));
-#pragma unroll
-            for (int e = 0; e < 4; ++e) keep_bits |= (((w >> (8 * e)) & 0xFFu) != 0u ? 1u : 0u) << e;
-          } else {
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (k4 + e < p.Tk) keep_bits |= (__ldg(mask_row + k4 + e) != 0 ? 1u : 0u) << e;
-          }
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i = 4 * c4 + e;
-          const int k = k4 + e;
-          float x = __uint_as_float(sr[i]);
-          if constexpr (kScore) x += add[e];
-          x *= p.scale_log2;
-          bool keep = (keep_bits >> e) & 1u;
-          if (need_bounds) keep = keep && (k < p.Tk);
-          if (need_causal) keep = keep && (k <= q + p.causal_off);
-          x = keep ? x : kNegInf;
-          sr[i] = __float_as_uint(x);
-          m_tile = fmaxf(m_tile, x);
-        }
-      }
+        if (!ok) break;
       }
 
       // Online softmax with lazy rescaling of O.
@@ -359,15 +532,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         l_run *= alpha;
         m_run = m_new;
       }
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // PV of tile j-1 has completed (S of tile j was issued after it).
+      if (i > 0 && __any_sync(0xffffffffu, need)) {
+        // The slot's previous PV has completed (this tile's S was issued after it).
 #pragma unroll
         for (int c = 0; c < D / 16; ++c) {
           uint32_t o[16];
           tmem_ld16(tO + 16 * c, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          for (int k = 0; k < 16; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
           tmem_st16(tO + 16 * c, o);
         }
       }
@@ -380,13 +553,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float a0 = fmaf(__uint_as_float(sr[32 * c + 2 * i]), p.scale_log2, -m_use);
-            const float a1 = fmaf(__uint_as_float(sr[32 * c + 2 * i + 1]), p.scale_log2, -m_use);
+          for (int k = 0; k < 16; ++k) {
+            const float a0 = fmaf(__uint_as_float(sr[32 * c + 2 * k]), p.scale_log2, -m_use);
+            const float a1 = fmaf(__uint_as_float(sr[32 * c + 2 * k + 1]), p.scale_log2, -m_use);
             const float p0 = ex2(a0);
-            const float p1 = (i & 1) ? ex2_poly(a1) : ex2(a1);
+            const float p1 = (k & 1) ? ex2_poly(a1) : ex2(a1);
             rowsum += p0 + p1;
-            pk[i] = pack2<kBF16>(p0, p1);
+            pk[k] = pack2<kBF16>(p0, p1);
           }
           tmem_st16(tS + 16 * c, pk);
         }
@@ -395,11 +568,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float p0 = ex2(__uint_as_float(sr[32 * c + 2 * i]) - m_use);
-            const float p1 = ex2(__uint_as_float(sr[32 * c + 2 * i + 1]) - m_use);
+          for (int k = 0; k < 16; ++k) {
+            const float p0 = ex2(__uint_as_float(sr[32 * c + 2 * k]) - m_use);
+            const float p1 = ex2(__uint_as_float(sr[32 * c + 2 * k + 1]) - m_use);
             rowsum += p0 + p1;
-            pk[i] = pack2<kBF16>(p0, p1);
+            pk[k] = pack2<kBF16>(p0, p1);
           }
           tmem_st16(tS + 16 * c, pk);
         }
@@ -410,13 +583,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       mbar_arrive(&p_full[t]);
     }
 
-    // Epilogue: O / l and LSE.
+    // Epilogue: O / l and LSE.  A slot that visits no tile (every block EMPTY) has
+    // only fully masked rows: O = NaN and LSE = -inf, as softmax over -inf gives.
     using Elem = uint16_t;
     Elem* o_row = nullptr;
     if (q_valid)
       o_row = reinterpret_cast<Elem*>(p.o) + b * p.o_stride[0] + static_cast<int64_t>(q) * p.o_stride[1] +
               h * p.o_stride[2];
-    if (n > 0 && ok) {
+    if (i > 0 && ok) {
       ok = __all_sync(0xffffffffu, mbar_wait(&o_full[t], 0, abort_flag));
       tc_fence_after();
       const float inv_l = 1.f / l_run;  // l == 0 (no valid key) -> inf -> O = NaN like the oracle
@@ -428,8 +602,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         if (q_valid) {
           uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pk[i] = pack2<kBF16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+          for (int k = 0; k < 16; ++k)
+            pk[k] = pack2<kBF16>(__uint_as_float(o[2 * k]) * inv_l, __uint_as_float(o[2 * k + 1]) * inv_l);
           uint4* dst = reinterpret_cast<uint4*>(o_row + 32 * c);
 #pragma unroll
           for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
@@ -458,7 +632,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
 
 template <int D, bool kBF16, bool kMask, bool kScore>
 cudaError_t launch_fwd_t(const FwdParams& p, cudaStream_t s) {
-  using L = FwdLayout<D>;
+  using L = FwdLayout<D, kMask, kScore>;
   auto kern = fwd_kernel<D, kBF16, kMask, kScore>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return e;

@@ -29,6 +29,17 @@ struct FwdParams {
   int32_t mask_vec;         // 1: rows are 4-B aligned, 32-bit loads allowed
   int32_t score_vec;        // 1: rows are 16-B aligned, 128-bit loads allowed
   int* status;              // device status word (bounded-wait timeouts)
+  // Block map (fa4d_mask_blocks) or null: byte b*mb_stride[0] + h*mb_stride[1] +
+  // qb*nkb + kb holds the state of the 128 x 128 block (qb, kb).
+  const uint8_t* mask_blocks;
+  int64_t mb_stride[2];
+  int32_t nkb;
+  // bias_tma = 1: mask / score tiles are staged in shared memory by TMA through
+  // these maps (dims (Tk, Tq, H or 1, B or 1); mask box (128, 128), score box
+  // (32, 128), 128-B swizzle); 0: the softmax threads load them from global memory.
+  int32_t bias_tma;
+  CUtensorMap tm_mask;
+  CUtensorMap tm_score;
 };
 
 // Backward: one CTA owns 128 keys of one (batch, KV head), loops over every
@@ -57,6 +68,19 @@ struct BwdParams {
   float scale_log2;
   float scale;
   int* status;
+  const uint8_t* mask_blocks;  // as in FwdParams
+  int64_t mb_stride[2];
+  int32_t nkb;
+};
+
+// Block-occupancy pre-pass: blocks[((b * Hm + h) * nqb + qb) * nkb + kb] =
+// 0 (no True element) / 1 (some) / 2 (all in-bounds elements True).
+struct MaskBlocksParams {
+  const uint8_t* mask;
+  int64_t stride[3];  // (b, h, row) elements
+  int32_t Bm, Hm, Tq, Tk, nqb, nkb;
+  int32_t vec;        // 1: base 16-B aligned and row stride a multiple of 16 with Tk % 16 == 0
+  uint8_t* blocks;
 };
 
 // Row dot products Delta = rowsum(O * dO) and zeroing of the dQ accumulator.
@@ -85,6 +109,7 @@ cudaError_t launch_fwd(const FwdParams& p, int D, bool bf16, bool has_mask, bool
 cudaError_t launch_bwd(const BwdParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);
 cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s);
+cudaError_t launch_mask_blocks(const MaskBlocksParams& p, cudaStream_t s);
 cudaError_t launch_exp2_check(float* out, int n, float lo, float hi, cudaStream_t s);
 
 }  // namespace fa4d

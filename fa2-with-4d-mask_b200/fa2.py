@@ -15,10 +15,17 @@ input dtype (the reference returns dQ in fp32 and lets autograd cast it,
 python/fa2.py:556).  ``use_atomic_backward`` is accepted for compatibility; both
 values run the same backward, in which dK/dV are summed over the GQA group inside
 the kernel and dQ is accumulated in fp32.
+
+A bool mask is first reduced to a block map (``fa4d_mask_blocks``: each 128 x 128
+block EMPTY, PARTIAL or FULL) that the forward and backward kernels use to skip
+EMPTY blocks and the mask loads of FULL ones.  The map is cached per mask tensor
+(identity of the tensor or of the tensor it views, plus its version counter), so a
+mask shared by every layer of a model is scanned once while it is unchanged.
 """
 
 from __future__ import annotations
 
+import weakref
 from typing import Optional
 
 import torch
@@ -36,6 +43,46 @@ def causal_mode(is_causal: bool, causal_align: str = "top_left") -> int:
         return _CAUSAL_ALIGN[causal_align]
     except KeyError:
         raise ValueError(f"unsupported causal_align: {causal_align}") from None
+
+
+class _BlockMapCache:
+    """Block maps of recently used masks.  An entry is reused only while the tensor
+    it was computed from (or the tensor that view points into) is alive and its
+    version counter is unchanged; any in-place write through autograd-visible
+    views bumps that counter."""
+
+    def __init__(self, capacity: int = 8):
+        self.capacity = capacity
+        self._entries: list = []
+
+    @staticmethod
+    def _key(mask: torch.Tensor) -> tuple:
+        return (mask.data_ptr(), tuple(mask.shape), tuple(mask.stride()), mask.dtype, mask.device, mask._version)
+
+    def get(self, mask: torch.Tensor) -> "_lib.BlockMap":
+        owner = mask._base if mask._base is not None else mask
+        key = self._key(mask)
+        for i, (ref, k, bm) in enumerate(self._entries):
+            if k == key and ref() is owner:
+                if i:
+                    self._entries.insert(0, self._entries.pop(i))
+                return bm
+        bm = _lib.mask_blocks(mask)
+        self._entries.insert(0, (weakref.ref(owner), key, bm))
+        del self._entries[self.capacity :]
+        return bm
+
+    def clear(self) -> None:
+        self._entries.clear()
+
+
+_block_maps = _BlockMapCache()
+
+
+def clear_block_map_cache() -> None:
+    """Drops every cached mask block map (e.g. after writing a mask in place through
+    a path that does not bump its version counter)."""
+    _block_maps.clear()
 
 
 def _fwd_views(Q, K, V, bhsd_input):
@@ -69,8 +116,10 @@ class _flash_attention_with_4d_mask(torch.autograd.Function):
         mode = causal_mode(bool(is_causal), causal_align)
         mask = _lib.prepare_bias(Mask, torch.bool) if Mask is not None else None
         score = _lib.prepare_bias(Score, torch.float32) if Score is not None else None
-        O, LSE = _lib.forward(q, k, v, mask, score, float(scale), mode)
+        blocks = _block_maps.get(mask) if mask is not None else None
+        O, LSE = _lib.forward(q, k, v, mask, score, float(scale), mode, blocks=blocks)
         ctx.save_for_backward(q, k, v, O, LSE, mask, score)
+        ctx.blocks = blocks
         ctx.scale = float(scale)
         ctx.mode = mode
         ctx.use_atomic_backward = use_atomic_backward
@@ -83,7 +132,7 @@ class _flash_attention_with_4d_mask(torch.autograd.Function):
         if ctx.bhsd_input:
             dO = dO.transpose(1, 2)
         dO = _lib.as_tma(dO)
-        dQ, dK, dV = _lib.backward(dO, q, k, v, O, LSE, mask, score, ctx.scale, ctx.mode)
+        dQ, dK, dV = _lib.backward(dO, q, k, v, O, LSE, mask, score, ctx.scale, ctx.mode, blocks=ctx.blocks)
         if ctx.bhsd_input:
             dQ, dK, dV = dQ.transpose(1, 2), dK.transpose(1, 2), dV.transpose(1, 2)
         return dQ, dK, dV, None, None, None, None, None, None, None
@@ -91,4 +140,4 @@ class _flash_attention_with_4d_mask(torch.autograd.Function):
 
 flash_attention_with_4d_mask = _flash_attention_with_4d_mask.apply
 
-__all__ = ["flash_attention_with_4d_mask", "causal_mode"]
+__all__ = ["flash_attention_with_4d_mask", "causal_mode", "clear_block_map_cache"]

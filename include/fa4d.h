@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define FA4D_ABI_VERSION 1
+#define FA4D_ABI_VERSION 2
 
 enum fa4d_dtype { FA4D_BF16 = 0, FA4D_F16 = 1 };
 
@@ -69,6 +69,16 @@ typedef struct fa4d_fwd_args {
   int32_t causal;          /* enum fa4d_causal */
   float scale;             /* softmax scale applied to (QK^T + score) */
   int32_t reserved[3];
+  /* Optional block map of `mask` from fa4d_mask_blocks (NULL = every block is
+   * treated as PARTIAL).  The state of 128 x 128 block (qb, kb) for batch b and
+   * query head h is the byte at
+   *   mask_blocks + b * mask_blocks_stride[0] + h * mask_blocks_stride[1]
+   *               + qb * ceil(Tk / 128) + kb;
+   * a stride is 0 where the mask broadcasts.  EMPTY blocks are skipped (their keys
+   * contribute nothing) and FULL blocks are processed without reading the mask.
+   * Ignored when mask is NULL. */
+  const uint8_t* mask_blocks;
+  int64_t mask_blocks_stride[2];
 } fa4d_fwd_args;
 
 typedef struct fa4d_bwd_args {
@@ -100,6 +110,8 @@ typedef struct fa4d_bwd_args {
   int32_t deterministic;   /* reserved, must be 0 */
   void* workspace;         /* device scratch, >= fa4d_bwd_workspace_size() bytes, 256-B aligned */
   size_t workspace_bytes;
+  const uint8_t* mask_blocks;      /* optional, as in fa4d_fwd_args */
+  int64_t mask_blocks_stride[2];
 } fa4d_bwd_args;
 
 /* Row stride (in floats) of the LSE buffer: Tq rounded up to a multiple of 128.
@@ -153,6 +165,20 @@ int fa4d_bwd_dq_convert(const fa4d_bwd_args* args, void* stream);
  *    order them on one stream. */
 #define FA4D_BWD_NOALLOC_MAX_WORKSPACE ((size_t)64 << 20)
 int fa4d_bwd_noalloc(const fa4d_bwd_args* args, void* stream);
+
+/* Block-occupancy pre-pass over a bool mask [Bm, Hm, Tq, Tk] (element strides
+ * (batch, head, row), key stride 1; Bm / Hm are the mask's own extents, 1 where it
+ * broadcasts).  Writes blocks[((b * Hm + h) * ceil(Tq/128) + qb) * ceil(Tk/128) + kb]
+ * = FA4D_BLOCK_EMPTY / _PARTIAL / _FULL for every 128 x 128 block, judged on the
+ * in-bounds elements only.  The map is what fa4d_fwd_args.mask_blocks and
+ * fa4d_bwd_args.mask_blocks take, and stays valid while the mask is unchanged, so
+ * one map serves the forward and backward of every layer sharing the mask.  No
+ * counterpart in the reference, whose kernels visit every tile
+ * (python/fa2.py:95-124, :242-302). */
+enum fa4d_block_state { FA4D_BLOCK_EMPTY = 0, FA4D_BLOCK_PARTIAL = 1, FA4D_BLOCK_FULL = 2 };
+size_t fa4d_mask_blocks_size(int32_t Bm, int32_t Hm, int32_t Tq, int32_t Tk);
+int fa4d_mask_blocks(const uint8_t* mask, const int64_t mask_stride[3], int32_t Bm, int32_t Hm, int32_t Tq,
+                     int32_t Tk, uint8_t* blocks, void* stream);
 
 /* Message for the last non-zero return on this thread ("" if none). */
 const char* fa4d_last_error(void);

@@ -1,0 +1,44 @@
+"""ORACLE — test infrastructure only: CPU restatement of the block-occupancy map
+the kernels use to skip work under a 4D bool mask.
+
+The reference has no such map: its forward and backward visit every 128-key tile
+and apply the mask per element (python/fa2.py:95-124 and :242-302), so skipping an
+EMPTY block (no True element) must not change any result, and a FULL block (every
+in-bounds element True) must behave exactly like an unmasked one.  This module
+states the classification the GPU pre-pass must reproduce bit for bit, and the
+fraction of blocks the packed-document workload leaves EMPTY.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+BLOCK = 128
+EMPTY, PARTIAL, FULL = 0, 1, 2
+
+
+def mask_blocks_ref(mask, block: int = BLOCK) -> np.ndarray:
+    """mask: [Bm, Hm, Tq, Tk] bool (or integer, nonzero = True).  Returns uint8
+    [Bm, Hm, ceil(Tq/block), ceil(Tk/block)] with EMPTY / PARTIAL / FULL, judged on
+    the in-bounds elements of each block only."""
+    m = np.asarray(mask) != 0
+    Bm, Hm, Tq, Tk = m.shape
+    nqb, nkb = -(-Tq // block), -(-Tk // block)
+    # Padding is False for "any" and True for "all", so it never changes a state.
+    any_pad = np.zeros((Bm, Hm, nqb * block, nkb * block), dtype=bool)
+    all_pad = np.ones_like(any_pad)
+    any_pad[:, :, :Tq, :Tk] = m
+    all_pad[:, :, :Tq, :Tk] = m
+    shape = (Bm, Hm, nqb, block, nkb, block)
+    has_any = any_pad.reshape(shape).any(axis=(3, 5))
+    has_all = all_pad.reshape(shape).all(axis=(3, 5))
+    out = np.full((Bm, Hm, nqb, nkb), PARTIAL, dtype=np.uint8)
+    out[~has_any] = EMPTY
+    out[has_all] = FULL
+    return out
+
+
+def empty_fraction(mask, block: int = BLOCK) -> float:
+    """Share of blocks with no True element."""
+    b = mask_blocks_ref(mask, block)
+    return float((b == EMPTY).mean())

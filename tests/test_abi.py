@@ -38,7 +38,7 @@ def test_library_exports_every_declared_function():
 
 
 def test_abi_version():
-    assert _lib.load_library().fa4d_abi_version() == 1
+    assert _lib.load_library().fa4d_abi_version() == _lib.ABI_VERSION == 2
 
 
 def _c_layout(struct: str, fields):

@@ -1,0 +1,89 @@
+"""CPU: the block-occupancy map — the oracle's classification against a direct
+per-block loop, the sparsity of the packed-document workload, and the reuse rules
+of the op's per-mask map cache (no device work)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import inputs as I
+from oracle.blocks import EMPTY, FULL, PARTIAL, empty_fraction, mask_blocks_ref
+
+impl_fa2 = __import__("fa2_with_4d_mask_b200.fa2", fromlist=["x"])
+
+
+def _loop_blocks(m: np.ndarray, block: int) -> np.ndarray:
+    Bm, Hm, Tq, Tk = m.shape
+    nqb, nkb = -(-Tq // block), -(-Tk // block)
+    out = np.zeros((Bm, Hm, nqb, nkb), dtype=np.uint8)
+    for b in range(Bm):
+        for h in range(Hm):
+            for i in range(nqb):
+                for j in range(nkb):
+                    t = m[b, h, i * block : (i + 1) * block, j * block : (j + 1) * block] != 0
+                    out[b, h, i, j] = FULL if t.all() else (PARTIAL if t.any() else EMPTY)
+    return out
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 5, 7), (2, 3, 130, 257), (1, 2, 256, 384)])
+def test_oracle_matches_direct_loop(shape):
+    rng = np.random.default_rng(sum(shape))
+    # Block-structured values so all three states occur.
+    m = rng.random(shape) < 0.5
+    Bm, Hm, Tq, Tk = shape
+    for i in range(0, Tq, 128):
+        for j in range(0, Tk, 128):
+            pick = rng.integers(3)
+            if pick == 0:
+                m[:, :, i : i + 128, j : j + 128] = False
+            elif pick == 1:
+                m[:, :, i : i + 128, j : j + 128] = True
+    for block in (16, 128):
+        np.testing.assert_array_equal(mask_blocks_ref(m, block), _loop_blocks(m, block))
+
+
+def test_oracle_nonzero_bytes_are_true_and_edges_ignore_padding():
+    m = np.full((1, 1, 200, 130), 7, dtype=np.uint8)
+    b = mask_blocks_ref(m)
+    assert b.shape == (1, 1, 2, 2) and (b == FULL).all()
+    m[0, 0, 199, 129] = 0
+    assert mask_blocks_ref(m)[0, 0, 1, 1] == PARTIAL
+
+
+def test_packed_document_workload_is_mostly_empty_blocks():
+    """The packed-document configuration (B=2, T=4096, documents of 128..1024) leaves
+    close to 90% of the 128 x 128 blocks with no True element."""
+    m = I.packed_doc_mask(2, 4096, min_len=128, max_len=1024, seed=5).numpy()
+    assert empty_fraction(m) > 0.8
+
+
+def test_block_map_cache_reuse_and_invalidation(monkeypatch):
+    calls = []
+
+    def fake(mask):
+        calls.append(mask)
+        return object()
+
+    monkeypatch.setattr(impl_fa2._lib, "mask_blocks", fake)
+    cache = impl_fa2._BlockMapCache(capacity=2)
+    base = torch.zeros(1, 1, 8, 8, dtype=torch.bool)
+    a = cache.get(base)
+    assert cache.get(base) is a and len(calls) == 1
+    # A fresh broadcast view of the same tensor reuses the entry of an identical view.
+    v1 = base.expand(2, 4, 8, 8)
+    m1 = cache.get(v1)
+    assert cache.get(base.expand(2, 4, 8, 8)) is m1 and len(calls) == 2
+    # An in-place write bumps the version counter: the map is recomputed.
+    base[0, 0, 0, 0] = True
+    assert cache.get(base) is not a and len(calls) == 3
+    # Another tensor with equal shape is never mistaken for the first.
+    other = torch.zeros(1, 1, 8, 8, dtype=torch.bool)
+    cache.get(other)
+    assert len(calls) == 4
+    # Capacity bounds the number of entries.
+    assert len(cache._entries) == 2
+    cache.clear()
+    cache.get(other)
+    assert len(calls) == 5
