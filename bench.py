@@ -351,18 +351,18 @@ def extra_measurements(_lib, dev, peaks):
     peak = peaks["bf16_tflops"]
 
     def fb(b, tq, tk, hq, hk, d, causal_mode, mask=None, score=None, iters=5):
-        """(fwd ms, bwd ms) with the mask's block map built once beforehand (as the op
-        caches it per mask); the map pass itself is timed by map_ms()."""
+        """(fwd ms, bwd ms) with the mask prepared once beforehand (block map + packed bits,
+        as the op caches it per mask); the preparation itself is timed by map_ms()."""
         q, k, v, do = (x.transpose(1, 2) for x in _dev_inputs(dev, b, tq, tk, hq, hk, d, seed=3))
         sc = d ** -0.5
-        bm = _lib.mask_blocks(mask) if mask is not None else None
+        bm = _lib.mask_prepare(mask) if mask is not None else None
         tf = time_fn(lambda: _lib.forward(q, k, v, mask, score, sc, causal_mode, blocks=bm), iters)
         o, lse = _lib.forward(q, k, v, mask, score, sc, causal_mode, blocks=bm)
         tb = time_fn(lambda: _lib.backward(do, q, k, v, o, lse, mask, score, sc, causal_mode, blocks=bm), iters)
         return tf, tb
 
     def map_ms(mask):
-        return round(time_fn(lambda: _lib.mask_blocks(mask), 5), 4)
+        return round(time_fn(lambda: _lib.mask_prepare(mask), 5), 4)
 
     tf, tb = fb(B, T, T, HQ, HK, D, _lib.CAUSAL_TOP_LEFT)
     ff, fbf = fwd_flops(B, HQ, T, T, D, True), fwd_bwd_flops(B, HQ, T, T, D, True)
@@ -380,7 +380,7 @@ def extra_measurements(_lib, dev, peaks):
                               "fwd_frac_hbm": round(bytes_fwd / tf / 1e6 / peaks["hbm_gbs"], 4),
                               "fwd_bwd_ms": round(tf + tb, 4),
                               "algorithmic_fwd_bytes": bytes_fwd,
-                              "block_map_ms": map_ms(mask)}
+                              "mask_prepare_ms": map_ms(mask)}
     del score, mask
     # cfg3: packed-document [B,1,T,T] mask
     b3, t3 = 2, 4096
@@ -396,7 +396,7 @@ def extra_measurements(_lib, dev, peaks):
                                "blocks": counts,
                                "fwd_live_block_tflops": round(live * ff / tf / 1e9, 1),
                                "fwd_bwd_live_block_tflops": round(live * fbf / (tf + tb) / 1e9, 1),
-                               "block_map_ms": map_ms(mview)}
+                               "mask_prepare_ms": map_ms(mview)}
     del mask, mview
     # cfg5: MQA, bshd, bottom-right causal, one GPU's shard of 16 (B=2)
     tf, tb = fb(2, 1024, 4096, 64, 1, 64, _lib.CAUSAL_BOTTOM_RIGHT, iters=3)

@@ -48,6 +48,8 @@ EXPORTED_SYMBOLS = (
     "fa4d_check_exp2",
     "fa4d_mask_blocks",
     "fa4d_mask_blocks_size",
+    "fa4d_mask_prepare",
+    "fa4d_mask_prepare_size",
 )
 
 ABI_VERSION = 2
@@ -86,6 +88,7 @@ class FwdArgs(ctypes.Structure):
         ("reserved", ctypes.c_int32 * 3),
         ("mask_blocks", ctypes.c_void_p),
         ("mask_blocks_stride", ctypes.c_int64 * 2),
+        ("mask_prepared", ctypes.c_void_p),
     ]
 
 
@@ -128,6 +131,7 @@ class BwdArgs(ctypes.Structure):
         ("workspace_bytes", ctypes.c_size_t),
         ("mask_blocks", ctypes.c_void_p),
         ("mask_blocks_stride", ctypes.c_int64 * 2),
+        ("mask_prepared", ctypes.c_void_p),
     ]
 
 
@@ -177,6 +181,10 @@ def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
         ctypes.c_void_p,
     ]
     lib.fa4d_mask_blocks.restype = ctypes.c_int
+    lib.fa4d_mask_prepare_size.argtypes = [ctypes.c_int32] * 4
+    lib.fa4d_mask_prepare_size.restype = ctypes.c_size_t
+    lib.fa4d_mask_prepare.argtypes = lib.fa4d_mask_blocks.argtypes
+    lib.fa4d_mask_prepare.restype = ctypes.c_int
     version = lib.fa4d_abi_version()
     if version != ABI_VERSION:
         raise RuntimeError(f"{p}: ABI version {version}, expected {ABI_VERSION}; rebuild with build.py")
@@ -285,12 +293,81 @@ def mask_blocks(mask: torch.Tensor) -> BlockMap:
     return BlockMap(blocks, strides)
 
 
-def _set_blocks(a, mask: Optional[torch.Tensor], blocks: Optional[BlockMap]) -> None:
-    if mask is not None and blocks is not None:
+class PreparedMask:
+    """Output of ``fa4d_mask_prepare`` for one mask: the block map and the mask as
+    packed bits (forward row layout, backward column layout) in one device buffer."""
+
+    __slots__ = ("buffer", "Bm", "Hm", "Tq", "Tk")
+
+    def __init__(self, buffer: torch.Tensor, Bm: int, Hm: int, Tq: int, Tk: int):
+        self.buffer = buffer
+        self.Bm, self.Hm, self.Tq, self.Tk = Bm, Hm, Tq, Tk
+
+    @property
+    def nqb(self) -> int:
+        return -(-self.Tq // BLOCK)
+
+    @property
+    def nkb(self) -> int:
+        return -(-self.Tk // BLOCK)
+
+    def _offsets(self) -> tuple:
+        a = lambda x: -(-x // 256) * 256
+        bh = self.Bm * self.Hm
+        nqt = -(-self.Tq // 64)
+        row = a(bh * self.nqb * self.nkb)
+        col = row + a(bh * self.nkb * self.Tq * 16)
+        return row, col, nqt
+
+    def blocks(self) -> torch.Tensor:
+        """Block map view [Bm, Hm, nqb, nkb] (uint8)."""
+        n = self.Bm * self.Hm * self.nqb * self.nkb
+        return self.buffer[:n].view(self.Bm, self.Hm, self.nqb, self.nkb)
+
+    def row_bits(self) -> torch.Tensor:
+        """Row bits view [Bm, Hm, nkb, Tq, 4] (int32 words)."""
+        row, _, _ = self._offsets()
+        n = self.Bm * self.Hm * self.nkb * self.Tq * 16
+        return self.buffer[row : row + n].view(torch.int32).view(self.Bm, self.Hm, self.nkb, self.Tq, 4)
+
+    def col_bits(self) -> torch.Tensor:
+        """Column bits view [Bm, Hm, nqt, Tk, 2] (int32 words)."""
+        _, col, nqt = self._offsets()
+        n = self.Bm * self.Hm * nqt * self.Tk * 8
+        return self.buffer[col : col + n].view(torch.int32).view(self.Bm, self.Hm, nqt, self.Tk, 2)
+
+
+def mask_prepare(mask: torch.Tensor) -> PreparedMask:
+    """Runs ``fa4d_mask_prepare`` over a [B|1, H|1, Tq, Tk] bool/uint8 mask view with
+    unit key stride (broadcast dimensions may have stride 0)."""
+    lib = load_library()
+    if mask.dim() != 4 or mask.element_size() != 1 or mask.stride(3) != 1:
+        raise ValueError("mask must be a 4D bool/uint8 tensor with unit key stride")
+    Bf, Hf, Tq, Tk = mask.shape
+    sb, sh, sr = _bias_strides(mask)
+    Bm = Bf if sb != 0 else 1
+    Hm = Hf if sh != 0 else 1
+    nbytes = int(lib.fa4d_mask_prepare_size(Bm, Hm, Tq, Tk))
+    buf = torch.empty((nbytes,), dtype=torch.uint8, device=mask.device)
+    st = (ctypes.c_int64 * 3)(sb, sh, sr)
+    with torch.cuda.device(mask.device):
+        rc = lib.fa4d_mask_prepare(mask.data_ptr(), st, Bm, Hm, Tq, Tk, buf.data_ptr(), _stream_ptr(mask.device))
+    if rc != FA4D_OK:
+        _raise(lib, rc, "fa4d_mask_prepare")
+    return PreparedMask(buf, Bm, Hm, Tq, Tk)
+
+
+def _set_blocks(a, mask: Optional[torch.Tensor], blocks) -> None:
+    """Attaches a BlockMap (map only) or a PreparedMask (map + bits) to the args."""
+    a.mask_blocks = None
+    a.mask_prepared = None
+    if mask is None or blocks is None:
+        return
+    if isinstance(blocks, PreparedMask):
+        a.mask_prepared = blocks.buffer.data_ptr()
+    else:
         a.mask_blocks = blocks.blocks.data_ptr()
         a.mask_blocks_stride = (ctypes.c_int64 * 2)(*blocks.strides)
-    else:
-        a.mask_blocks = None
 
 
 def _stream_ptr(device: torch.device) -> int:
@@ -309,9 +386,9 @@ def forward(
     score: Optional[torch.Tensor],
     scale: float,
     causal: int,
-    blocks: Optional[BlockMap] = None,
+    blocks=None,
 ) -> tuple:
-    """Runs fa4d_fwd (with the mask's block map when given).  q: [B, Tq, Hq, D] view, k/v: [B, Tk, Hk, D] views (TMA-friendly).
+    """Runs fa4d_fwd (with the mask's BlockMap or PreparedMask when given).  q: [B, Tq, Hq, D] view, k/v: [B, Tk, Hk, D] views (TMA-friendly).
     Returns (O [B, Tq, Hq, D] contiguous, LSE [B, Hq, lse_row_stride(Tq)] fp32)."""
     lib = load_library()
     B, Tq, Hq, D = q.shape
@@ -352,7 +429,7 @@ def backward(
     scale: float,
     causal: int,
     stages=None,
-    blocks: Optional[BlockMap] = None,
+    blocks=None,
 ) -> tuple:
     """Runs fa4d_bwd on [B, T, H, D] views.  Returns (dQ, dK, dV) contiguous in the
     input dtype, dK/dV summed over the GQA group.

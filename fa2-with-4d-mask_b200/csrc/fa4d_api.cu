@@ -145,6 +145,37 @@ bool encode_bias(CUtensorMap* m, const void* ptr, int B, int H, int Tq, int Tk, 
 
 int nblocks(int T) { return (T + 127) / 128; }
 
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Byte offsets inside a prepared-mask buffer: [block map][row bits][column bits].
+struct PrepLayout {
+  size_t blocks, row_bits, col_bits, total;
+  int nqb, nkb, nqt;
+};
+PrepLayout prep_layout(int Bm, int Hm, int Tq, int Tk) {
+  PrepLayout L;
+  L.nqb = nblocks(Tq);
+  L.nkb = nblocks(Tk);
+  L.nqt = (Tq + 63) / 64;
+  const size_t bh = static_cast<size_t>(Bm) * Hm;
+  L.blocks = 0;
+  L.row_bits = align256(bh * L.nqb * L.nkb);
+  L.col_bits = L.row_bits + align256(bh * L.nkb * static_cast<size_t>(Tq) * 16);
+  L.total = L.col_bits + align256(bh * L.nqt * static_cast<size_t>(Tk) * 8);
+  return L;
+}
+
+// Points the kernel parameters at the block map of a prepared mask
+// (fa4d_mask_prepare) with extents Bm x Hm; returns its layout for the bit arrays.
+template <class P>
+PrepLayout use_prepared_map(P& p, const void* prepared, int Bm, int Hm, int Tq, int Tk) {
+  const PrepLayout L = prep_layout(Bm, Hm, Tq, Tk);
+  p.mask_blocks = static_cast<const uint8_t*>(prepared) + L.blocks;
+  p.mb_stride[0] = Bm > 1 ? static_cast<int64_t>(Hm) * L.nqb * L.nkb : 0;
+  p.mb_stride[1] = Hm > 1 ? static_cast<int64_t>(L.nqb) * L.nkb : 0;
+  return L;
+}
+
 int check_common(int B, int Tq, int Tk, int Hq, int Hk, int D, int dtype, int causal, float scale) {
   if (B < 1 || Tq < 1 || Tk < 1 || Hq < 1 || Hk < 1)
     return fail(FA4D_ERR_INVALID, "sizes must be positive (B=%d Tq=%d Tk=%d Hq=%d Hk=%d)", B, Tq, Tk, Hq, Hk);
@@ -189,6 +220,46 @@ size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D) {
 const char* fa4d_last_error(void) { return g_last_error.c_str(); }
 
 int fa4d_abi_version(void) { return FA4D_ABI_VERSION; }
+
+size_t fa4d_mask_prepare_size(int32_t Bm, int32_t Hm, int32_t Tq, int32_t Tk) {
+  if (Bm < 1 || Hm < 1 || Tq < 1 || Tk < 1) return 0;
+  return prep_layout(Bm, Hm, Tq, Tk).total;
+}
+
+int fa4d_mask_prepare(const uint8_t* mask, const int64_t mask_stride[3], int32_t Bm, int32_t Hm, int32_t Tq,
+                      int32_t Tk, void* prepared, void* stream) {
+  if (!mask || !mask_stride || !prepared) return fail(FA4D_ERR_INVALID, "mask, mask_stride and prepared are required");
+  if (Bm < 1 || Hm < 1 || Tq < 1 || Tk < 1)
+    return fail(FA4D_ERR_INVALID, "sizes must be positive (Bm=%d Hm=%d Tq=%d Tk=%d)", Bm, Hm, Tq, Tk);
+  if (static_cast<int64_t>(Bm) * Hm > 65535 || nblocks(Tq) > 65535)
+    return fail(FA4D_ERR_UNSUPPORTED, "Bm*Hm and ceil(Tq/128) must be <= 65535");
+  if (mask_stride[0] < 0 || mask_stride[1] < 0 || mask_stride[2] < 0)
+    return fail(FA4D_ERR_INVALID, "mask strides must be non-negative");
+  if (!aligned(prepared, 256)) return fail(FA4D_ERR_LAYOUT, "prepared buffer must be 256-byte aligned");
+  int rc = bind_device_of(mask, "mask");
+  if (rc) return rc;
+  const PrepLayout L = prep_layout(Bm, Hm, Tq, Tk);
+  fa4d::MaskPrepParams p;
+  memset(&p, 0, sizeof(p));
+  p.mask = mask;
+  for (int i = 0; i < 3; ++i) p.stride[i] = mask_stride[i];
+  p.Bm = Bm;
+  p.Hm = Hm;
+  p.Tq = Tq;
+  p.Tk = Tk;
+  p.nqb = L.nqb;
+  p.nkb = L.nkb;
+  p.nqt = L.nqt;
+  p.vec = aligned(mask, 16) && Tk % 16 == 0 && mask_stride[0] % 16 == 0 && mask_stride[1] % 16 == 0 &&
+          mask_stride[2] % 16 == 0;
+  char* base = static_cast<char*>(prepared);
+  p.blocks = reinterpret_cast<uint8_t*>(base + L.blocks);
+  p.row_bits = reinterpret_cast<uint32_t*>(base + L.row_bits);
+  p.col_bits = reinterpret_cast<uint32_t*>(base + L.col_bits);
+  cudaError_t e = fa4d::launch_mask_prepare(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "mask prepare launch failed: %s", cudaGetErrorString(e));
+  return ok();
+}
 
 size_t fa4d_mask_blocks_size(int32_t Bm, int32_t Hm, int32_t Tq, int32_t Tk) {
   if (Bm < 1 || Hm < 1 || Tq < 1 || Tk < 1) return 0;
@@ -288,14 +359,21 @@ int fa4d_fwd(const fa4d_fwd_args* a, void* stream) {
   p.status = status_word_ptr();
   if (!p.status) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
   p.nkb = nblocks(a->Tk);
-  if (a->mask && a->mask_blocks) {
+  if (a->mask && a->mask_prepared) {
+    if (!aligned(a->mask_prepared, 256)) return fail(FA4D_ERR_LAYOUT, "mask_prepared must be 256-byte aligned");
+    const int Bm = a->mask_stride[0] ? a->B : 1, Hm = a->mask_stride[1] ? a->Hq : 1;
+    const PrepLayout L = use_prepared_map(p, a->mask_prepared, Bm, Hm, a->Tq, a->Tk);
+    p.mask_bits = reinterpret_cast<const uint32_t*>(static_cast<const char*>(a->mask_prepared) + L.row_bits);
+    const int64_t per_head = static_cast<int64_t>(L.nkb) * a->Tq * 4;
+    p.mbits_stride[0] = Bm > 1 ? per_head * Hm : 0;
+    p.mbits_stride[1] = Hm > 1 ? per_head : 0;
+  } else if (a->mask && a->mask_blocks) {
     p.mask_blocks = a->mask_blocks;
     p.mb_stride[0] = a->mask_blocks_stride[0];
     p.mb_stride[1] = a->mask_blocks_stride[1];
   }
-  if (a->mask || a->score) {
-    p.bias_tma = (!a->mask || encode_bias(&p.tm_mask, a->mask, a->B, a->Hq, a->Tq, a->Tk, a->mask_stride, 1)) &&
-                 (!a->score || encode_bias(&p.tm_score, a->score, a->B, a->Hq, a->Tq, a->Tk, a->score_stride, 4));
+  if (a->score) {
+    p.bias_tma = encode_bias(&p.tm_score, a->score, a->B, a->Hq, a->Tq, a->Tk, a->score_stride, 4);
   }
   cudaError_t e = fa4d::launch_fwd(p, a->D, bf16, a->mask != nullptr, a->score != nullptr,
                                    static_cast<cudaStream_t>(stream));
@@ -377,7 +455,15 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   p.scale = a->scale;
   p.status = status;
   p.nkb = nblocks(a->Tk);
-  if (a->mask && a->mask_blocks) {
+  if (a->mask && a->mask_prepared) {
+    if (!aligned(a->mask_prepared, 256)) return fail(FA4D_ERR_LAYOUT, "mask_prepared must be 256-byte aligned");
+    const int Bm = a->mask_stride[0] ? a->B : 1, Hm = a->mask_stride[1] ? a->Hq : 1;
+    const PrepLayout L = use_prepared_map(p, a->mask_prepared, Bm, Hm, a->Tq, a->Tk);
+    p.mask_bits_t = reinterpret_cast<const uint32_t*>(static_cast<const char*>(a->mask_prepared) + L.col_bits);
+    const int64_t per_head = static_cast<int64_t>(L.nqt) * a->Tk * 2;
+    p.mbt_stride[0] = Bm > 1 ? per_head * Hm : 0;
+    p.mbt_stride[1] = Hm > 1 ? per_head : 0;
+  } else if (a->mask && a->mask_blocks) {
     p.mask_blocks = a->mask_blocks;
     p.mb_stride[0] = a->mask_blocks_stride[0];
     p.mb_stride[1] = a->mask_blocks_stride[1];

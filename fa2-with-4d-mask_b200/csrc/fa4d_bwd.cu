@@ -384,6 +384,35 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       const uint8_t* mask_col = nullptr;
       if (kScore) score_col = p.score + b * p.score_stride[0] + h * p.score_stride[1] + kc;
       if (kMask) mask_col = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + kc;
+      // Keep flags of the tile's 64 queries for this key (bit c = query q0 + c): mask,
+      // query bound, key bound and causal limit, applied as whole-word masks.
+      uint32_t kw[2] = {0xffffffffu, 0xffffffffu};
+      if (!fast) {
+        if (use_mask) {
+          if (p.mask_bits_t) {
+            const uint2 v = __ldg(reinterpret_cast<const uint2*>(p.mask_bits_t + b * p.mbt_stride[0] +
+                                                                  h * p.mbt_stride[1]) +
+                                  static_cast<int64_t>(q0 >> 6) * p.Tk + kc);
+            kw[0] = v.x;
+            kw[1] = v.y;
+          } else {
+#pragma unroll 8
+            for (int c = 0; c < 64; ++c) {
+              const int64_t qc = min(q0 + c, p.Tq - 1);
+              if (__ldg(mask_col + qc * p.mask_stride[2]) == 0) kw[c >> 5] &= ~(1u << (c & 31));
+            }
+          }
+        }
+        if (need_bounds || need_causal) {
+#pragma unroll
+          for (int w = 0; w < 2; ++w) {
+            const int base = q0 + 32 * w;
+            uint32_t lim = k_valid ? low_bits(p.Tq - base) : 0u;
+            if (need_causal) lim &= ~low_bits(k - p.causal_off - base);  // keep q >= k - off
+            kw[w] &= lim;
+          }
+        }
+      }
       float pv[64];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -401,19 +430,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             pv[c + 3] = ex2(fmaf(__uint_as_float(sr[4 * i + 3]), p.scale_log2, -l.w));
           }
         } else {
+          const uint32_t w = kw[half];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int c = 32 * half + i;
-            const int q = q0 + c;
-            const int64_t qc = min(q, p.Tq - 1);
-            bool keep = true;
-            if (need_bounds) keep = k_valid && (q < p.Tq);
-            if (need_causal) keep = keep && (k <= q + p.causal_off);
             float x = __uint_as_float(sr[i]);
-            if constexpr (kScore) x += __ldg(score_col + qc * p.score_stride[2]);
-            if (use_mask) keep = keep && (__ldg(mask_col + qc * p.mask_stride[2]) != 0);
+            if constexpr (kScore) x += __ldg(score_col + min(q0 + c, p.Tq - 1) * p.score_stride[2]);
             const float e = ex2(fmaf(x, p.scale_log2, -sLSE[qs * 64 + c]));
-            pv[c] = keep ? e : 0.f;
+            pv[c] = ((w >> i) & 1u) ? e : 0.f;
           }
         }
         // P^T (16-bit) for these 32 queries goes to columns 16*half .. 16*half+15,

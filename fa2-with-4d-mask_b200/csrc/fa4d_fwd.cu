@@ -44,14 +44,13 @@ constexpr float kNegInf = -INFINITY;
 // O is only rescaled when the running max grows by more than this (log2 units);
 // in between, P = exp2(s - stale max) stays <= 2^8, exact after the final 1/l.
 constexpr float kRescaleThreshold = 8.0f;
-// One staged mask tile (128 rows x 128 keys, 1 B) or score chunk (128 rows x 32
-// keys, fp32): 128 B per row, 128-B swizzled.
+// One staged score chunk (128 rows x 32 keys, fp32): 128 B per row, 128-B swizzled.
 constexpr int kRingEntry = 16384;
 
 template <int D, bool kMask, bool kScore>
 struct FwdLayout {
   static constexpr int kTile = 128 * D * 2;  // one 128-row tile of 16-bit elements
-  // With a score at D=128 the staging rings take the room of one K/V stage.
+  // With a score at D=128 the score staging rings take the room of one K/V stage.
   static constexpr int kKVStages = (kScore && D == 128) ? 1 : 2;
   static constexpr int kQ = 0;  // 2 query slots
   static constexpr int kK = kQ + 2 * kTile;
@@ -59,14 +58,14 @@ struct FwdLayout {
   static constexpr int kRing = kV + kKVStages * kTile;  // [2 slots][kRingDepth] entries
   static constexpr int kRingRoom = 232448 - 1024 - 512 - kRing;
   static constexpr int kRingFit = kRingRoom / (2 * kRingEntry);
-  static constexpr int kRingDepth = (kMask || kScore) ? (kRingFit < 4 ? kRingFit : 4) : 0;
+  static constexpr int kRingDepth = kScore ? (kRingFit < 4 ? kRingFit : 4) : 0;
   static constexpr int kBar = kRing + 2 * kRingDepth * kRingEntry;
   static constexpr int kNumBars = 16 + 4 * kRingDepth;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
   static_assert(kAlloc <= 232448, "shared memory beyond the 227 KB per-block limit");
-  static_assert(!(kMask || kScore) || kRingDepth >= 1, "no room for the mask/score staging ring");
+  static_assert(!kScore || kRingDepth >= 1, "no room for the score staging ring");
 };
 
 // S[slot] = Q[slot] K^T : M=128, N=128, K=D; both operands K-major, 128-B swizzled.
@@ -134,16 +133,10 @@ __device__ __forceinline__ int next_union(const SlotTiles<kMask>& s0, const Slot
   return kt;
 }
 
-// Bit e (e = 0..3) is set when byte e of w is nonzero.
-__device__ __forceinline__ uint32_t nonzero_bits4(uint32_t w) {
-  return ((__vcmpne4(w, 0u) & 0x01010101u) * 0x01020408u) >> 24;
-}
-
 template <int D, bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_constant__ FwdParams p) {
   using L = FwdLayout<D, kMask, kScore>;
-  constexpr bool kBias = kMask || kScore;
-  constexpr int R = L::kRingDepth;
+  constexpr int R = L::kRingDepth > 0 ? L::kRingDepth : 1;  // ring index modulus (ring unused if 0 deep)
   constexpr int KVS = L::kKVStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -157,8 +150,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
   uint64_t* p_full = bars + 11;  // [2] per slot
   uint64_t* o_full = bars + 13;  // [2] per slot
   uint64_t* mma_drain = bars + 15;
-  uint64_t* ring_full = bars + 16;          // [2 slots][R]
-  uint64_t* ring_empty = bars + 16 + 2 * R;  // [2 slots][R], 128 arrivals
+  uint64_t* ring_full = bars + 16;                         // [2 slots][kRingDepth]
+  uint64_t* ring_empty = bars + 16 + 2 * L::kRingDepth;   // [2 slots][kRingDepth], 128 arrivals
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -195,7 +188,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       mbar_init(&o_full[i], 1);
     }
     mbar_init(mma_drain, 1);
-    for (int i = 0; i < 2 * R; ++i) {
+    for (int i = 0; i < 2 * L::kRingDepth; ++i) {
       mbar_init(&ring_full[i], 1);
       mbar_init(&ring_empty[i], 128);
     }
@@ -341,18 +334,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       wait(mma_drain, 0);
     }
     __syncwarp();
-    } else if (kBias) {
-    // ------------------------------------------------------------ mask / score staging
-    // Warp 3 feeds query slot 0, warp 2 (after the TMEM allocation) slot 1: for each
-    // tile the slot visits, the mask tile (PARTIAL blocks only) and then the four
-    // 32-key score chunks, in that order, into the slot's ring.
+    } else if (kScore) {
+    // ------------------------------------------------------------ score staging
+    // Warp 3 feeds query slot 0, warp 2 (after the TMEM allocation) slot 1: the four
+    // 32-key score chunks of every tile the slot visits, in order, into its ring.
     const int t = warp == 3 ? 0 : 1;
     const SlotTiles<kMask> tl = t ? tiles1 : tiles0;
     if (lane == 0 && p.bias_tma && tl.n > 0) {
-      if (kMask) prefetch_tmap(&p.tm_mask);
-      if (kScore) prefetch_tmap(&p.tm_score);
+      prefetch_tmap(&p.tm_score);
       const int qs = q0 + 128 * t;
-      const int hm = p.mask_stride[1] ? h : 0, bm = p.mask_stride[0] ? b : 0;
       const int hs = p.score_stride[1] ? h : 0, bs = p.score_stride[0] ? b : 0;
       uint8_t* ring = smem + L::kRing + t * R * kRingEntry;
       uint64_t* full = ring_full + t * R;
@@ -360,24 +350,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       int g = 0;
       bool ok = true;
       for (int kt = tl.next(0); ok && kt < tl.n; kt = tl.next(kt + 1)) {
-        if (kMask && tl.state(kt) == 1) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
           const int e = g % R;
           ok = mbar_wait(&empty[e], ((g / R) & 1) ^ 1, abort_flag);
           if (!ok) break;
           mbar_arrive_expect_tx(&full[e], kRingEntry);
-          tma_load_4d(ring + e * kRingEntry, &p.tm_mask, &full[e], kt * 128, qs, hm, bm);
+          tma_load_4d(ring + e * kRingEntry, &p.tm_score, &full[e], kt * 128 + 32 * c, qs, hs, bs);
           ++g;
-        }
-        if (kScore) {
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            const int e = g % R;
-            ok = mbar_wait(&empty[e], ((g / R) & 1) ^ 1, abort_flag);
-            if (!ok) break;
-            mbar_arrive_expect_tx(&full[e], kRingEntry);
-            tma_load_4d(ring + e * kRingEntry, &p.tm_score, &full[e], kt * 128 + 32 * c, qs, hs, bs);
-            ++g;
-          }
         }
       }
       if (*reinterpret_cast<volatile int*>(abort_flag)) {
@@ -399,43 +379,51 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     const uint32_t tO = tmem + lane_base + 256 + D * t;
     const SlotTiles<kMask> tl = t ? tiles1 : tiles0;
 
-    // Global-memory fallback (bias_tma == 0): rows past Tq read row Tq-1 (always in
-    // bounds) and are never stored, so the loads carry no per-lane branch and the
-    // warp stays converged for the TMEM ops.
+    // Rows past Tq read row Tq-1 of the mask / score (always in bounds) and are never
+    // stored, so the loads carry no per-lane branch and the warp stays converged for
+    // the TMEM ops.
     const int64_t qc = min(q, p.Tq - 1);
     const float* score_row = nullptr;
     const uint8_t* mask_row = nullptr;
+    const uint4* bits_row = nullptr;  // prepared mask bits: one uint4 per key tile
     if (kScore) score_row = p.score + b * p.score_stride[0] + h * p.score_stride[1] + qc * p.score_stride[2];
-    if (kMask) mask_row = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + qc * p.mask_stride[2];
-    // Staged path: this thread's row of each ring entry (128 B, 16-B units swizzled by row % 8).
-    const uint8_t* ring_row = smem + L::kRing + t * R * kRingEntry + row * 128;
+    if (kMask) {
+      mask_row = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + qc * p.mask_stride[2];
+      if (p.mask_bits)
+        bits_row = reinterpret_cast<const uint4*>(p.mask_bits + b * p.mbits_stride[0] + h * p.mbits_stride[1]) + qc;
+    }
+    // Staged score: this thread's row of each ring entry (128 B, 16-B units swizzled by row % 8).
+    const uint32_t ring_row = smem_u32(smem + L::kRing + t * R * kRingEntry + row * 128);
     uint64_t* full = ring_full + t * R;
     uint64_t* empty = ring_empty + t * R;
     const int sw = row & 7;
     int g = 0;
+    // Keys this row may see at all: below Tk and, when causal, k <= q + causal_off.
+    const int key_lim = p.causal ? min(p.Tk, static_cast<int>(min(static_cast<long long>(q) + p.causal_off + 1,
+                                                                     static_cast<long long>(p.Tk))))
+                                 : p.Tk;
 
     float m_run = kNegInf;
     float l_run = 0.f;
     bool ok = true;
     int i = 0;  // tiles processed by this slot
-    for (int kt = tl.next(0); kt < tl.n; kt = tl.next(kt + 1), ++i) {
+    int kt = tl.next(0);
+    // Mask bits of the next PARTIAL tile are loaded one tile ahead.
+    uint4 bits_next = make_uint4(0u, 0u, 0u, 0u);
+    if (kMask && bits_row && kt < tl.n && tl.state(kt) == 1) bits_next = __ldg(bits_row + static_cast<int64_t>(kt) * p.Tq);
+    for (; kt < tl.n; ++i) {
+      const int kt_next = tl.next(kt + 1);
       const bool use_mask = kMask && tl.state(kt) == 1;  // warp-uniform
-      uint32_t mbits[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
-      if (kMask && use_mask && p.bias_tma) {
-        const int e = g % R;
-        ok = __all_sync(0xffffffffu, mbar_wait(&full[e], (g / R) & 1, abort_flag));
-        if (!ok) break;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 w0 = *reinterpret_cast<const uint4*>(ring_row + e * kRingEntry + (((2 * c) ^ sw) << 4));
-          const uint4 w1 = *reinterpret_cast<const uint4*>(ring_row + e * kRingEntry + (((2 * c + 1) ^ sw) << 4));
-          mbits[c] = nonzero_bits4(w0.x) | (nonzero_bits4(w0.y) << 4) | (nonzero_bits4(w0.z) << 8) |
-                     (nonzero_bits4(w0.w) << 12) | (nonzero_bits4(w1.x) << 16) | (nonzero_bits4(w1.y) << 20) |
-                     (nonzero_bits4(w1.z) << 24) | (nonzero_bits4(w1.w) << 28);
-        }
-        mbar_arrive(&empty[e]);
-        ++g;
+      uint32_t mw[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};  // keep bit per key
+      if (kMask && use_mask && bits_row) {
+        mw[0] = bits_next.x;
+        mw[1] = bits_next.y;
+        mw[2] = bits_next.z;
+        mw[3] = bits_next.w;
       }
+      if (kMask && bits_row && kt_next < tl.n && tl.state(kt_next) == 1)
+        bits_next = __ldg(bits_row + static_cast<int64_t>(kt_next) * p.Tq);
+
       // Warp-uniform outcome: the tcgen05.ld below is warp-collective.
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], i & 1, abort_flag));
       if (!ok) break;
@@ -458,23 +446,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         for (int k = 0; k < 128; ++k) m4[k & 3] = fmaxf(m4[k & 3], __uint_as_float(sr[k]));
         m_tile = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
       } else {
+        if (kMask && use_mask && !bits_row) {
+          // No prepared bits: read this row's 128 mask bytes from global memory.
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int kc = kbase + 32 * c;
-          uint32_t mb = mbits[c];
-          if (kMask && use_mask && !p.bias_tma) {
-            mb = 0u;
+          for (int c = 0; c < 4; ++c) {
+            const int kc = kbase + 32 * c;
+            uint32_t w = 0u;
             // kc is the same for every lane, so these branches are warp-uniform.
             if (p.mask_vec && kc + 31 < p.Tk) {
 #pragma unroll
-              for (int w = 0; w < 8; ++w)
-                mb |= nonzero_bits4(__ldg(reinterpret_cast<const unsigned int*>(mask_row + kc) + w)) << (4 * w);
+              for (int u = 0; u < 8; ++u)
+                w |= keep_bits4(__ldg(reinterpret_cast<const unsigned int*>(mask_row + kc) + u)) << (4 * u);
             } else {
 #pragma unroll
               for (int e = 0; e < 32; ++e)
-                if (kc + e < p.Tk) mb |= (__ldg(mask_row + kc + e) != 0 ? 1u : 0u) << e;
+                if (kc + e < p.Tk) w |= (__ldg(mask_row + kc + e) != 0 ? 1u : 0u) << e;
             }
+            mw[c] = w;
           }
+        }
+        if (need_bounds || need_causal) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) mw[c] &= low_bits(key_lim - (kbase + 32 * c));
+        }
+        float m4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int kc = kbase + 32 * c;
           float add[32];
           if constexpr (kScore) {
             if (p.bias_tma) {
@@ -483,7 +481,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
               if (!ok) break;
 #pragma unroll
               for (int u = 0; u < 8; ++u) {
-                const float4 v = *reinterpret_cast<const float4*>(ring_row + e * kRingEntry + ((u ^ sw) << 4));
+                const float4 v = lds_f4(ring_row + e * kRingEntry + ((u ^ sw) << 4));
                 add[4 * u] = v.x;
                 add[4 * u + 1] = v.y;
                 add[4 * u + 2] = v.z;
@@ -505,22 +503,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
               for (int e = 0; e < 32; ++e) add[e] = (kc + e < p.Tk) ? __ldg(score_row + kc + e) : 0.f;
             }
           }
+          const uint32_t w = mw[c];
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const int k = kc + e;
             float x = __uint_as_float(sr[32 * c + e]);
             if constexpr (kScore) x += add[e];
             x *= p.scale_log2;
-            bool keep = true;
-            if constexpr (kMask) keep = (mb >> e) & 1u;
-            if (need_bounds) keep = keep && (k < p.Tk);
-            if (need_causal) keep = keep && (k <= q + p.causal_off);
-            x = keep ? x : kNegInf;
+            x = ((w >> e) & 1u) ? x : kNegInf;
             sr[32 * c + e] = __float_as_uint(x);
-            m_tile = fmaxf(m_tile, x);
+            m4[e & 3] = fmaxf(m4[e & 3], x);
           }
         }
         if (!ok) break;
+        m_tile = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
 
       // Online softmax with lazy rescaling of O.
@@ -581,6 +576,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
+      kt = kt_next;
     }
 
     // Epilogue: O / l and LSE.  A slot that visits no tile (every block EMPTY) has

@@ -40,6 +40,11 @@ struct FwdParams {
   int32_t bias_tma;
   CUtensorMap tm_mask;
   CUtensorMap tm_score;
+  // Prepared row bits (fa4d_mask_prepare) or null: the uint4 at word offset
+  // b*mbits_stride[0] + h*mbits_stride[1] + (kt*Tq + q)*4 holds the keep flags of
+  // the 128 keys of key tile kt for query row q.
+  const uint32_t* mask_bits;
+  int64_t mbits_stride[2];
 };
 
 // Backward: one CTA owns 128 keys of one (batch, KV head), loops over every
@@ -71,6 +76,11 @@ struct BwdParams {
   const uint8_t* mask_blocks;  // as in FwdParams
   int64_t mb_stride[2];
   int32_t nkb;
+  // Prepared column bits or null: the uint2 at word offset b*mbt_stride[0] +
+  // h*mbt_stride[1] + (qt*Tk + k)*2 holds the keep flags of the 64 queries of
+  // query tile qt for key k.
+  const uint32_t* mask_bits_t;
+  int64_t mbt_stride[2];
 };
 
 // Block-occupancy pre-pass: blocks[((b * Hm + h) * nqb + qb) * nkb + kb] =
@@ -81,6 +91,19 @@ struct MaskBlocksParams {
   int32_t Bm, Hm, Tq, Tk, nqb, nkb;
   int32_t vec;        // 1: base 16-B aligned and row stride a multiple of 16 with Tk % 16 == 0
   uint8_t* blocks;
+};
+
+// Mask preparation: block map as above plus the mask as packed bits, row-major for
+// the forward and transposed for the backward (see mask_prepare_kernel).
+struct MaskPrepParams {
+  const uint8_t* mask;
+  int64_t stride[3];
+  int32_t Bm, Hm, Tq, Tk, nqb, nkb;
+  int32_t vec;
+  int32_t nqt;        // ceil(Tq / 64)
+  uint8_t* blocks;
+  uint32_t* row_bits;
+  uint32_t* col_bits;
 };
 
 // Row dot products Delta = rowsum(O * dO) and zeroing of the dQ accumulator.
@@ -110,6 +133,7 @@ cudaError_t launch_bwd(const BwdParams& p, int D, bool bf16, bool has_mask, bool
 cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_mask_blocks(const MaskBlocksParams& p, cudaStream_t s);
+cudaError_t launch_mask_prepare(const MaskPrepParams& p, cudaStream_t s);
 cudaError_t launch_exp2_check(float* out, int n, float lo, float hi, cudaStream_t s);
 
 }  // namespace fa4d

@@ -322,4 +322,22 @@ __device__ __forceinline__ void red_add_f32(float* addr, float v) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }
 
+// ------------------------------------------------------------------ mask bits
+// Keep flags (nonzero = keep) of the 4 bytes of w as bits 0..3.
+__device__ __forceinline__ uint32_t keep_bits4(uint32_t w) {
+  const uint32_t hi = (((w & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | w) & 0x80808080u;  // bit 8j+7 = byte j nonzero
+  return (hi * 0x00204081u) >> 28;  // bits 7, 15, 23, 31 gathered into 28..31
+}
+// Bits 0..n-1 set (n clamped to [0, 32]).
+__device__ __forceinline__ uint32_t low_bits(int n) {
+  return n <= 0 ? 0u : (n >= 32 ? 0xffffffffu : ((1u << n) - 1u));
+}
+
+// ------------------------------------------------------------------ shared loads
+__device__ __forceinline__ float4 lds_f4(uint32_t saddr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(saddr));
+  return v;
+}
+
 }  // namespace fa4d

@@ -16,11 +16,13 @@ python/fa2.py:556).  ``use_atomic_backward`` is accepted for compatibility; both
 values run the same backward, in which dK/dV are summed over the GQA group inside
 the kernel and dQ is accumulated in fp32.
 
-A bool mask is first reduced to a block map (``fa4d_mask_blocks``: each 128 x 128
-block EMPTY, PARTIAL or FULL) that the forward and backward kernels use to skip
-EMPTY blocks and the mask loads of FULL ones.  The map is cached per mask tensor
-(identity of the tensor or of the tensor it views, plus its version counter), so a
-mask shared by every layer of a model is scanned once while it is unchanged.
+A bool mask is first prepared once (``fa4d_mask_prepare``): a block map (each
+128 x 128 block EMPTY, PARTIAL or FULL) that the forward and backward kernels use
+to skip EMPTY blocks and the mask reads of FULL ones, and the mask as packed bits
+that the kernels read instead of the bytes.  The preparation is cached per mask
+tensor (identity of the tensor or of the tensor it views, plus its version
+counter), so a mask shared by every layer of a model is scanned once while it is
+unchanged.
 """
 
 from __future__ import annotations
@@ -59,7 +61,7 @@ class _BlockMapCache:
     def _key(mask: torch.Tensor) -> tuple:
         return (mask.data_ptr(), tuple(mask.shape), tuple(mask.stride()), mask.dtype, mask.device, mask._version)
 
-    def get(self, mask: torch.Tensor) -> "_lib.BlockMap":
+    def get(self, mask: torch.Tensor) -> "_lib.PreparedMask":
         owner = mask._base if mask._base is not None else mask
         key = self._key(mask)
         for i, (ref, k, bm) in enumerate(self._entries):
@@ -67,7 +69,7 @@ class _BlockMapCache:
                 if i:
                     self._entries.insert(0, self._entries.pop(i))
                 return bm
-        bm = _lib.mask_blocks(mask)
+        bm = _lib.mask_prepare(mask)
         self._entries.insert(0, (weakref.ref(owner), key, bm))
         del self._entries[self.capacity :]
         return bm
@@ -80,8 +82,8 @@ _block_maps = _BlockMapCache()
 
 
 def clear_block_map_cache() -> None:
-    """Drops every cached mask block map (e.g. after writing a mask in place through
-    a path that does not bump its version counter)."""
+    """Drops every cached mask preparation (e.g. after writing a mask in place
+    through a path that does not bump its version counter)."""
     _block_maps.clear()
 
 

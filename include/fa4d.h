@@ -79,6 +79,12 @@ typedef struct fa4d_fwd_args {
    * Ignored when mask is NULL. */
   const uint8_t* mask_blocks;
   int64_t mask_blocks_stride[2];
+  /* Optional output of fa4d_mask_prepare for `mask` (NULL = none), 256-B aligned.
+   * It holds the block map and the mask as packed bits; when given, the kernels
+   * skip EMPTY blocks and read the bits instead of the mask bytes, and
+   * mask_blocks is ignored.  It must have been prepared with Bm = (mask_stride[0]
+   * ? B : 1) and Hm = (mask_stride[1] ? Hq : 1) and the same Tq, Tk. */
+  const void* mask_prepared;
 } fa4d_fwd_args;
 
 typedef struct fa4d_bwd_args {
@@ -112,6 +118,7 @@ typedef struct fa4d_bwd_args {
   size_t workspace_bytes;
   const uint8_t* mask_blocks;      /* optional, as in fa4d_fwd_args */
   int64_t mask_blocks_stride[2];
+  const void* mask_prepared;       /* optional, as in fa4d_fwd_args */
 } fa4d_bwd_args;
 
 /* Row stride (in floats) of the LSE buffer: Tq rounded up to a multiple of 128.
@@ -179,6 +186,24 @@ enum fa4d_block_state { FA4D_BLOCK_EMPTY = 0, FA4D_BLOCK_PARTIAL = 1, FA4D_BLOCK
 size_t fa4d_mask_blocks_size(int32_t Bm, int32_t Hm, int32_t Tq, int32_t Tk);
 int fa4d_mask_blocks(const uint8_t* mask, const int64_t mask_stride[3], int32_t Bm, int32_t Hm, int32_t Tq,
                      int32_t Tk, uint8_t* blocks, void* stream);
+
+/* Mask preparation: one pass over a bool mask [Bm, Hm, Tq, Tk] (strides and
+ * extents as for fa4d_mask_blocks) that writes into the caller's buffer of
+ * fa4d_mask_prepare_size() bytes (256-B aligned):
+ *   - the block map of fa4d_mask_blocks (byte offset 0);
+ *   - row bits: per (b, h) a [ceil(Tk/128)][Tq][4] array of uint32 whose entry
+ *     (kt, q, w) holds the flags of keys 128*kt + 32*w + 0..31 for query q;
+ *   - column bits: per (b, h) a [ceil(Tq/64)][Tk][2] array of uint32 whose entry
+ *     (qt, k, w) holds the flags of queries 64*qt + 32*w + 0..31 for key k;
+ * with flags past Tk / Tq zero.  The forward reads one 16-byte row-bit word group
+ * per query row and key tile, the backward one 8-byte column-bit group per key and
+ * query tile, instead of 128 or 64 mask bytes.  Like the block map, the buffer stays
+ * valid while the mask is unchanged (one preparation serves every call sharing the
+ * mask).  No counterpart in the reference, which reads the bool mask per element
+ * (python/fa2.py:108, :274-280). */
+size_t fa4d_mask_prepare_size(int32_t Bm, int32_t Hm, int32_t Tq, int32_t Tk);
+int fa4d_mask_prepare(const uint8_t* mask, const int64_t mask_stride[3], int32_t Bm, int32_t Hm, int32_t Tq,
+                      int32_t Tk, void* prepared, void* stream);
 
 /* Message for the last non-zero return on this thread ("" if none). */
 const char* fa4d_last_error(void);

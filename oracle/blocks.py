@@ -42,3 +42,28 @@ def empty_fraction(mask, block: int = BLOCK) -> float:
     """Share of blocks with no True element."""
     b = mask_blocks_ref(mask, block)
     return float((b == EMPTY).mean())
+
+
+def _pack32(flags: np.ndarray) -> np.ndarray:
+    """Packs the last axis (a multiple of 32 booleans) into int32 words, bit j of
+    word w = flag 32*w + j."""
+    f = flags.astype(np.uint64).reshape(*flags.shape[:-1], -1, 32)
+    words = (f << np.arange(32, dtype=np.uint64)).sum(axis=-1)
+    return words.astype(np.uint32).view(np.int32)
+
+
+def mask_bits_ref(mask):
+    """The packed-bit layouts of a prepared mask [Bm, Hm, Tq, Tk]:
+    row bits [Bm, Hm, ceil(Tk/128), Tq, 4] (word w of (kt, q) = keys 128kt+32w+0..31)
+    and column bits [Bm, Hm, ceil(Tq/64), Tk, 2] (word w of (qt, k) = queries
+    64qt+32w+0..31), flags past Tk / Tq zero."""
+    m = np.asarray(mask) != 0
+    Bm, Hm, Tq, Tk = m.shape
+    nkb, nqt = -(-Tk // BLOCK), -(-Tq // 64)
+    rows = np.zeros((Bm, Hm, Tq, nkb * BLOCK), dtype=bool)
+    rows[..., :Tk] = m
+    rw = _pack32(rows).reshape(Bm, Hm, Tq, nkb, 4).transpose(0, 1, 3, 2, 4)
+    cols = np.zeros((Bm, Hm, Tk, nqt * 64), dtype=bool)
+    cols[..., :Tq] = m.transpose(0, 1, 3, 2)
+    cw = _pack32(cols).reshape(Bm, Hm, Tk, nqt, 2).transpose(0, 1, 3, 2, 4)
+    return np.ascontiguousarray(rw), np.ascontiguousarray(cw)

@@ -66,7 +66,7 @@ def test_block_map_cache_reuse_and_invalidation(monkeypatch):
         calls.append(mask)
         return object()
 
-    monkeypatch.setattr(impl_fa2._lib, "mask_blocks", fake)
+    monkeypatch.setattr(impl_fa2._lib, "mask_prepare", fake)
     cache = impl_fa2._BlockMapCache(capacity=2)
     base = torch.zeros(1, 1, 8, 8, dtype=torch.bool)
     a = cache.get(base)
@@ -87,3 +87,20 @@ def test_block_map_cache_reuse_and_invalidation(monkeypatch):
     cache.clear()
     cache.get(other)
     assert len(calls) == 5
+
+
+def test_bits_oracle_layout():
+    rng = np.random.default_rng(3)
+    m = rng.random((1, 2, 70, 200)) < 0.5
+    from oracle.blocks import mask_bits_ref
+
+    rw, cw = mask_bits_ref(m)
+    assert rw.shape == (1, 2, 2, 70, 4) and cw.shape == (1, 2, 2, 200, 2)
+    for (h, q, k) in [(0, 0, 0), (1, 69, 199), (1, 33, 130), (0, 5, 127)]:
+        word = rw[0, h, k // 128, q, (k % 128) // 32].view(np.uint32)
+        assert bool((int(word) >> (k % 32)) & 1) == bool(m[0, h, q, k])
+        word = cw[0, h, q // 64, k, (q % 64) // 32].view(np.uint32)
+        assert bool((int(word) >> (q % 32)) & 1) == bool(m[0, h, q, k])
+    # Flags past Tk / Tq are zero.
+    assert (rw[0, :, 1, :, 3] == 0).all() and (cw[0, :, 1, :, 1] == 0).all()
+    assert (rw[0, :, 1, :, 2].view(np.uint32) >> 8 == 0).all()

@@ -1,5 +1,6 @@
-"""GPU: the block-occupancy pre-pass (fa4d_mask_blocks) against the oracle's
-classification, and block-sparse skipping in the forward and backward kernels.
+"""GPU: the mask pre-passes (fa4d_mask_blocks, fa4d_mask_prepare) against the
+oracle's block classification and bit layouts, and block-sparse skipping plus
+packed-bit mask reads in the forward and backward kernels.
 
 Skipping an EMPTY block removes keys whose probabilities are exactly zero, and a
 FULL block is processed like an unmasked one, so results with the block map must
@@ -14,7 +15,7 @@ import torch
 
 from conftest import out_err, rel_err
 from oracle import inputs as I
-from oracle.blocks import EMPTY, FULL, PARTIAL, mask_blocks_ref
+from oracle.blocks import EMPTY, FULL, PARTIAL, mask_bits_ref, mask_blocks_ref
 from test_gpu_parity import DEV, _fp32_oracle_and_status, check, oracle, run_api  # noqa: F401
 
 from fa2_with_4d_mask_b200 import _lib
@@ -41,6 +42,34 @@ def test_mask_blocks_match_oracle(shape):
     m = _structured_mask(shape, sum(shape))
     got = _lib.mask_blocks(m.to(DEV)).blocks.cpu().numpy()
     np.testing.assert_array_equal(got, mask_blocks_ref(m.numpy()))
+
+
+def _check_prepared(mask_dev, ref_mask):
+    pm = _lib.mask_prepare(mask_dev)
+    np.testing.assert_array_equal(pm.blocks().cpu().numpy(), mask_blocks_ref(ref_mask))
+    rw, cw = mask_bits_ref(ref_mask)
+    np.testing.assert_array_equal(pm.row_bits().cpu().numpy(), rw)
+    np.testing.assert_array_equal(pm.col_bits().cpu().numpy(), cw)
+    return pm
+
+
+@pytest.mark.parametrize("shape", [(2, 3, 300, 520), (1, 2, 256, 512), (1, 1, 1, 1), (2, 1, 1000, 4096)])
+def test_mask_prepare_matches_oracle(shape):
+    m = _structured_mask(shape, sum(shape) + 1)
+    _check_prepared(m.to(DEV), m.numpy())
+
+
+def test_mask_prepare_broadcast_uint8_and_unaligned_rows():
+    T = 640
+    base = I.packed_doc_mask(1, T, min_len=128, max_len=384, seed=31)
+    pm = _check_prepared(base.to(DEV).expand(2, 4, T, T), base.numpy())
+    assert (pm.Bm, pm.Hm) == (1, 1)
+    _check_prepared((base.to(torch.uint8) * 9).to(DEV), base.numpy())
+    wide = torch.zeros(1, 1, T, T + 3, dtype=torch.bool)
+    wide[..., :T] = base
+    _check_prepared(wide.to(DEV)[..., :T], base.numpy())
+    odd = _structured_mask((1, 2, 77, 333), 5)
+    _check_prepared(odd.to(DEV), odd.numpy())
 
 
 def test_mask_blocks_broadcast_uint8_and_unaligned_rows():
@@ -80,22 +109,26 @@ def test_packed_documents_block_sparse(causal):
     check(got, oracle(q, k, v, do, mask=mask, causal=causal), f"packed docs c={causal}")
 
 
-def test_skipping_is_exact():
-    """Skipping EMPTY blocks changes nothing: with a map whose FULL blocks are
-    demoted to PARTIAL (so every visited block takes the masked path) O, dK and dV
-    are bit-identical to the run without a map.  FULL blocks take the unmasked
-    forward path, whose exponent arithmetic differs in rounding (checked in
-    test_full_blocks_equal_no_mask)."""
+@pytest.mark.parametrize("causal", [_lib.CAUSAL_NONE, _lib.CAUSAL_TOP_LEFT])
+def test_mask_paths_are_exact(causal):
+    """Three ways to read one mask give bit-identical O, dK and dV: mask bytes with no
+    map, mask bytes with the block map (EMPTY blocks skipped), and the prepared packed
+    bits with the same map.  FULL blocks are demoted to PARTIAL here so every visited
+    block takes the masked path; FULL blocks take the unmasked forward path, whose
+    exponent arithmetic rounds differently (checked in test_full_blocks_equal_no_mask)."""
     B, T, Hq, Hk, D = 1, 896, 4, 1, 128
     q, k, v, do = I.qkv(B, T, T, Hq, Hk, D, seed=34)
     mask = I.packed_doc_mask(B, T, min_len=128, max_len=400, seed=35).to(DEV)
     bm = _lib.mask_blocks(mask)
     assert (bm.blocks == EMPTY).any()
     bm.blocks[bm.blocks == FULL] = PARTIAL
-    a = _raw(q, k, v, do, mask, blocks=None)
-    b = _raw(q, k, v, do, mask, blocks=bm)
-    assert torch.equal(a[0], b[0]) and torch.equal(a[2], b[2]) and torch.equal(a[3], b[3])
-    assert rel_err(b[1].float(), a[1].float()) < 1e-2
+    pm = _lib.mask_prepare(mask)
+    pm.blocks()[pm.blocks() == FULL] = PARTIAL
+    a = _raw(q, k, v, do, mask, causal=causal, blocks=None)
+    for blocks in (bm, pm):
+        b = _raw(q, k, v, do, mask, causal=causal, blocks=blocks)
+        assert torch.equal(a[0], b[0]) and torch.equal(a[2], b[2]) and torch.equal(a[3], b[3])
+        assert rel_err(b[1].float(), a[1].float()) < 1e-2
 
 
 def test_full_blocks_equal_no_mask():
@@ -106,8 +139,9 @@ def test_full_blocks_equal_no_mask():
     bm = _lib.mask_blocks(mask)
     assert (bm.blocks == FULL).all()
     a = _raw(q, k, v, do, None)
-    b = _raw(q, k, v, do, mask, blocks=bm)
-    assert torch.equal(a[0], b[0]) and torch.equal(a[2], b[2]) and torch.equal(a[3], b[3])
+    for blocks in (bm, _lib.mask_prepare(mask)):
+        b = _raw(q, k, v, do, mask, blocks=blocks)
+        assert torch.equal(a[0], b[0]) and torch.equal(a[2], b[2]) and torch.equal(a[3], b[3])
 
 
 def test_per_head_block_sparse_mask_with_score():
