@@ -116,10 +116,11 @@ int encode_bthd(CUtensorMap* m, const void* ptr, int B, int T, int H, int D, con
 
 // Tensor map over a [B or 1, H or 1, Tq, Tk] mask (1-byte) or score (4-byte) tensor
 // given element strides (b, h, row): dims (Tk, Tq, H', B') with a broadcast (stride
-// 0) dimension given extent 1, box (128 bytes of keys, 128 rows, 1, 1), 128-B swizzle,
+// 0) dimension given extent 1, box (128 bytes of keys, `rows` rows, 1, 1), 128-B swizzle,
 // zero fill out of bounds.  Returns false when the layout cannot be described by a
 // tensor map (unaligned base or strides); the kernels then load from global memory.
-bool encode_bias(CUtensorMap* m, const void* ptr, int B, int H, int Tq, int Tk, const int64_t st[3], int esize) {
+bool encode_bias(CUtensorMap* m, const void* ptr, int B, int H, int Tq, int Tk, const int64_t st[3], int esize,
+                 int rows = 128) {
   auto enc = tensor_map_encoder();
   if (!enc || !ptr || !aligned(ptr, 16)) return false;
   const int64_t row = st[2] * esize;
@@ -135,7 +136,7 @@ bool encode_bias(CUtensorMap* m, const void* ptr, int B, int H, int Tq, int Tk, 
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(Tk), static_cast<cuuint64_t>(Tq), static_cast<cuuint64_t>(ext_h),
                         static_cast<cuuint64_t>(ext_b)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(row), static_cast<cuuint64_t>(sh), static_cast<cuuint64_t>(sb)};
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / esize), 128, 1, 1};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / esize), static_cast<cuuint32_t>(rows), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(m, esize == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
                    const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -468,6 +469,7 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
     p.mb_stride[0] = a->mask_blocks_stride[0];
     p.mb_stride[1] = a->mask_blocks_stride[1];
   }
+  if (a->score) p.score_pf = encode_bias(&p.tm_score, a->score, a->B, a->Hq, a->Tq, a->Tk, a->score_stride, 4, 64);
 
   fa4d::PrepParams& pp = plan->prep;
   pp.o = a->o;

@@ -233,6 +233,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       prefetch_tmap(&p.tm_do);
       prefetch_tmap(&p.tm_k);
       prefetch_tmap(&p.tm_v);
+      if (kScore && p.score_pf) prefetch_tmap(&p.tm_score);
       mbar_arrive_expect_tx(kv_full, 2 * L::kKV);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
@@ -255,6 +256,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         const int64_t row = (static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + q0;
         bulk_load(smem + L::kLSE + qs * 256, p.lse + row, 256, &q_full[qs]);
         bulk_load(smem + L::kDelta + qs * 256, p.delta + row, 256, &q_full[qs]);
+        if (kScore && p.score_pf) {
+          // The P/dS warpgroups read this tile's score column by column about two
+          // tiles from now; have it in L2 by then.
+          const int hs = p.score_stride[1] ? h : 0, bs = p.score_stride[0] ? b : 0;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tma_prefetch_l2_4d(&p.tm_score, k0 + 32 * c, q0, hs, bs);
+        }
         issued = it + 1;
       }
       if (*reinterpret_cast<volatile int*>(abort_flag)) {
@@ -364,7 +372,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     bool ok = true;
     QTiles<kMask> cur = first;
     if (wg == 1) cur.advance();
-    for (int it = wg; cur.valid(); it += 2, cur.advance(), cur.advance()) {
+    // Prepared mask bits of this warpgroup's next PARTIAL tile, loaded one tile ahead.
+    auto load_bits = [&](const QTiles<kMask>& c) {
+      const int hh = hk * G + c.g();
+      return __ldg(reinterpret_cast<const uint2*>(p.mask_bits_t + b * p.mbt_stride[0] + hh * p.mbt_stride[1]) +
+                   static_cast<int64_t>(c.q0() >> 6) * p.Tk + kc);
+    };
+    uint2 bits_next = make_uint2(0u, 0u);
+    if (kMask && p.mask_bits_t && cur.valid() && cur.state() == 1) bits_next = load_bits(cur);
+    for (int it = wg; cur.valid(); it += 2) {
+      QTiles<kMask> nxt = cur;
+      nxt.advance();
+      nxt.advance();
+      const uint2 bits_cur = bits_next;
+      if (kMask && p.mask_bits_t && nxt.valid() && nxt.state() == 1) bits_next = load_bits(nxt);
       const int st = wg;
       const uint32_t par = (it >> 1) & 1;
       const int qs = it % kQStages;
@@ -390,11 +411,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       if (!fast) {
         if (use_mask) {
           if (p.mask_bits_t) {
-            const uint2 v = __ldg(reinterpret_cast<const uint2*>(p.mask_bits_t + b * p.mbt_stride[0] +
-                                                                  h * p.mbt_stride[1]) +
-                                  static_cast<int64_t>(q0 >> 6) * p.Tk + kc);
-            kw[0] = v.x;
-            kw[1] = v.y;
+            kw[0] = bits_cur.x;
+            kw[1] = bits_cur.y;
           } else {
 #pragma unroll 8
             for (int c = 0; c < 64; ++c) {
@@ -482,6 +500,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&ds_full[st]);
+      cur = nxt;
     }
 
     // Epilogue: warpgroup 0 writes dV, warpgroup 1 writes dK (zeros when no query

@@ -81,6 +81,10 @@ struct BwdParams {
   // query tile qt for key k.
   const uint32_t* mask_bits_t;
   int64_t mbt_stride[2];
+  // score_pf = 1: the producer prefetches each query tile's score into L2 through
+  // tm_score (dims (Tk, Tq, H or 1, B or 1), box (32, 64)).
+  int32_t score_pf;
+  CUtensorMap tm_score;
 };
 
 // Block-occupancy pre-pass: blocks[((b * Hm + h) * nqb + qb) * nkb + kb] =
