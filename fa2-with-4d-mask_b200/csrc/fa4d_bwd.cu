@@ -141,7 +141,9 @@ template <int D, bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_constant__ BwdParams p) {
   using L = BwdLayout<D>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-B aligned base, derived by pointer arithmetic on the shared array so the
+  // compiler keeps the shared address space (LDS/STS rather than generic loads/stores).
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* kv_full = bars + 0;
   uint64_t* dkv_full = bars + 1;

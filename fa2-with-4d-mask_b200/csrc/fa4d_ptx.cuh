@@ -67,14 +67,18 @@ __device__ __forceinline__ uint32_t mbar_try_wait_sleep(uint64_t* bar, uint32_t 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait_sleep(bar, parity, 1000000u)) {
-    if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
-    if (clock64() - t0 > kWaitLimitCycles) {
-      *reinterpret_cast<volatile int*>(abort_flag) = 1;
-      return false;
+  // Each try_wait blocks in hardware for a while before reporting "not yet", so the
+  // loop is cheap; the abort flag and the clock are checked every 16 tries.
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((n & 15u) == 0u) {
+      if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
+      if (clock64() - t0 > kWaitLimitCycles) {
+        *reinterpret_cast<volatile int*>(abort_flag) = 1;
+        return false;
+      }
     }
   }
-  return true;
 }
 
 // Abort-path wait for copies still in flight: gives up after a short bound.
