@@ -44,6 +44,12 @@ constexpr float kNegInf = -INFINITY;
 // O is only rescaled when the running max grows by more than this (log2 units);
 // in between, P = exp2(s - stale max) stays <= 2^8, exact after the final 1/l.
 constexpr float kRescaleThreshold = 8.0f;
+// In the unmasked fast path one exponential pair in kPolyEvery is evaluated on the FMA
+// pipe (ex2_poly2) instead of the MUFU unit.
+#ifndef FA4D_POLY_EVERY
+#define FA4D_POLY_EVERY 3
+#endif
+constexpr int kPolyEvery = FA4D_POLY_EVERY;
 // One staged score chunk (128 rows x 32 keys, fp32): 128 B per row, 128-B swizzled.
 constexpr int kRingEntry = 16384;
 
@@ -544,22 +550,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       const float m_use = (m_run == kNegInf) ? 0.f : m_run;
       float rowsum = 0.f;
       if (fast) {
-        // exp2(s * scale * log2(e) - m); one element in four on the FMA pipe
-        // (ex2_poly) so the MUFU unit is not the limit.
+        // exp2(s * scale * log2(e) - m) on pairs of packed fp32; every kPolyEvery-th
+        // pair on the FMA pipe (ex2_poly2) so the MUFU unit is not the limit.
+        const uint64_t sc2 = f2(p.scale_log2, p.scale_log2), nm2 = f2(-m_use, -m_use);
+        uint64_t rs2 = f2(0.f, 0.f);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
-            const float a0 = fmaf(__uint_as_float(sr[32 * c + 2 * k]), p.scale_log2, -m_use);
-            const float a1 = fmaf(__uint_as_float(sr[32 * c + 2 * k + 1]), p.scale_log2, -m_use);
-            const float p0 = ex2(a0);
-            const float p1 = (k & 1) ? ex2_poly(a1) : ex2(a1);
-            rowsum += p0 + p1;
-            pk[k] = pack2<kBF16>(p0, p1);
+            const float2 a = f2_split(
+                ffma2(f2(__uint_as_float(sr[32 * c + 2 * k]), __uint_as_float(sr[32 * c + 2 * k + 1])), sc2, nm2));
+            const float2 pr = (k % kPolyEvery == kPolyEvery - 1) ? ex2_poly2(a.x, a.y)
+                                                                 : make_float2(ex2(a.x), ex2(a.y));
+            rs2 = fadd2(rs2, f2(pr.x, pr.y));
+            pk[k] = pack2<kBF16>(pr.x, pr.y);
           }
           tmem_st16(tS + 16 * c, pk);
         }
+        const float2 rs = f2_split(rs2);
+        rowsum = rs.x + rs.y;
       } else {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -661,12 +671,12 @@ cudaError_t launch_fwd(const FwdParams& p, int D, bool bf16, bool has_mask, bool
 
 namespace {
 
-// out[i] = ex2_poly(x_i) / exp2f(x_i) - 1 on an even grid x_i over [lo, hi].
+// out[i] = ex2_poly2(x_i) / exp2f(x_i) - 1 on an even grid x_i over [lo, hi].
 __global__ void exp2_check_kernel(float* out, int n, float lo, float hi) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const float x = lo + (hi - lo) * (static_cast<float>(i) / static_cast<float>(n - 1));
-  out[i] = fa4d::ex2_poly(x) / exp2f(x) - 1.0f;
+  out[i] = fa4d::ex2_poly2(x, x).y / exp2f(x) - 1.0f;
 }
 
 }  // namespace

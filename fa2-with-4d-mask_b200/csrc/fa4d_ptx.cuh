@@ -307,6 +307,56 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
+// ------------------------------------------------------------------ packed fp32 pairs
+// sm_100 executes add/sub/fma on two fp32 values held in one 64-bit register pair as
+// one instruction (same rounding as the scalar forms).
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 f2_split(uint64_t v) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  return make_float2(a, b);
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// ex2_poly on two arguments with packed fp32 arithmetic; bit-identical to two calls of
+// ex2_poly (every step rounds the same way).
+__device__ __forceinline__ float2 ex2_poly2(float x0, float x1) {
+  const uint64_t x = f2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const uint64_t shift = f2(12582912.0f, 12582912.0f);
+  const uint64_t t = fadd2(x, shift);
+  const uint64_t f = fsub2(x, fsub2(t, shift));
+  uint64_t p = ffma2(f2(0.055171605f, 0.055171605f), f, f2(0.24261111f, 0.24261111f));
+  p = ffma2(p, f, f2(0.69326097f, 0.69326097f));
+  p = ffma2(p, f, f2(0.99992806f, 0.99992806f));
+  const float2 tv = f2_split(t), pv = f2_split(p);
+  const int n0 = __float_as_int(tv.x) - 0x4B400000, n1 = __float_as_int(tv.y) - 0x4B400000;
+  return make_float2(__int_as_float(__float_as_int(pv.x) + (n0 << 23)),
+                     __int_as_float(__float_as_int(pv.y) + (n1 << 23)));
+}
+
 template <bool kBF16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   if constexpr (kBF16) {
