@@ -50,7 +50,9 @@ EXPORTED_SYMBOLS = (
     "fa4d_mask_blocks_size",
     "fa4d_mask_prepare",
     "fa4d_mask_prepare_size",
+    "fa4d_check_wait_timeout",
 )
+DEV_TIMEOUT_FWD, DEV_TIMEOUT_BWD, DEV_TIMEOUT_CHECK = 1, 2, 4
 
 ABI_VERSION = 2
 BLOCK = 128  # rows / keys per block of the mask's block map
@@ -181,6 +183,8 @@ def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
         ctypes.c_void_p,
     ]
     lib.fa4d_mask_blocks.restype = ctypes.c_int
+    lib.fa4d_check_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_int64, ctypes.c_void_p]
+    lib.fa4d_check_wait_timeout.restype = ctypes.c_int
     lib.fa4d_mask_prepare_size.argtypes = [ctypes.c_int32] * 4
     lib.fa4d_mask_prepare_size.restype = ctypes.c_size_t
     lib.fa4d_mask_prepare.argtypes = lib.fa4d_mask_blocks.argtypes

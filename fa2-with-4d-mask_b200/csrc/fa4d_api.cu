@@ -305,6 +305,18 @@ int fa4d_check_exp2(float* out, int32_t n, float lo, float hi, void* stream) {
   return ok();
 }
 
+int fa4d_check_wait_timeout(int device, int64_t limit_cycles, void* stream) {
+  if (limit_cycles < 1 || limit_cycles > 1000000000LL)
+    return fail(FA4D_ERR_INVALID, "limit_cycles must be in [1, 1e9]");
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "cudaSetDevice(%d) failed: %s", device, cudaGetErrorString(e));
+  int* word = status_word_ptr();
+  if (!word) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
+  e = fa4d::launch_wait_timeout_check(word, limit_cycles, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "wait check launch failed: %s", cudaGetErrorString(e));
+  return ok();
+}
+
 int fa4d_device_status(int device, void* stream, int clear) {
   cudaError_t se = cudaSetDevice(device);
   if (se != cudaSuccess) return fail(FA4D_ERR_CUDA, "cudaSetDevice(%d) failed: %s", device, cudaGetErrorString(se));

@@ -681,7 +681,33 @@ __global__ void exp2_check_kernel(float* out, int n, float lo, float hi) {
 
 }  // namespace
 
+namespace {
+
+// A wait on an mbarrier that nothing ever completes: the same bounded wait the
+// attention kernels use must give up after `limit` clocks and report it through the
+// status word, leaving the context usable.
+__global__ void wait_timeout_check_kernel(int* status, long long limit) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    fa4d::mbar_init(&bar, 1);
+    abort_flag = 0;
+    fa4d::fence_mbar_init();
+  }
+  __syncthreads();
+  const bool done = fa4d::mbar_wait(&bar, 0, &abort_flag, limit);
+  __syncwarp();
+  if (threadIdx.x == 0 && !done && *reinterpret_cast<volatile int*>(&abort_flag))
+    atomicOr(status, FA4D_DEV_TIMEOUT_CHECK);
+}
+
+}  // namespace
+
 namespace fa4d {
+cudaError_t launch_wait_timeout_check(int* status, long long limit, cudaStream_t s) {
+  wait_timeout_check_kernel<<<1, 32, 0, s>>>(status, limit);
+  return cudaGetLastError();
+}
 cudaError_t launch_exp2_check(float* out, int n, float lo, float hi, cudaStream_t s) {
   exp2_check_kernel<<<(n + 255) / 256, 256, 0, s>>>(out, n, lo, hi);
   return cudaGetLastError();

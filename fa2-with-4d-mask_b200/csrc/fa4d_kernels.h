@@ -138,6 +138,7 @@ cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_mask_blocks(const MaskBlocksParams& p, cudaStream_t s);
 cudaError_t launch_mask_prepare(const MaskPrepParams& p, cudaStream_t s);
+cudaError_t launch_wait_timeout_check(int* status, long long limit, cudaStream_t s);
 cudaError_t launch_exp2_check(float* out, int n, float lo, float hi, cudaStream_t s);
 
 }  // namespace fa4d

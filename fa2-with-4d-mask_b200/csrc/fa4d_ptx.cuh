@@ -64,7 +64,8 @@ __device__ __forceinline__ uint32_t mbar_try_wait_sleep(uint64_t* bar, uint32_t 
 // within kWaitLimitCycles (the CTA's abort flag is then raised; the kernel reports
 // it in the device status word before exiting) or if another role of the CTA
 // already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* abort_flag,
+                                          long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   // Each try_wait blocks in hardware for a while before reporting "not yet", so the
@@ -73,7 +74,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* a
     if (mbar_try_wait(bar, parity)) return true;
     if ((n & 15u) == 0u) {
       if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
-      if (clock64() - t0 > kWaitLimitCycles) {
+      if (clock64() - t0 > limit) {
         *reinterpret_cast<volatile int*>(abort_flag) = 1;
         return false;
       }

@@ -214,7 +214,15 @@ const char* fa4d_last_error(void);
  * fails.  No counterpart in the reference (its kernels have no bounded waits). */
 #define FA4D_DEV_TIMEOUT_FWD 1
 #define FA4D_DEV_TIMEOUT_BWD 2
+#define FA4D_DEV_TIMEOUT_CHECK 4
 int fa4d_device_status(int device, void* stream, int clear);
+
+/* Diagnostic (no counterpart in the reference): runs the kernels' bounded mbarrier
+ * wait on a barrier nothing completes, with a limit of `limit_cycles` SM clocks
+ * (1..1e9), on the device that is current for the calling thread.  The wait gives up,
+ * the kernel sets FA4D_DEV_TIMEOUT_CHECK in the status word and returns; read and
+ * clear it with fa4d_device_status.  Exercises the timeout path without any fault. */
+int fa4d_check_wait_timeout(int device, int64_t limit_cycles, void* stream);
 
 /* FA4D_ABI_VERSION of the loaded library. */
 int fa4d_abi_version(void);
