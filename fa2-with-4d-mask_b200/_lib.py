@@ -51,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "fa4d_mask_prepare",
     "fa4d_mask_prepare_size",
     "fa4d_check_wait_timeout",
+    "fa4d_bwd_workspace_size_ex",
 )
 DEV_TIMEOUT_FWD, DEV_TIMEOUT_BWD, DEV_TIMEOUT_CHECK = 1, 2, 4
 
@@ -156,6 +157,8 @@ def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
     lib.fa4d_lse_row_stride.restype = ctypes.c_int64
     lib.fa4d_bwd_workspace_size.argtypes = [ctypes.c_int32] * 4
     lib.fa4d_bwd_workspace_size.restype = ctypes.c_size_t
+    lib.fa4d_bwd_workspace_size_ex.argtypes = [ctypes.c_int32] * 6
+    lib.fa4d_bwd_workspace_size_ex.restype = ctypes.c_size_t
     lib.fa4d_fwd.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
     lib.fa4d_fwd.restype = ctypes.c_int
     for name in ("fa4d_bwd", "fa4d_bwd_preprocess", "fa4d_bwd_main", "fa4d_bwd_dq_convert", "fa4d_bwd_noalloc"):
@@ -448,7 +451,7 @@ def backward(
     dq = torch.empty((B, Tq, Hq, D), dtype=q.dtype, device=q.device)
     dk = torch.empty((B, Tk, Hk, D), dtype=q.dtype, device=q.device)
     dv = torch.empty((B, Tk, Hk, D), dtype=q.dtype, device=q.device)
-    ws_bytes = int(lib.fa4d_bwd_workspace_size(B, Tq, Hq, D))
+    ws_bytes = int(lib.fa4d_bwd_workspace_size_ex(B, Tq, Tk, Hq, Hk, D))
     ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=q.device)
     a = BwdArgs()
     a.q, a.k, a.v, a.o, a.dout = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr()

@@ -205,6 +205,41 @@ int causal_offset(int causal, int Tq, int Tk) { return causal == FA4D_CAUSAL_BOT
 
 int64_t lse_ld_of(int Tq) { return (static_cast<int64_t>(Tq) + 127) / 128 * 128; }
 
+// Bytes of one set of split-group partial slices [S][B, Tk, Hk, D] fp32.
+size_t part_bytes(int S, int B, int Tk, int Hk, int D) {
+  return (static_cast<size_t>(S) * B * Tk * Hk * D * sizeof(float) + 255) / 256 * 256;
+}
+
+int sm_count();
+
+// Group split of the backward: when one CTA per (key tile, KV head, batch) would leave
+// SMs idle (MQA, short key sequences), the query-head group is split over S CTAs
+// (a power of two dividing the group size, at most 8) until the grid covers about two
+// CTAs per SM.
+int group_split(int B, int Tk, int Hq, int Hk) {
+  const int G = Hq / Hk;
+  const int64_t base = static_cast<int64_t>((Tk + 127) / 128) * Hk * B;
+  const int64_t want = 2 * static_cast<int64_t>(sm_count());
+  int S = 1;
+  while (S < 8 && G % (2 * S) == 0 && base * S < want && static_cast<int64_t>(Hk) * 2 * S <= 65535) S *= 2;
+  return S;
+}
+
+// SM count of the current device (cached per device).
+int sm_count() {
+  static std::mutex mu;
+  static int counts[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!counts[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
+
 }  // namespace
 
 extern "C" {
@@ -216,6 +251,11 @@ size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D) {
   const size_t dq_al = (dq + 255) / 256 * 256;
   const size_t delta = static_cast<size_t>(B) * Hq * lse_ld_of(Tq) * sizeof(float);
   return dq_al + (delta + 255) / 256 * 256;
+}
+
+size_t fa4d_bwd_workspace_size_ex(int32_t B, int32_t Tq, int32_t Tk, int32_t Hq, int32_t Hk, int32_t D) {
+  const int S = (B > 0 && Tk > 0 && Hq > 0 && Hk > 0 && Hq % Hk == 0) ? group_split(B, Tk, Hq, Hk) : 1;
+  return fa4d_bwd_workspace_size(B, Tq, Hq, D) + (S > 1 ? 2 * part_bytes(S, B, Tk, Hk, D) : 0);
 }
 
 const char* fa4d_last_error(void) { return g_last_error.c_str(); }
@@ -402,6 +442,7 @@ struct BwdPlan {
   fa4d::BwdParams main;
   fa4d::PrepParams prep;
   fa4d::ConvertParams convert;
+  fa4d::DkvConvertParams dkv;
   bool bf16;
   int D;
   bool has_mask, has_score;
@@ -482,6 +523,37 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
     p.mb_stride[1] = a->mask_blocks_stride[1];
   }
   if (a->score) p.score_pf = encode_bias(&p.tm_score, a->score, a->B, a->Hq, a->Tq, a->Tk, a->score_stride, 4, 64);
+  // Group split (see group_split), used when the caller's workspace was sized with
+  // fa4d_bwd_workspace_size_ex; otherwise one CTA per key tile takes the whole group.
+  p.g_split = 1;
+  {
+    const int S = group_split(a->B, a->Tk, a->Hq, a->Hk);
+    const size_t base_ws = fa4d_bwd_workspace_size(a->B, a->Tq, a->Hq, a->D);
+    const size_t pb = part_bytes(S, a->B, a->Tk, a->Hk, a->D);
+    if (S > 1 && a->workspace_bytes >= base_ws + 2 * pb) {
+      {
+        p.g_split = S;
+        p.part_stride = static_cast<int64_t>(a->B) * a->Tk * a->Hk * a->D;
+        p.dk_part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + base_ws);
+        p.dv_part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + base_ws + pb);
+        fa4d::DkvConvertParams& kp = plan->dkv;
+        kp.dk_part = p.dk_part;
+        kp.dv_part = p.dv_part;
+        kp.part_stride = p.part_stride;
+        kp.n_split = S;
+        kp.dk = a->dk;
+        kp.dv = a->dv;
+        for (int i = 0; i < 3; ++i) {
+          kp.dk_stride[i] = a->dk_stride[i];
+          kp.dv_stride[i] = a->dv_stride[i];
+        }
+        kp.B = a->B;
+        kp.Tk = a->Tk;
+        kp.Hk = a->Hk;
+        kp.D = a->D;
+      }
+    }
+  }
 
   fa4d::PrepParams& pp = plan->prep;
   pp.o = a->o;
@@ -517,12 +589,14 @@ int run_stage(const BwdPlan& plan, int stage, cudaStream_t s) {
   if (stage == 0) {
     e = fa4d::launch_bwd_prep(plan.prep, plan.bf16, s);
     what = "backward preprocess";
+
   } else if (stage == 1) {
     e = fa4d::launch_bwd(plan.main, plan.D, plan.bf16, plan.has_mask, plan.has_score, s);
     what = "backward main";
   } else {
     e = fa4d::launch_dq_convert(plan.convert, plan.bf16, s);
     what = "dQ convert";
+    if (e == cudaSuccess && plan.main.g_split > 1) e = fa4d::launch_dkv_convert(plan.dkv, plan.bf16, s);
   }
   if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
   return FA4D_OK;
@@ -610,7 +684,8 @@ int fa4d_bwd_noalloc(const fa4d_bwd_args* a, void* stream) {
   if (!scratch) return rc;
   fa4d_bwd_args b = *a;
   b.workspace = scratch;
-  b.workspace_bytes = kNoAllocScratchBytes;
+  // Sized like fa4d_bwd's basic workspace, so the call runs the same (unsplit) plan.
+  b.workspace_bytes = need;
   // The preprocess stage zeroes the dQ accumulator and writes every Delta entry, so
   // nothing left in the buffer by an earlier call reaches this one's results.
   return bwd_stages(&b, 0, 2, stream);

@@ -166,9 +166,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int k0 = blockIdx.x * 128;
-  const int hk = blockIdx.y;
+  // blockIdx.y = KV head x group split: the CTA takes query heads
+  // [h_first, h_first + G) of its KV head's group (G = Hq / Hk / g_split).
+  const int hk = blockIdx.y / p.g_split;
   const int b = blockIdx.z;
-  const int G = p.Hq / p.Hk;
+  const int G = p.Hq / p.Hk / p.g_split;
+  const int h_first = hk * (p.Hq / p.Hk) + (blockIdx.y - hk * p.g_split) * G;
 
   // Query tiles this key tile interacts with.
   int first_qt = 0;
@@ -180,7 +183,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   const int nq = max(0, num_qt_total - first_qt);
   QTiles<kMask> first;
   first.map = (kMask && p.mask_blocks)
-                  ? p.mask_blocks + b * p.mb_stride[0] + static_cast<int64_t>(hk) * G * p.mb_stride[1] + blockIdx.x
+                  ? p.mask_blocks + b * p.mb_stride[0] + static_cast<int64_t>(h_first) * p.mb_stride[1] + blockIdx.x
                   : nullptr;
   first.head_stride = p.mb_stride[1];
   first.row_stride = p.nkb;
@@ -246,7 +249,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       QTiles<kMask> cur = first;
       for (int it = 0; cur.valid(); ++it, cur.advance()) {
         const int qs = it % kQStages;
-        const int h = hk * G + cur.g();
+        const int h = h_first + cur.g();
         const int q0 = cur.q0();
         if (!mbar_wait(&q_empty[qs], ((it / kQStages) & 1) ^ 1, abort_flag)) break;
         mbar_arrive_expect_tx(&q_full[qs], 2 * L::kQT + 512);
@@ -376,7 +379,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     if (wg == 1) cur.advance();
     // Prepared mask bits of this warpgroup's next PARTIAL tile, loaded one tile ahead.
     auto load_bits = [&](const QTiles<kMask>& c) {
-      const int hh = hk * G + c.g();
+      const int hh = h_first + c.g();
       return __ldg(reinterpret_cast<const uint2*>(p.mask_bits_t + b * p.mbt_stride[0] + hh * p.mbt_stride[1]) +
                    static_cast<int64_t>(c.q0() >> 6) * p.Tk + kc);
     };
@@ -391,7 +394,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       const int st = wg;
       const uint32_t par = (it >> 1) & 1;
       const int qs = it % kQStages;
-      const int h = hk * G + cur.g();
+      const int h = h_first + cur.g();
       const int q0 = cur.q0();
       const bool use_mask = kMask && cur.state() == 1;  // warp-uniform
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], par, abort_flag) &&
@@ -506,7 +509,36 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     }
 
     // Epilogue: warpgroup 0 writes dV, warpgroup 1 writes dK (zeros when no query
-    // interacts with this key tile).
+    // interacts with this key tile).  With a split group each CTA writes its partial
+    // sums (fp32) into its own slice; dkv_convert_kernel adds the slices in order.
+    if (p.g_split > 1) {
+      const int split = blockIdx.y - hk * p.g_split;
+      float* part = (wg == 0 ? p.dv_part : p.dk_part) + split * p.part_stride +
+                    ((static_cast<int64_t>(b) * p.Tk + kc) * p.Hk + hk) * D;
+      if (any_work && ok) {
+        ok = __all_sync(0xffffffffu, mbar_wait(dkv_full, 0, abort_flag));
+        tc_fence_after();
+        const uint32_t tA = tmem + lane_base + (wg == 0 ? kColDV : kColDK);
+        const float out_scale = wg == 0 ? 1.f : p.scale;  // dK = scale * dS^T Q
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tA + 32 * c, v);
+          tmem_wait_ld();
+          if (k_valid) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              *reinterpret_cast<float4*>(part + 32 * c + 4 * u) =
+                  make_float4(__uint_as_float(v[4 * u]) * out_scale, __uint_as_float(v[4 * u + 1]) * out_scale,
+                              __uint_as_float(v[4 * u + 2]) * out_scale, __uint_as_float(v[4 * u + 3]) * out_scale);
+          }
+        }
+      } else if (k_valid && !any_work) {
+#pragma unroll
+        for (int u = 0; u < D / 4; ++u) reinterpret_cast<float4*>(part)[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      tc_fence_before();
+    } else {
     uint16_t* dst_row = nullptr;
     if (k_valid) {
       const int64_t* st3 = wg == 0 ? p.dv_stride : p.dk_stride;
@@ -538,6 +570,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       for (int u = 0; u < D / 8; ++u) reinterpret_cast<uint4*>(dst_row)[u] = make_uint4(0, 0, 0, 0);
     }
     tc_fence_before();
+    }
   } else {
     regs_dec<kRegsDrain>();
     // ------------------------------------------------------------ dQ drain
@@ -551,7 +584,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     QTiles<kMask> cur = first;
     for (int it = 0; cur.valid(); ++it, cur.advance()) {
       const int st = it & 1;
-      const int h = hk * G + cur.g();
+      const int h = h_first + cur.g();
       const int q0 = cur.q0();
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&dq_full[st], (it >> 1) & 1, abort_flag));
       if (!ok) break;
@@ -636,6 +669,36 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
   if (lane == 0) p.delta[(static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t] = acc;
 }
 
+// dK, dV (input dtype, caller strides) = sum over the split slices [n_split][B, Tk, Hk,
+// D] of the split-group backward's fp32 partials (dK already scaled), added in slice
+// order so the result does not depend on scheduling; 8 elements per thread.
+template <bool kBF16>
+__global__ void __launch_bounds__(256) dkv_convert_kernel(const DkvConvertParams p) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int per_row = p.D / 8;
+  const int64_t rows = static_cast<int64_t>(p.B) * p.Tk * p.Hk;
+  if (i >= 2 * rows * per_row) return;
+  const bool is_v = i >= rows * per_row;
+  const int64_t j = is_v ? i - rows * per_row : i;
+  const int d8 = static_cast<int>(j % per_row);
+  const int64_t row = j / per_row;  // (b, t, h) with h fastest
+  const int h = static_cast<int>(row % p.Hk);
+  const int t = static_cast<int>((row / p.Hk) % p.Tk);
+  const int b = static_cast<int>(row / (static_cast<int64_t>(p.Hk) * p.Tk));
+  const float* base = (is_v ? p.dv_part : p.dk_part) + row * p.D + d8 * 8;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
+  for (int sidx = 0; sidx < p.n_split; ++sidx) {
+    const float4* src = reinterpret_cast<const float4*>(base + sidx * p.part_stride);
+    const float4 x = src[0], y = src[1];
+    a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+    c.x += y.x; c.y += y.y; c.z += y.z; c.w += y.w;
+  }
+  const int64_t* st = is_v ? p.dv_stride : p.dk_stride;
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(is_v ? p.dv : p.dk) + b * st[0] +
+                                        static_cast<int64_t>(t) * st[1] + h * st[2] + d8 * 8);
+  *dst = make_uint4(pack2<kBF16>(a.x, a.y), pack2<kBF16>(a.z, a.w), pack2<kBF16>(c.x, c.y), pack2<kBF16>(c.z, c.w));
+}
+
 // dQ (input dtype, caller strides) = scale * dq_acc [B, Hq, lse_ld, D], 8 elements per thread.
 template <bool kBF16>
 __global__ void __launch_bounds__(256) dq_convert_kernel(const ConvertParams p) {
@@ -665,7 +728,7 @@ cudaError_t launch_bwd_t(const BwdParams& p, cudaStream_t s) {
   auto kern = bwd_kernel<D, kBF16, kMask, kScore>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return e;
-  dim3 grid((p.Tk + 127) / 128, p.Hk, p.B);
+  dim3 grid((p.Tk + 127) / 128, p.Hk * p.g_split, p.B);
   kern<<<grid, kBwdThreads, L::kAlloc, s>>>(p);
   return cudaGetLastError();
 }
@@ -700,6 +763,14 @@ cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s) {
   } else {
     return cudaErrorInvalidValue;
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dkv_convert(const DkvConvertParams& p, bool bf16, cudaStream_t s) {
+  const int64_t total = 2 * static_cast<int64_t>(p.B) * p.Tk * p.Hk * (p.D / 8);
+  const int64_t blocks = (total + 255) / 256;
+  if (bf16) dkv_convert_kernel<true><<<blocks, 256, 0, s>>>(p);
+  else dkv_convert_kernel<false><<<blocks, 256, 0, s>>>(p);
   return cudaGetLastError();
 }
 

@@ -85,6 +85,26 @@ struct BwdParams {
   // tm_score (dims (Tk, Tq, H or 1, B or 1), box (32, 64)).
   int32_t score_pf;
   CUtensorMap tm_score;
+  // Group split: g_split CTAs share one key tile, each taking Hq/Hk/g_split query heads
+  // of the group; with g_split > 1 each writes its fp32 partial dK, dV into slice
+  // `split` of [g_split][B, Tk, Hk, D] (part_stride elements per slice) instead of dk / dv.
+  int32_t g_split;
+  float* dk_part;
+  float* dv_part;
+  int64_t part_stride;
+};
+
+// dK, dV (input dtype, caller strides) from the split-group partial slices.
+struct DkvConvertParams {
+  const float* dk_part;
+  const float* dv_part;
+  int64_t part_stride;
+  int32_t n_split;
+  void* dk;
+  void* dv;
+  int64_t dk_stride[3];
+  int64_t dv_stride[3];
+  int32_t B, Tk, Hk, D;
 };
 
 // Block-occupancy pre-pass: blocks[((b * Hm + h) * nqb + qb) * nkb + kb] =
@@ -136,6 +156,7 @@ cudaError_t launch_fwd(const FwdParams& p, int D, bool bf16, bool has_mask, bool
 cudaError_t launch_bwd(const BwdParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);
 cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s);
+cudaError_t launch_dkv_convert(const DkvConvertParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_mask_blocks(const MaskBlocksParams& p, cudaStream_t s);
 cudaError_t launch_mask_prepare(const MaskPrepParams& p, cudaStream_t s);
 cudaError_t launch_wait_timeout_check(int* status, long long limit, cudaStream_t s);

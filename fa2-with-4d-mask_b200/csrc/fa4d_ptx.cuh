@@ -384,6 +384,12 @@ __device__ __forceinline__ void red_add_f32(float* addr, float v) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }
 
+// Element-wise fp32 add of 4 values into global memory, performed in L2.
+__device__ __forceinline__ void red_add_v4_f32(float* gdst, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gdst), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
 // ------------------------------------------------------------------ mask bits
 // Keep flags (nonzero = keep) of the 4 bytes of w as bits 0..3.
 __device__ __forceinline__ uint32_t keep_bits4(uint32_t w) {

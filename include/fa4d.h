@@ -130,6 +130,16 @@ int64_t fa4d_lse_row_stride(int32_t Tq);
  * Delta [B, Hq, fa4d_lse_row_stride(Tq)]. */
 size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D);
 
+/* Workspace bytes including the backward's group-split buffers.  When one CTA per
+ * (key tile, KV head, batch) would leave SMs idle (MQA, short key sequences), fa4d_bwd
+ * splits each KV head's query-head group over S CTAs (S a power of two, at most 8,
+ * chosen from the sizes and the current device's SM count); each writes its fp32
+ * partial dK/dV into its own slice and the slices are added in a fixed order, so the
+ * result does not depend on scheduling.  A workspace of fa4d_bwd_workspace_size()
+ * bytes (no room for the slices) makes fa4d_bwd run unsplit.  Returns
+ * fa4d_bwd_workspace_size() when no split would be used. */
+size_t fa4d_bwd_workspace_size_ex(int32_t B, int32_t Tq, int32_t Tk, int32_t Hq, int32_t Hk, int32_t D);
+
 /* Forward: O = softmax(((Q K^T + score) * scale) masked) V and LSE.
  * Replaces the launch of flash_attention_fwd_with_4d_mask at
  * python/fa2.py:474-478 (kernel python/fa2.py:22-139). */
