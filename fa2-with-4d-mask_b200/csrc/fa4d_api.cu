@@ -183,6 +183,8 @@ int check_common(int B, int Tq, int Tk, int Hq, int Hk, int D, int dtype, int ca
   if (Hq % Hk != 0)
     return fail(FA4D_ERR_INVALID, "query heads (%d) must be divisible by key/value heads (%d)", Hq, Hk);
   if (B > 65535 || Hq > 65535) return fail(FA4D_ERR_INVALID, "B and Hq must be <= 65535");
+  if ((Tq + 255) / 256 > 65535 || (Tk + 127) / 128 > 65535)
+    return fail(FA4D_ERR_UNSUPPORTED, "sequence too long for the launch grid (Tq <= 16M, Tk <= 8M)");
   if (Tq > (1 << 30) || Tk > (1 << 30)) return fail(FA4D_ERR_INVALID, "sequence length too large");
   if (D != 64 && D != 128) return fail(FA4D_ERR_UNSUPPORTED, "head dim %d is not built (64, 128)", D);
   if (dtype != FA4D_BF16 && dtype != FA4D_F16) return fail(FA4D_ERR_INVALID, "dtype %d is not bf16/f16", dtype);

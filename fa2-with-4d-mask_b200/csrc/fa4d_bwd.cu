@@ -165,13 +165,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int k0 = blockIdx.x * 128;
-  // blockIdx.y = KV head x group split: the CTA takes query heads
+  // Grid (Hk x group split, key tiles, B), dispatched x-fastest: all heads of one key
+  // tile go out together, and under a causal mask the first key tiles (which see the
+  // most queries) go first.  blockIdx.x = KV head x split: the CTA takes query heads
   // [h_first, h_first + G) of its KV head's group (G = Hq / Hk / g_split).
-  const int hk = blockIdx.y / p.g_split;
+  const int kb = blockIdx.y;
+  const int k0 = kb * 128;
+  const int hk = blockIdx.x / p.g_split;
+  const int split = blockIdx.x - hk * p.g_split;
   const int b = blockIdx.z;
   const int G = p.Hq / p.Hk / p.g_split;
-  const int h_first = hk * (p.Hq / p.Hk) + (blockIdx.y - hk * p.g_split) * G;
+  const int h_first = hk * (p.Hq / p.Hk) + split * G;
 
   // Query tiles this key tile interacts with.
   int first_qt = 0;
@@ -183,7 +187,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   const int nq = max(0, num_qt_total - first_qt);
   QTiles<kMask> first;
   first.map = (kMask && p.mask_blocks)
-                  ? p.mask_blocks + b * p.mb_stride[0] + static_cast<int64_t>(h_first) * p.mb_stride[1] + blockIdx.x
+                  ? p.mask_blocks + b * p.mb_stride[0] + static_cast<int64_t>(h_first) * p.mb_stride[1] + kb
                   : nullptr;
   first.head_stride = p.mb_stride[1];
   first.row_stride = p.nkb;
@@ -512,7 +516,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     // interacts with this key tile).  With a split group each CTA writes its partial
     // sums (fp32) into its own slice; dkv_convert_kernel adds the slices in order.
     if (p.g_split > 1) {
-      const int split = blockIdx.y - hk * p.g_split;
       float* part = (wg == 0 ? p.dv_part : p.dk_part) + split * p.part_stride +
                     ((static_cast<int64_t>(b) * p.Tk + kc) * p.Hk + hk) * D;
       if (any_work && ok) {
@@ -728,7 +731,7 @@ cudaError_t launch_bwd_t(const BwdParams& p, cudaStream_t s) {
   auto kern = bwd_kernel<D, kBF16, kMask, kScore>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return e;
-  dim3 grid((p.Tk + 127) / 128, p.Hk * p.g_split, p.B);
+  dim3 grid(p.Hk * p.g_split, (p.Tk + 127) / 128, p.B);
   kern<<<grid, kBwdThreads, L::kAlloc, s>>>(p);
   return cudaGetLastError();
 }

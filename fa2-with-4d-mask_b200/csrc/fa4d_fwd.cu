@@ -165,8 +165,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qblk = p.causal ? static_cast<int>(gridDim.x - 1 - blockIdx.x) : static_cast<int>(blockIdx.x);
-  const int h = blockIdx.y;
+  // Grid (Hq, query blocks, B): CTAs are dispatched x-fastest, so all heads of one
+  // query block go out together; causal runs the longest blocks (last rows) first.
+  const int qblk = p.causal ? static_cast<int>(gridDim.y - 1 - blockIdx.y) : static_cast<int>(blockIdx.y);
+  const int h = blockIdx.x;
   const int b = blockIdx.z;
   const int hk = h / (p.Hq / p.Hk);
   const int q0 = qblk * 256;
@@ -644,7 +646,7 @@ cudaError_t launch_fwd_t(const FwdParams& p, cudaStream_t s) {
   auto kern = fwd_kernel<D, kBF16, kMask, kScore>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return e;
-  dim3 grid((p.Tq + 255) / 256, p.Hq, p.B);
+  dim3 grid(p.Hq, (p.Tq + 255) / 256, p.B);
   kern<<<grid, kFwdThreads, L::kAlloc, s>>>(p);
   return cudaGetLastError();
 }
