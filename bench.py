@@ -168,7 +168,11 @@ def _run_ours(args, _lib):
     ev = lambda: torch.cuda.Event(enable_timing=True)
     rec = {"fwd": [], "preprocess": [], "main": [], "dq_convert": [], "step": []}
 
-    def step(timed):
+    def step(timed, events=True):
+        if not events:  # the step as captured into the CUDA graph
+            o, lse = _lib.forward(q, k, v, None, None, scale, _lib.CAUSAL_NONE)
+            _lib.backward(do, q, k, v, o, lse, None, None, scale, _lib.CAUSAL_NONE)
+            return o
         e0, e1 = ev(), ev()
         e0.record(stream)
         o, lse = _lib.forward(q, k, v, None, None, scale, _lib.CAUSAL_NONE)
@@ -194,12 +198,30 @@ def _run_ours(args, _lib):
     for _ in range(args.warmup):
         step(False)
     torch.cuda.synchronize(dev)
+    # Per-kernel times: eager launches with events around each stage.
+    for _ in range(min(args.steps, 10)):
+        flush.zero_()
+        step(True)
+    torch.cuda.synchronize(dev)
+    # The timed steps replay the step (fwd + the 3 backward launches) as one CUDA
+    # graph, so host-side launch work cannot leave gaps between the kernels.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        o = step(False, events=False)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
     if dist:
         dist.barrier()
     torch.cuda.synchronize(dev)
+    steps_ev = []
     for _ in range(args.steps):
         flush.zero_()  # L2 flush between steps, outside the step's events
-        o = step(True)
+        a, b = ev(), ev()
+        a.record(stream)
+        graph.replay()
+        b.record(stream)
+        steps_ev.append((a, b))
     torch.cuda.synchronize(dev)
     if dist:
         dist.barrier()
@@ -207,6 +229,8 @@ def _run_ours(args, _lib):
     clocks = sampler.stop() if sampler else None
 
     ms = {k2: sum(a.elapsed_time(b) for a, b in v2) / max(1, len(v2)) for k2, v2 in rec.items()}
+    ms["step_eager"] = ms.pop("step")
+    ms["step"] = sum(a.elapsed_time(b) for a, b in steps_ev) / len(steps_ev)
     step_ms = torch.tensor([ms["step"]], device=dev, dtype=torch.float64)
     if dist:
         dist.all_reduce(step_ms, op=dist.ReduceOp.MAX)
@@ -259,7 +283,9 @@ def _run_ours(args, _lib):
         "fwd_tflops": round(fwd_tflops, 2),
         "fwd_frac_of_peak": round(fwd_tflops / peak, 4),
         "fwd_bwd_frac_of_peak": round(value / world / peak, 4),
-        "kernel_ms": {k2: round(v2, 4) for k2, v2 in ms.items() if k2 != "step"},
+        "kernel_ms": {k2: round(v2, 4) for k2, v2 in ms.items() if k2 not in ("step", "step_eager")},
+        "step_ms_eager_launches": round(ms["step_eager"], 4),
+        "timing": "CUDA events around each timed step, which replays the step as one captured CUDA graph",
         "roofline": {
             "kernel": "bwd_kernel<128,bf16> (fa4d_bwd_main)",
             "bound": "tensor",

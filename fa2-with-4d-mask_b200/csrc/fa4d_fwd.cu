@@ -139,6 +139,28 @@ __device__ __forceinline__ int next_union(const SlotTiles<kMask>& s0, const Slot
   return kt;
 }
 
+// Keep bits of keys kbase..kbase+127 of one mask row read as bytes (the path without
+// prepared bits).  Kept out of line so its loads do not raise the register pressure
+// of the softmax loop.
+__device__ __noinline__ uint4 mask_words_from_bytes(const uint8_t* row, int kbase, int Tk, int vec) {
+  uint32_t w[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int kc = kbase + 32 * c;
+    uint32_t x = 0u;
+    // kc is the same for every lane, so these branches are warp-uniform.
+    if (vec && kc + 31 < Tk) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) x |= keep_bits4(__ldg(reinterpret_cast<const unsigned int*>(row + kc) + u)) << (4 * u);
+    } else {
+      for (int e = 0; e < 32; ++e)
+        if (kc + e < Tk) x |= (__ldg(row + kc + e) != 0 ? 1u : 0u) << e;
+    }
+    w[c] = x;
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 template <int D, bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_constant__ FwdParams p) {
   using L = FwdLayout<D, kMask, kScore>;
@@ -458,32 +480,36 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       } else {
         if (kMask && use_mask && !bits_row) {
           // No prepared bits: read this row's 128 mask bytes from global memory.
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int kc = kbase + 32 * c;
-            uint32_t w = 0u;
-            // kc is the same for every lane, so these branches are warp-uniform.
-            if (p.mask_vec && kc + 31 < p.Tk) {
-#pragma unroll
-              for (int u = 0; u < 8; ++u)
-                w |= keep_bits4(__ldg(reinterpret_cast<const unsigned int*>(mask_row + kc) + u)) << (4 * u);
-            } else {
-#pragma unroll
-              for (int e = 0; e < 32; ++e)
-                if (kc + e < p.Tk) w |= (__ldg(mask_row + kc + e) != 0 ? 1u : 0u) << e;
-            }
-            mw[c] = w;
-          }
+          const uint4 v = mask_words_from_bytes(mask_row, kbase, p.Tk, p.mask_vec);
+          mw[0] = v.x;
+          mw[1] = v.y;
+          mw[2] = v.z;
+          mw[3] = v.w;
         }
         if (need_bounds || need_causal) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) mw[c] &= low_bits(key_lim - (kbase + 32 * c));
         }
         float m4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
+        // x = (s + score) * scale, -inf where the keep bit is clear; the score is
+        // consumed four values at a time so few registers are live beside S.
+        auto apply4 = [&](int e0, float a0, float a1, float a2, float a3, uint32_t w) {
+          const float av[4] = {a0, a1, a2, a3};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int e = e0 + j;
+            float x = __uint_as_float(sr[e]);
+            if constexpr (kScore) x += av[j];
+            x *= p.scale_log2;
+            x = ((w >> (e & 31)) & 1u) ? x : kNegInf;
+            sr[e] = __float_as_uint(x);
+            m4[j] = fmaxf(m4[j], x);
+          }
+        };
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int kc = kbase + 32 * c;
-          float add[32];
+          const uint32_t w = mw[c];
           if constexpr (kScore) {
             if (p.bias_tma) {
               const int e = g % R;
@@ -492,10 +518,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
 #pragma unroll
               for (int u = 0; u < 8; ++u) {
                 const float4 v = lds_f4(ring_row + e * kRingEntry + ((u ^ sw) << 4));
-                add[4 * u] = v.x;
-                add[4 * u + 1] = v.y;
-                add[4 * u + 2] = v.z;
-                add[4 * u + 3] = v.w;
+                apply4(32 * c + 4 * u, v.x, v.y, v.z, v.w, w);
               }
               mbar_arrive(&empty[e]);
               ++g;
@@ -503,25 +526,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
 #pragma unroll
               for (int u = 0; u < 8; ++u) {
                 const float4 v = __ldg(reinterpret_cast<const float4*>(score_row + kc) + u);
-                add[4 * u] = v.x;
-                add[4 * u + 1] = v.y;
-                add[4 * u + 2] = v.z;
-                add[4 * u + 3] = v.w;
+                apply4(32 * c + 4 * u, v.x, v.y, v.z, v.w, w);
               }
             } else {
 #pragma unroll
-              for (int e = 0; e < 32; ++e) add[e] = (kc + e < p.Tk) ? __ldg(score_row + kc + e) : 0.f;
+              for (int u = 0; u < 8; ++u) {
+                const int k4 = kc + 4 * u;
+                apply4(32 * c + 4 * u, (k4 < p.Tk) ? __ldg(score_row + k4) : 0.f,
+                       (k4 + 1 < p.Tk) ? __ldg(score_row + k4 + 1) : 0.f,
+                       (k4 + 2 < p.Tk) ? __ldg(score_row + k4 + 2) : 0.f,
+                       (k4 + 3 < p.Tk) ? __ldg(score_row + k4 + 3) : 0.f, w);
+              }
             }
-          }
-          const uint32_t w = mw[c];
+          } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            float x = __uint_as_float(sr[32 * c + e]);
-            if constexpr (kScore) x += add[e];
-            x *= p.scale_log2;
-            x = ((w >> e) & 1u) ? x : kNegInf;
-            sr[32 * c + e] = __float_as_uint(x);
-            m4[e & 3] = fmaxf(m4[e & 3], x);
+            for (int u = 0; u < 8; ++u) apply4(32 * c + 4 * u, 0.f, 0.f, 0.f, 0.f, w);
           }
         }
         if (!ok) break;
