@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "fa4d_mask_prepare_size",
     "fa4d_check_wait_timeout",
     "fa4d_bwd_workspace_size_ex",
+    "fa4d_mask_prepare_docs",
 )
 DEV_TIMEOUT_FWD, DEV_TIMEOUT_BWD, DEV_TIMEOUT_CHECK = 1, 2, 4
 
@@ -192,6 +193,17 @@ def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
     lib.fa4d_mask_prepare_size.restype = ctypes.c_size_t
     lib.fa4d_mask_prepare.argtypes = lib.fa4d_mask_blocks.argtypes
     lib.fa4d_mask_prepare.restype = ctypes.c_int
+    lib.fa4d_mask_prepare_docs.argtypes = [
+        ctypes.c_void_p,
+        ctypes.c_void_p,
+        ctypes.POINTER(ctypes.c_int64),
+        ctypes.c_int32,
+        ctypes.c_int32,
+        ctypes.c_int32,
+        ctypes.c_void_p,
+        ctypes.c_void_p,
+    ]
+    lib.fa4d_mask_prepare_docs.restype = ctypes.c_int
     version = lib.fa4d_abi_version()
     if version != ABI_VERSION:
         raise RuntimeError(f"{p}: ABI version {version}, expected {ABI_VERSION}; rebuild with build.py")
@@ -364,14 +376,41 @@ def mask_prepare(mask: torch.Tensor) -> PreparedMask:
     return PreparedMask(buf, Bm, Hm, Tq, Tk)
 
 
+def mask_prepare_docs(doc_q: torch.Tensor, doc_k: torch.Tensor, batch: int) -> PreparedMask:
+    """Runs ``fa4d_mask_prepare_docs``: the prepared mask of per-token document ids
+    doc_q [B|1, Tq] and doc_k [B|1, Tk] (keep iff equal and >= 0), for batch ``batch``."""
+    lib = load_library()
+    if doc_q.dim() != 2 or doc_k.dim() != 2:
+        raise ValueError("document ids must be [B or 1, T] tensors")
+    doc_q = doc_q.to(torch.int32)
+    doc_k = doc_k.to(torch.int32)
+    if doc_q.stride(1) != 1:
+        doc_q = doc_q.contiguous()
+    if doc_k.stride(1) != 1:
+        doc_k = doc_k.contiguous()
+    Tq, Tk = doc_q.shape[1], doc_k.shape[1]
+    st = (ctypes.c_int64 * 2)(0 if doc_q.shape[0] == 1 else doc_q.stride(0), 0 if doc_k.shape[0] == 1 else doc_k.stride(0))
+    nbytes = int(lib.fa4d_mask_prepare_size(batch, 1, Tq, Tk))
+    buf = torch.empty((nbytes,), dtype=torch.uint8, device=doc_q.device)
+    with torch.cuda.device(doc_q.device):
+        rc = lib.fa4d_mask_prepare_docs(doc_q.data_ptr(), doc_k.data_ptr(), st, batch, Tq, Tk, buf.data_ptr(),
+                                        _stream_ptr(doc_q.device))
+    if rc != FA4D_OK:
+        _raise(lib, rc, "fa4d_mask_prepare_docs")
+    return PreparedMask(buf, batch, 1, Tq, Tk)
+
+
 def _set_blocks(a, mask: Optional[torch.Tensor], blocks) -> None:
-    """Attaches a BlockMap (map only) or a PreparedMask (map + bits) to the args."""
+    """Attaches a BlockMap (map only) or a PreparedMask (map + bits) to the args; a
+    PreparedMask without a mask tensor is a document-id preparation."""
     a.mask_blocks = None
     a.mask_prepared = None
-    if mask is None or blocks is None:
+    if blocks is None:
         return
     if isinstance(blocks, PreparedMask):
         a.mask_prepared = blocks.buffer.data_ptr()
+    elif mask is None:
+        return
     else:
         a.mask_blocks = blocks.blocks.data_ptr()
         a.mask_blocks_stride = (ctypes.c_int64 * 2)(*blocks.strides)

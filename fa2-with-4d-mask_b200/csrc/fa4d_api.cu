@@ -304,6 +304,39 @@ int fa4d_mask_prepare(const uint8_t* mask, const int64_t mask_stride[3], int32_t
   return ok();
 }
 
+int fa4d_mask_prepare_docs(const int32_t* doc_q, const int32_t* doc_k, const int64_t doc_stride[2], int32_t Bm,
+                           int32_t Tq, int32_t Tk, void* prepared, void* stream) {
+  if (!doc_q || !doc_k || !doc_stride || !prepared)
+    return fail(FA4D_ERR_INVALID, "doc_q, doc_k, doc_stride and prepared are required");
+  if (Bm < 1 || Tq < 1 || Tk < 1) return fail(FA4D_ERR_INVALID, "sizes must be positive (Bm=%d Tq=%d Tk=%d)", Bm, Tq, Tk);
+  if (Bm > 65535 || nblocks(Tq) > 65535) return fail(FA4D_ERR_UNSUPPORTED, "Bm and ceil(Tq/128) must be <= 65535");
+  if (doc_stride[0] < 0 || doc_stride[1] < 0) return fail(FA4D_ERR_INVALID, "doc strides must be non-negative");
+  if (!aligned(prepared, 256)) return fail(FA4D_ERR_LAYOUT, "prepared buffer must be 256-byte aligned");
+  int rc = bind_device_of(doc_q, "doc_q");
+  if (rc) return rc;
+  const PrepLayout L = prep_layout(Bm, 1, Tq, Tk);
+  fa4d::MaskPrepParams p;
+  memset(&p, 0, sizeof(p));
+  p.Bm = Bm;
+  p.Hm = 1;
+  p.Tq = Tq;
+  p.Tk = Tk;
+  p.nqb = L.nqb;
+  p.nkb = L.nkb;
+  p.nqt = L.nqt;
+  p.doc_q = doc_q;
+  p.doc_k = doc_k;
+  p.doc_q_stride = doc_stride[0];
+  p.doc_k_stride = doc_stride[1];
+  char* base = static_cast<char*>(prepared);
+  p.blocks = reinterpret_cast<uint8_t*>(base + L.blocks);
+  p.row_bits = reinterpret_cast<uint32_t*>(base + L.row_bits);
+  p.col_bits = reinterpret_cast<uint32_t*>(base + L.col_bits);
+  cudaError_t e = fa4d::launch_mask_prepare(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "document mask prepare launch failed: %s", cudaGetErrorString(e));
+  return ok();
+}
+
 size_t fa4d_mask_blocks_size(int32_t Bm, int32_t Hm, int32_t Tq, int32_t Tk) {
   if (Bm < 1 || Hm < 1 || Tq < 1 || Tk < 1) return 0;
   return static_cast<size_t>(Bm) * Hm * nblocks(Tq) * nblocks(Tk);
@@ -414,11 +447,13 @@ int fa4d_fwd(const fa4d_fwd_args* a, void* stream) {
   p.status = status_word_ptr();
   if (!p.status) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
   p.nkb = nblocks(a->Tk);
-  if (a->mask && a->mask_prepared) {
+  if (a->mask_prepared) {
     if (!aligned(a->mask_prepared, 256)) return fail(FA4D_ERR_LAYOUT, "mask_prepared must be 256-byte aligned");
-    const int Bm = a->mask_stride[0] ? a->B : 1, Hm = a->mask_stride[1] ? a->Hq : 1;
+    // Without a mask pointer the buffer came from fa4d_mask_prepare_docs: Bm = B, Hm = 1.
+    const int Bm = (!a->mask || a->mask_stride[0]) ? a->B : 1, Hm = (a->mask && a->mask_stride[1]) ? a->Hq : 1;
     const PrepLayout L = use_prepared_map(p, a->mask_prepared, Bm, Hm, a->Tq, a->Tk);
     p.mask_bits = reinterpret_cast<const uint32_t*>(static_cast<const char*>(a->mask_prepared) + L.row_bits);
+    p.empty_rows_zero = a->mask == nullptr;
     const int64_t per_head = static_cast<int64_t>(L.nkb) * a->Tq * 4;
     p.mbits_stride[0] = Bm > 1 ? per_head * Hm : 0;
     p.mbits_stride[1] = Hm > 1 ? per_head : 0;
@@ -430,7 +465,7 @@ int fa4d_fwd(const fa4d_fwd_args* a, void* stream) {
   if (a->score) {
     p.bias_tma = encode_bias(&p.tm_score, a->score, a->B, a->Hq, a->Tq, a->Tk, a->score_stride, 4);
   }
-  cudaError_t e = fa4d::launch_fwd(p, a->D, bf16, a->mask != nullptr, a->score != nullptr,
+  cudaError_t e = fa4d::launch_fwd(p, a->D, bf16, a->mask != nullptr || a->mask_prepared != nullptr, a->score != nullptr,
                                    static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "forward launch failed: %s", cudaGetErrorString(e));
   return ok();
@@ -479,7 +514,7 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   memset(plan, 0, sizeof(*plan));
   plan->bf16 = bf16;
   plan->D = a->D;
-  plan->has_mask = a->mask != nullptr;
+  plan->has_mask = a->mask != nullptr || a->mask_prepared != nullptr;
   plan->has_score = a->score != nullptr;
   fa4d::BwdParams& p = plan->main;
   if ((rc = encode_bthd(&p.tm_q, a->q, a->B, a->Tq, a->Hq, a->D, a->q_stride, 64, bf16, "q"))) return rc;
@@ -511,9 +546,9 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   p.scale = a->scale;
   p.status = status;
   p.nkb = nblocks(a->Tk);
-  if (a->mask && a->mask_prepared) {
+  if (a->mask_prepared) {
     if (!aligned(a->mask_prepared, 256)) return fail(FA4D_ERR_LAYOUT, "mask_prepared must be 256-byte aligned");
-    const int Bm = a->mask_stride[0] ? a->B : 1, Hm = a->mask_stride[1] ? a->Hq : 1;
+    const int Bm = (!a->mask || a->mask_stride[0]) ? a->B : 1, Hm = (a->mask && a->mask_stride[1]) ? a->Hq : 1;
     const PrepLayout L = use_prepared_map(p, a->mask_prepared, Bm, Hm, a->Tq, a->Tk);
     p.mask_bits_t = reinterpret_cast<const uint32_t*>(static_cast<const char*>(a->mask_prepared) + L.col_bits);
     const int64_t per_head = static_cast<int64_t>(L.nqt) * a->Tk * 2;

@@ -622,7 +622,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     if (i > 0 && ok) {
       ok = __all_sync(0xffffffffu, mbar_wait(&o_full[t], 0, abort_flag));
       tc_fence_after();
-      const float inv_l = 1.f / l_run;  // l == 0 (no valid key) -> inf -> O = NaN like the oracle
+      // l == 0 (no valid key): O = NaN like the oracle (inv_l = inf, O = 0 * inf), or
+      // O = 0 in document mode.
+      const float inv_l = (l_run > 0.f || !p.empty_rows_zero) ? 1.f / l_run : 0.f;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
@@ -639,7 +641,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         }
       }
     } else if (q_valid) {
-      const uint32_t nan2 = pack2<kBF16>(NAN, NAN);
+      const uint32_t nan2 = p.empty_rows_zero ? 0u : pack2<kBF16>(NAN, NAN);
       uint4* dst = reinterpret_cast<uint4*>(o_row);
 #pragma unroll
       for (int v = 0; v < D / 8; ++v) dst[v] = make_uint4(nan2, nan2, nan2, nan2);

@@ -45,6 +45,9 @@ struct FwdParams {
   // the 128 keys of key tile kt for query row q.
   const uint32_t* mask_bits;
   int64_t mbits_stride[2];
+  // 1: rows that keep no key get O = 0 instead of NaN (document-id mode, where such
+  // rows are padding).
+  int32_t empty_rows_zero;
 };
 
 // Backward: one CTA owns 128 keys of one (batch, KV head), loops over every
@@ -125,6 +128,11 @@ struct MaskPrepParams {
   int32_t Bm, Hm, Tq, Tk, nqb, nkb;
   int32_t vec;
   int32_t nqt;        // ceil(Tq / 64)
+  // Document ids instead of mask bytes (doc_q non-null): [Bm][Tq] and [Bm][Tk] int32
+  // with batch strides; keep (q, k) iff doc_q == doc_k >= 0.
+  const int32_t* doc_q;
+  const int32_t* doc_k;
+  int64_t doc_q_stride, doc_k_stride;
   uint8_t* blocks;
   uint32_t* row_bits;
   uint32_t* col_bits;

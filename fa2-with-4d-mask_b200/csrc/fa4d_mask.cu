@@ -99,7 +99,9 @@ __device__ __forceinline__ uint32_t keep_word(const uint4& a, const uint4& b) {
 // Keys / queries past Tk / Tq read as 0.  Grid: (ceil(Tk / 512), ceil(Tq / 128),
 // Bm * Hm), 128 threads; warp w owns query rows 32w..32w+31 of the block row
 // (lane = row) and walks 16 chunks of 32 keys; column words come from one ballot per key.
-template <bool kVec>
+// Source of the keep flags: mask bytes (kVec: 16-byte loads) or per-token document
+// ids (kDocs: keep iff the query's and the key's ids are equal and not negative).
+template <bool kVec, bool kDocs>
 __global__ void __launch_bounds__(128) mask_prepare_kernel(const MaskPrepParams p) {
   __shared__ uint32_t s_any[4], s_all[4];
   const int tid = threadIdx.x;
@@ -117,7 +119,10 @@ __global__ void __launch_bounds__(128) mask_prepare_kernel(const MaskPrepParams 
     s_all[tid] = 1u;
   }
   __syncthreads();
-  const uint8_t* src = p.mask + b * p.stride[0] + h * p.stride[1] + static_cast<int64_t>(row_ok ? row : 0) * p.stride[2];
+  const uint8_t* src = kDocs ? nullptr
+                             : p.mask + b * p.stride[0] + h * p.stride[1] +
+                                   static_cast<int64_t>(row_ok ? row : 0) * p.stride[2];
+  const int32_t doc_row = (kDocs && row_ok) ? __ldg(p.doc_q + b * p.doc_q_stride + row) : -1;
   uint32_t* row_bits = p.row_bits + static_cast<int64_t>(bh) * p.nkb * p.Tq * 4;
   // This warp's 32 rows are half (q0w / 32) % 2 of query tile q0w / 64.
   const int qt = q0w >> 6;
@@ -131,7 +136,15 @@ __global__ void __launch_bounds__(128) mask_prepare_kernel(const MaskPrepParams 
     const int nin = min(max(p.Tk - kc, 0), 32);
     const uint32_t inb = nin >= 32 ? 0xffffffffu : ((1u << nin) - 1u);
     uint32_t rw = 0u;
-    if (row_ok && nin > 0) {
+    if (kDocs) {
+      // Lane j holds key kc+j's document; each row compares against all 32.
+      const int32_t doc_key = (kc + lane < p.Tk) ? __ldg(p.doc_k + b * p.doc_k_stride + kc + lane) : -2;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int32_t dk = __shfl_sync(0xffffffffu, doc_key, j);
+        if (doc_row >= 0 && dk == doc_row) rw |= 1u << j;
+      }
+    } else if (row_ok && nin > 0) {
       if (kVec) {
         // Tk % 16 == 0: each 16-byte half is entirely in or out of bounds.
         const uint4 z = make_uint4(0u, 0u, 0u, 0u);
@@ -180,10 +193,12 @@ __global__ void __launch_bounds__(128) mask_prepare_kernel(const MaskPrepParams 
 
 cudaError_t launch_mask_prepare(const MaskPrepParams& p, cudaStream_t s) {
   dim3 grid((p.Tk + 511) / 512, p.nqb, p.Bm * p.Hm);
-  if (p.vec)
-    mask_prepare_kernel<true><<<grid, 128, 0, s>>>(p);
+  if (p.doc_q)
+    mask_prepare_kernel<false, true><<<grid, 128, 0, s>>>(p);
+  else if (p.vec)
+    mask_prepare_kernel<true, false><<<grid, 128, 0, s>>>(p);
   else
-    mask_prepare_kernel<false><<<grid, 128, 0, s>>>(p);
+    mask_prepare_kernel<false, false><<<grid, 128, 0, s>>>(p);
   return cudaGetLastError();
 }
 

@@ -6,7 +6,10 @@ Drop-in for the reference op ``_flash_attention_with_4d_mask``
 output in the input layout, nine gradients (dQ, dK, dV and six ``None``).
 One optional tenth positional argument, ``causal_align`` ("top_left", the
 reference's semantics, or "bottom_right"), selects where the causal diagonal
-sits when Tq != Tk.
+sits when Tq != Tk.  An optional eleventh, ``doc_ids``, describes packed sequences
+without a mask tensor: per-token document ids ([B or 1, T] for self-attention, or a
+(doc_q, doc_k) pair); query q keeps key k iff their ids are equal and not negative,
+and query rows with a negative id (padding) produce zeros.
 
 Differences that do not change results: BHSD inputs are passed to the kernels as
 strided views instead of contiguous copies (a copy is made only when the strides
@@ -58,21 +61,27 @@ class _BlockMapCache:
         self._entries: list = []
 
     @staticmethod
-    def _key(mask: torch.Tensor) -> tuple:
-        return (mask.data_ptr(), tuple(mask.shape), tuple(mask.stride()), mask.dtype, mask.device, mask._version)
+    def _key(t: torch.Tensor) -> tuple:
+        return (t.data_ptr(), tuple(t.shape), tuple(t.stride()), t.dtype, t.device, t._version)
 
-    def get(self, mask: torch.Tensor) -> "_lib.PreparedMask":
-        owner = mask._base if mask._base is not None else mask
-        key = self._key(mask)
-        for i, (ref, k, bm) in enumerate(self._entries):
-            if k == key and ref() is owner:
+    def _lookup(self, tensors: tuple, extra, build):
+        owners = tuple(t._base if t._base is not None else t for t in tensors)
+        key = (tuple(self._key(t) for t in tensors), extra)
+        for i, (refs, k, val) in enumerate(self._entries):
+            if k == key and all(r() is o for r, o in zip(refs, owners)):
                 if i:
                     self._entries.insert(0, self._entries.pop(i))
-                return bm
-        bm = _lib.mask_prepare(mask)
-        self._entries.insert(0, (weakref.ref(owner), key, bm))
+                return val
+        val = build()
+        self._entries.insert(0, (tuple(weakref.ref(o) for o in owners), key, val))
         del self._entries[self.capacity :]
-        return bm
+        return val
+
+    def get(self, mask: torch.Tensor) -> "_lib.PreparedMask":
+        return self._lookup((mask,), None, lambda: _lib.mask_prepare(mask))
+
+    def get_docs(self, doc_q: torch.Tensor, doc_k: torch.Tensor, batch: int) -> "_lib.PreparedMask":
+        return self._lookup((doc_q, doc_k), batch, lambda: _lib.mask_prepare_docs(doc_q, doc_k, batch))
 
     def clear(self) -> None:
         self._entries.clear()
@@ -85,6 +94,27 @@ def clear_block_map_cache() -> None:
     """Drops every cached mask preparation (e.g. after writing a mask in place
     through a path that does not bump its version counter)."""
     _block_maps.clear()
+
+
+def _doc_ids(doc_ids, B: int, Tq: int, Tk: int, device) -> tuple:
+    """(doc_q [B|1, Tq], doc_k [B|1, Tk]) int32 on `device` from a [B|1, T] tensor
+    (self-attention, Tq == Tk) or a (doc_q, doc_k) pair."""
+    if isinstance(doc_ids, (tuple, list)):
+        if len(doc_ids) != 2:
+            raise ValueError("doc_ids must be a tensor or a (doc_q, doc_k) pair")
+        dq, dk = doc_ids
+    else:
+        if Tq != Tk:
+            raise ValueError("doc_ids as one tensor needs Tq == Tk; pass (doc_q, doc_k)")
+        dq = dk = doc_ids
+    out = []
+    for t, T, name in ((dq, Tq, "doc_q"), (dk, Tk, "doc_k")):
+        if not isinstance(t, torch.Tensor) or t.dim() != 2 or t.shape[1] != T or t.shape[0] not in (1, B):
+            raise ValueError(f"{name} must be an integer tensor of shape [B or 1, {T}]")
+        if t.dtype.is_floating_point or t.dtype == torch.bool:
+            raise ValueError(f"{name} must be an integer tensor")
+        out.append(t.to(device=device, dtype=torch.int32))
+    return out[0], out[1]
 
 
 def _fwd_views(Q, K, V, bhsd_input):
@@ -107,6 +137,7 @@ class _flash_attention_with_4d_mask(torch.autograd.Function):
         use_atomic_backward: Optional[bool] = True,
         bhsd_input: Optional[bool] = True,
         causal_align: str = "top_left",
+        doc_ids=None,
     ):
         assert Q.dim() == 4 and K.dim() == 4 and V.dim() == 4
         if not Q.is_cuda:
@@ -118,7 +149,13 @@ class _flash_attention_with_4d_mask(torch.autograd.Function):
         mode = causal_mode(bool(is_causal), causal_align)
         mask = _lib.prepare_bias(Mask, torch.bool) if Mask is not None else None
         score = _lib.prepare_bias(Score, torch.float32) if Score is not None else None
-        blocks = _block_maps.get(mask) if mask is not None else None
+        if doc_ids is not None:
+            if mask is not None:
+                raise ValueError("doc_ids cannot be combined with a bool mask")
+            doc_q, doc_k = _doc_ids(doc_ids, B, Tq, k.shape[1], q.device)
+            blocks = _block_maps.get_docs(doc_q, doc_k, B)
+        else:
+            blocks = _block_maps.get(mask) if mask is not None else None
         O, LSE = _lib.forward(q, k, v, mask, score, float(scale), mode, blocks=blocks)
         ctx.save_for_backward(q, k, v, O, LSE, mask, score)
         ctx.blocks = blocks
@@ -137,7 +174,7 @@ class _flash_attention_with_4d_mask(torch.autograd.Function):
         dQ, dK, dV = _lib.backward(dO, q, k, v, O, LSE, mask, score, ctx.scale, ctx.mode, blocks=ctx.blocks)
         if ctx.bhsd_input:
             dQ, dK, dV = dQ.transpose(1, 2), dK.transpose(1, 2), dV.transpose(1, 2)
-        return dQ, dK, dV, None, None, None, None, None, None, None
+        return dQ, dK, dV, None, None, None, None, None, None, None, None
 
 
 flash_attention_with_4d_mask = _flash_attention_with_4d_mask.apply

@@ -16,8 +16,11 @@ to the kernel as a stride-0 view instead of being materialised to
 ``[B, Hq, Tq, Tk]`` (the reference's ``expand().contiguous()``,
 python/modeling_attention.py:57-59); the values read are identical.
 
-Extra keyword (not in the reference): ``causal_align`` = "top_left" (default,
-the reference's ``q >= k``) or "bottom_right" (``k <= q + Tk - Tq``).
+Extra keywords (not in the reference): ``causal_align`` = "top_left" (default,
+the reference's ``q >= k``) or "bottom_right" (``k <= q + Tk - Tq``); ``doc_ids``,
+per-token document ids of packed sequences ([B or 1, T], or a (doc_q, doc_k) pair)
+used instead of a block-diagonal bool mask — the reference header advertises packed /
+right-padded inputs (python/fa2.py:1) but supports them only through a dense mask.
 """
 
 from __future__ import annotations
@@ -99,6 +102,7 @@ def tilelang_flash_attention(
     attention_mask_is_scaled: bool = True,
     use_atomic_backward: bool = True,
     causal_align: str = "top_left",
+    doc_ids=None,
 ) -> torch.Tensor:
     """FlashAttention-2 on B200 with an optional 4D bool mask and fp32 score.
 
@@ -114,6 +118,10 @@ def tilelang_flash_attention(
         attention_mask_is_scaled: divide a float ``attention_mask`` by ``scale``.
         use_atomic_backward: accepted for compatibility (one backward serves both).
         causal_align: "top_left" (reference semantics) or "bottom_right".
+        doc_ids: optional per-token document ids (int) of packed sequences, [B or 1,
+            T] or a (doc_q, doc_k) pair; keeps (q, k) with equal, non-negative ids.
+            Cannot be combined with a bool mask; a float ``attention_mask`` / score
+            still adds.  Rows with a negative id are padding and produce zeros.
 
     Returns:
         The attention output in the input layout.
@@ -166,6 +174,7 @@ def tilelang_flash_attention(
         bool(use_atomic_backward),
         layout == "bhsd",
         causal_align,
+        doc_ids,
     )
 
 
@@ -195,6 +204,7 @@ def tilelang_attention_forward(
     use_atomic_backward = kwargs.pop("use_atomic_backward", True)
     attention_mask_is_scaled = kwargs.pop("attention_mask_is_scaled", True)
     causal_align = kwargs.pop("causal_align", "top_left")
+    doc_ids = kwargs.pop("doc_ids", None)
     is_causal = kwargs.pop("is_causal", None)
     if is_causal is None:
         is_causal = attention_mask is None and bool(getattr(module, "is_causal", True))
@@ -212,6 +222,7 @@ def tilelang_attention_forward(
         attention_mask_is_scaled=attention_mask_is_scaled,
         use_atomic_backward=use_atomic_backward,
         causal_align=causal_align,
+        doc_ids=doc_ids,
     )
     return out, None
 

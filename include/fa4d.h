@@ -83,7 +83,9 @@ typedef struct fa4d_fwd_args {
    * It holds the block map and the mask as packed bits; when given, the kernels
    * skip EMPTY blocks and read the bits instead of the mask bytes, and
    * mask_blocks is ignored.  It must have been prepared with Bm = (mask_stride[0]
-   * ? B : 1) and Hm = (mask_stride[1] ? Hq : 1) and the same Tq, Tk. */
+   * ? B : 1) and Hm = (mask_stride[1] ? Hq : 1) and the same Tq, Tk.  With mask ==
+   * NULL it may instead come from fa4d_mask_prepare_docs with Bm = B: the keep flags
+   * are then those of the document ids (no mask tensor exists). */
   const void* mask_prepared;
 } fa4d_fwd_args;
 
@@ -214,6 +216,20 @@ int fa4d_mask_blocks(const uint8_t* mask, const int64_t mask_stride[3], int32_t 
 size_t fa4d_mask_prepare_size(int32_t Bm, int32_t Hm, int32_t Tq, int32_t Tk);
 int fa4d_mask_prepare(const uint8_t* mask, const int64_t mask_stride[3], int32_t Bm, int32_t Hm, int32_t Tq,
                       int32_t Tk, void* prepared, void* stream);
+
+/* Packed sequences without a mask tensor: per-token document ids doc_q [Bm, Tq] and
+ * doc_k [Bm, Tk] (int32, batch strides doc_stride[0] / doc_stride[1] in elements, 0 to
+ * broadcast one row over the batch; unit token stride) define keep(q, k) =
+ * doc_q[q] == doc_k[k] && doc_q[q] >= 0 (a negative id marks padding, which attends
+ * to nothing).  Writes the same prepared-mask buffer as fa4d_mask_prepare with
+ * Hm = 1 (fa4d_mask_prepare_size(Bm, 1, Tq, Tk) bytes), reading O(T) ids instead of
+ * O(T^2) mask bytes; pass it as mask_prepared with mask == NULL (Bm must be B).
+ * In this mode a query row that keeps no key (padding) gets O = 0 and LSE = -inf
+ * rather than the NaN a fully masked row gives, so padding adds nothing to dK / dV.
+ * The reference's header advertises right-padded / packed support
+ * (python/fa2.py:1) but implements it only through a dense 4D mask. */
+int fa4d_mask_prepare_docs(const int32_t* doc_q, const int32_t* doc_k, const int64_t doc_stride[2], int32_t Bm,
+                           int32_t Tq, int32_t Tk, void* prepared, void* stream);
 
 /* Message for the last non-zero return on this thread ("" if none). */
 const char* fa4d_last_error(void);

@@ -79,3 +79,27 @@ def fwd_bwd_flops(B, Hq, Tq, Tk, D, causal):
 
 def default_scale(D):
     return 1.0 / math.sqrt(D)
+
+
+def doc_mask(doc_q, doc_k):
+    """Bool mask [B, 1, Tq, Tk] of per-token document ids [B, Tq] / [B, Tk]: keep (q, k)
+    iff the ids are equal and not negative (negative = padding)."""
+    dq = torch.as_tensor(doc_q)
+    dk = torch.as_tensor(doc_k)
+    keep = (dq[:, :, None] == dk[:, None, :]) & (dq[:, :, None] >= 0)
+    return keep[:, None]
+
+
+def packed_doc_ids(B, T, *, min_len=128, max_len=1024, pad=0, seed=2):
+    """[B, T] int32 document ids of seeded documents with lengths uniform in
+    [min_len, max_len] (the last truncated), the final `pad` tokens of every row -1."""
+    g = gen(seed)
+    ids = torch.full((B, T), -1, dtype=torch.int32)
+    for b in range(B):
+        s, d = 0, 0
+        while s < T - pad:
+            n = int(torch.randint(min_len, max_len + 1, (1,), generator=g))
+            e = min(T - pad, s + n)
+            ids[b, s:e] = d
+            s, d = e, d + 1
+    return ids

@@ -154,3 +154,22 @@ def test_unknown_causal_align():
     assert causal_mode(True) == 1 and causal_mode(True, "bottom_right") == 2
     with pytest.raises(ValueError, match="unsupported causal_align"):
         causal_mode(True, "middle")
+
+
+def test_doc_ids_are_validated_and_forwarded(captured):
+    q, k, v = qkv(B=2, Tq=16, Tk=16)
+    ids = torch.zeros(2, 16, dtype=torch.int32)
+    api.tilelang_flash_attention(q, k, v, doc_ids=ids)
+    assert captured[-1][10] is ids
+
+
+def test_doc_id_parsing():
+    impl_fa2 = __import__("fa2_with_4d_mask_b200.fa2", fromlist=["x"])
+    dq, dk = impl_fa2._doc_ids(torch.arange(8).view(1, 8), 2, 8, 8, "cpu")
+    assert dq.dtype == torch.int32 and dq.shape == (1, 8) and dk is not None
+    with pytest.raises(ValueError, match="Tq == Tk"):
+        impl_fa2._doc_ids(torch.zeros(1, 8, dtype=torch.int64), 1, 8, 9, "cpu")
+    with pytest.raises(ValueError, match="doc_k must be"):
+        impl_fa2._doc_ids((torch.zeros(1, 8, dtype=torch.int64), torch.zeros(1, 7, dtype=torch.int64)), 1, 8, 9, "cpu")
+    with pytest.raises(ValueError, match="integer"):
+        impl_fa2._doc_ids(torch.zeros(1, 8), 1, 8, 8, "cpu")

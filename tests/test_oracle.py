@@ -7,6 +7,7 @@ import pytest
 import torch
 
 from conftest import golden_names, load_golden
+from oracle import inputs as I
 from oracle.eager import attention_ref, attention_ref_grads, bottom_right_mask, merge_wrapper_inputs
 
 # Both sides are fp32 eager math; only summation order differs.
@@ -77,3 +78,18 @@ def test_fully_masked_row_is_nan_like_softmax():
     mask[0, 0, 2] = False
     out = attention_ref(q, k, v, mask, None, scale=1.0, is_causal=False)
     assert torch.isnan(out[0, 0, 2]).all() and not torch.isnan(out[0, 0, [0, 1, 3]]).any()
+
+
+def test_doc_mask_matches_block_diagonal_construction():
+    """The document-id mask equals the packed-document mask built block by block."""
+    ids = I.packed_doc_ids(2, 300, min_len=40, max_len=90, pad=20, seed=9)
+    m = I.doc_mask(ids, ids)
+    ref = torch.zeros(2, 1, 300, 300, dtype=torch.bool)
+    for b in range(2):
+        for d in ids[b].unique().tolist():
+            if d < 0:
+                continue
+            idx = (ids[b] == d).nonzero().flatten()
+            ref[b, 0, idx.min() : idx.max() + 1, idx.min() : idx.max() + 1] = True
+    assert torch.equal(m, ref)
+    assert not m[:, :, 280:].any() and not m[:, :, :, 280:].any()
