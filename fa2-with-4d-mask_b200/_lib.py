@@ -476,6 +476,7 @@ def backward(
     causal: int,
     stages=None,
     blocks=None,
+    deterministic: bool = False,
 ) -> tuple:
     """Runs fa4d_bwd on [B, T, H, D] views.  Returns (dQ, dK, dV) contiguous in the
     input dtype, dK/dV summed over the GQA group.
@@ -483,7 +484,9 @@ def backward(
     ``stages`` optionally replaces the single fa4d_bwd call by a list of callables
     ``f(name, launch)``; each receives the stage name ("preprocess", "main",
     "dq_convert") and a zero-argument function that enqueues that stage, so a caller
-    can bracket each stage (e.g. with CUDA events)."""
+    can bracket each stage (e.g. with CUDA events).  ``deterministic`` selects the
+    bit-reproducible backward (dQ from a separate in-order pass; the third stage
+    is then that pass)."""
     lib = load_library()
     B, Tq, Hq, D = q.shape
     Tk, Hk = k.shape[1], k.shape[2]
@@ -512,7 +515,7 @@ def backward(
     a.dtype = _dtype_code(q.dtype)
     a.causal = int(causal)
     a.scale = float(scale)
-    a.deterministic = 0
+    a.deterministic = 1 if deterministic else 0
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws_bytes
     _set_blocks(a, mask, blocks)

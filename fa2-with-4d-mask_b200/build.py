@@ -23,7 +23,7 @@ INCLUDE = REPO / "include"
 BUILD = HERE / "_build"
 LIB = HERE / "libfa4d.so"
 
-SOURCES = ["fa4d_api.cu", "fa4d_fwd.cu", "fa4d_bwd.cu", "fa4d_mask.cu"]
+SOURCES = ["fa4d_api.cu", "fa4d_fwd.cu", "fa4d_bwd.cu", "fa4d_mask.cu", "fa4d_dq.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O2"]
 

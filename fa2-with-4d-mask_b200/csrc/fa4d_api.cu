@@ -477,6 +477,8 @@ namespace {
 
 struct BwdPlan {
   fa4d::BwdParams main;
+  fa4d::DqParams dq;  // deterministic mode only
+  bool deterministic;
   fa4d::PrepParams prep;
   fa4d::ConvertParams convert;
   fa4d::DkvConvertParams dkv;
@@ -492,7 +494,7 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   if (rc) return rc;
   if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse)
     return fail(FA4D_ERR_INVALID, "q, k, v, o, dout and lse are required");
-  if (a->deterministic) return fail(FA4D_ERR_UNSUPPORTED, "deterministic dQ is reserved");
+  if (a->deterministic != 0 && a->deterministic != 1) return fail(FA4D_ERR_INVALID, "deterministic must be 0 or 1");
   if ((rc = check_rows16(a->dq, a->dq_stride, "dq"))) return rc;
   if ((rc = check_rows16(a->dk, a->dk_stride, "dk"))) return rc;
   if ((rc = check_rows16(a->dv, a->dv_stride, "dv"))) return rc;
@@ -592,11 +594,60 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
     }
   }
 
+  if (a->deterministic) {
+    // dQ from its own kernel (one CTA per query tile, key tiles in order); the main
+    // kernel skips its dQ products and nothing is accumulated.
+    plan->deterministic = true;
+    p.skip_dq = 1;
+    fa4d::DqParams& d = plan->dq;
+    if ((rc = encode_bthd(&d.tm_q, a->q, a->B, a->Tq, a->Hq, a->D, a->q_stride, 128, bf16, "q"))) return rc;
+    if ((rc = encode_bthd(&d.tm_do, a->dout, a->B, a->Tq, a->Hq, a->D, a->do_stride, 128, bf16, "dout"))) return rc;
+    if ((rc = encode_bthd(&d.tm_k, a->k, a->B, a->Tk, a->Hk, a->D, a->k_stride, 128, bf16, "k"))) return rc;
+    if ((rc = encode_bthd(&d.tm_v, a->v, a->B, a->Tk, a->Hk, a->D, a->v_stride, 128, bf16, "v"))) return rc;
+    d.lse = a->lse;
+    d.delta = delta;
+    d.dq = a->dq;
+    d.mask = a->mask;
+    d.score = a->score;
+    for (int i = 0; i < 3; ++i) {
+      d.dq_stride[i] = a->dq_stride[i];
+      d.mask_stride[i] = a->mask_stride[i];
+      d.score_stride[i] = a->score_stride[i];
+    }
+    d.mask_blocks = p.mask_blocks;
+    d.mb_stride[0] = p.mb_stride[0];
+    d.mb_stride[1] = p.mb_stride[1];
+    d.nkb = p.nkb;
+    if (a->mask_prepared) {
+      const int Bm = (!a->mask || a->mask_stride[0]) ? a->B : 1, Hm = (a->mask && a->mask_stride[1]) ? a->Hq : 1;
+      const PrepLayout L = prep_layout(Bm, Hm, a->Tq, a->Tk);
+      d.mask_bits = reinterpret_cast<const uint32_t*>(static_cast<const char*>(a->mask_prepared) + L.row_bits);
+      const int64_t per_head = static_cast<int64_t>(L.nkb) * a->Tq * 4;
+      d.mbits_stride[0] = Bm > 1 ? per_head * Hm : 0;
+      d.mbits_stride[1] = Hm > 1 ? per_head : 0;
+    }
+    d.mask_vec = a->mask && aligned(a->mask, 4) && a->mask_stride[0] % 4 == 0 && a->mask_stride[1] % 4 == 0 &&
+                 a->mask_stride[2] % 4 == 0;
+    d.score_vec = a->score && aligned(a->score, 16) && a->score_stride[0] % 4 == 0 &&
+                  a->score_stride[1] % 4 == 0 && a->score_stride[2] % 4 == 0;
+    d.B = a->B;
+    d.Tq = a->Tq;
+    d.Tk = a->Tk;
+    d.Hq = a->Hq;
+    d.Hk = a->Hk;
+    d.lse_ld = static_cast<int32_t>(lse_ld);
+    d.causal = p.causal;
+    d.causal_off = p.causal_off;
+    d.scale_log2 = p.scale_log2;
+    d.scale = a->scale;
+    d.status = status;
+  }
+
   fa4d::PrepParams& pp = plan->prep;
   pp.o = a->o;
   pp.dout = a->dout;
   pp.delta = delta;
-  pp.dq_acc = dq_acc;
+  pp.dq_acc = a->deterministic ? nullptr : dq_acc;
   for (int i = 0; i < 3; ++i) {
     pp.o_stride[i] = a->o_stride[i];
     pp.do_stride[i] = a->do_stride[i];
@@ -631,8 +682,13 @@ int run_stage(const BwdPlan& plan, int stage, cudaStream_t s) {
     e = fa4d::launch_bwd(plan.main, plan.D, plan.bf16, plan.has_mask, plan.has_score, s);
     what = "backward main";
   } else {
-    e = fa4d::launch_dq_convert(plan.convert, plan.bf16, s);
-    what = "dQ convert";
+    if (plan.deterministic) {
+      e = fa4d::launch_dq(plan.dq, plan.D, plan.bf16, plan.has_mask, plan.has_score, s);
+      what = "deterministic dQ";
+    } else {
+      e = fa4d::launch_dq_convert(plan.convert, plan.bf16, s);
+      what = "dQ convert";
+    }
     if (e == cudaSuccess && plan.main.g_split > 1) e = fa4d::launch_dkv_convert(plan.dkv, plan.bf16, s);
   }
   if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));

@@ -327,9 +327,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         if (elect_one()) {
           issue_dk<D, kBF16>(tmem + kColDK, sDS + st * L::kDS, sQ + qs * L::kQT, it > 0);
           tc_commit(&q_empty[qs]);
-          // dQ^T overwrites this tile's dP^T (read before ds_full).
-          issue_dq<D, kBF16>(tmem + kColX + 64 * st, sK, sDS + st * L::kDS);
-          tc_commit(&dq_full[st]);
+          if (!p.skip_dq) {
+            // dQ^T overwrites this tile's dP^T (read before ds_full).
+            issue_dq<D, kBF16>(tmem + kColX + 64 * st, sK, sDS + st * L::kDS);
+            tc_commit(&dq_full[st]);
+          }
           tc_commit(&ds_empty[st]);
         }
         __syncwarp();
@@ -346,8 +348,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             tc_commit(&s_full[st]);
           }
           __syncwarp();
-          // dP of tile it+2 reuses X[st] once the drain has read dQ^T of tile it.
-          ok = wait(&dq_empty[st], par);
+          // dP of tile it+2 reuses X[st] once the drain has read dQ^T of tile it (at
+          // once when dQ is left to the deterministic kernel: ds_full ended the reads).
+          if (!p.skip_dq) ok = wait(&dq_empty[st], par);
           if (!ok) break;
           tc_fence_after();
           if (elect_one()) {
@@ -585,7 +588,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     const bool leader = (warp == 12 && lane == 0);
     float* stage = reinterpret_cast<float*>(smem + L::kDQs);  // [64 queries][D]
     QTiles<kMask> cur = first;
-    for (int it = 0; cur.valid(); ++it, cur.advance()) {
+    for (int it = 0; !p.skip_dq && cur.valid(); ++it, cur.advance()) {
       const int st = it & 1;
       const int h = h_first + cur.g();
       const int q0 = cur.q0();
@@ -663,11 +666,13 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    float* dq = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t) * D + lane * E;
-    if constexpr (E == 4)
-      *reinterpret_cast<float4*>(dq) = make_float4(0.f, 0.f, 0.f, 0.f);
-    else
-      *reinterpret_cast<float2*>(dq) = make_float2(0.f, 0.f);
+    if (p.dq_acc) {  // null in deterministic mode (dQ is not accumulated)
+      float* dq = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t) * D + lane * E;
+      if constexpr (E == 4)
+        *reinterpret_cast<float4*>(dq) = make_float4(0.f, 0.f, 0.f, 0.f);
+      else
+        *reinterpret_cast<float2*>(dq) = make_float2(0.f, 0.f);
+    }
   }
   if (lane == 0) p.delta[(static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t] = acc;
 }

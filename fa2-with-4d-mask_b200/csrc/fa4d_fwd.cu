@@ -29,6 +29,7 @@
 #include "fa4d.h"
 #include "fa4d_kernels.h"
 #include "fa4d_ptx.cuh"
+#include "fa4d_tiles.cuh"
 
 namespace fa4d {
 
@@ -96,69 +97,11 @@ __device__ __forceinline__ void issue_pv(uint32_t tO, uint32_t tP, uint32_t sV, 
   }
 }
 
-// Number of 128-key tiles query rows [qs, qe) need.
-__device__ __forceinline__ int kv_tiles_for(int qs, int qe, const FwdParams& p) {
-  if (qs >= p.Tq) return 0;
-  int kv_end = p.Tk;
-  if (p.causal) {
-    const long long lim = static_cast<long long>(qe) + p.causal_off;  // keys < qe + off
-    kv_end = lim < p.Tk ? static_cast<int>(lim) : p.Tk;
-  }
-  return kv_end > 0 ? (kv_end + 127) / 128 : 0;
-}
-
-// The 128-key tiles one 128-row query slot visits: the tiles below n (key bounds and
-// the causal limit) minus the EMPTY blocks of the mask's block map.
-template <bool kMask>
-struct SlotTiles {
-  const uint8_t* map;  // this slot's row of the block map, or null
-  int n;
-  // 0: skip; 1: visit and apply the mask; 2: visit, the mask keeps every key.
-  __device__ __forceinline__ int state(int kt) const {
-    if (kt >= n) return 0;
-    if (!kMask) return 2;
-    if (!map) return 1;
-    const int v = __ldg(map + kt);
-    return v == 0 ? 0 : (v == 2 ? 2 : 1);
-  }
-  __device__ __forceinline__ int next(int kt) const {
-    while (kt < n && state(kt) == 0) ++kt;
-    return kt;
-  }
-  __device__ __forceinline__ int last() const {
-    int kt = n - 1;
-    while (kt >= 0 && state(kt) == 0) --kt;
-    return kt;
-  }
-};
-
 // First tile at or after kt that either slot visits (n_max if none).
 template <bool kMask>
 __device__ __forceinline__ int next_union(const SlotTiles<kMask>& s0, const SlotTiles<kMask>& s1, int kt, int n_max) {
   while (kt < n_max && s0.state(kt) == 0 && s1.state(kt) == 0) ++kt;
   return kt;
-}
-
-// Keep bits of keys kbase..kbase+127 of one mask row read as bytes (the path without
-// prepared bits).  Kept out of line so its loads do not raise the register pressure
-// of the softmax loop.
-__device__ __noinline__ uint4 mask_words_from_bytes(const uint8_t* row, int kbase, int Tk, int vec) {
-  uint32_t w[4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int kc = kbase + 32 * c;
-    uint32_t x = 0u;
-    // kc is the same for every lane, so these branches are warp-uniform.
-    if (vec && kc + 31 < Tk) {
-#pragma unroll
-      for (int u = 0; u < 8; ++u) x |= keep_bits4(__ldg(reinterpret_cast<const unsigned int*>(row + kc) + u)) << (4 * u);
-    } else {
-      for (int e = 0; e < 32; ++e)
-        if (kc + e < Tk) x |= (__ldg(row + kc + e) != 0 ? 1u : 0u) << e;
-    }
-    w[c] = x;
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 template <int D, bool kBF16, bool kMask, bool kScore>
@@ -199,8 +142,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
   {
     const uint8_t* row = nullptr;
     if (kMask && p.mask_blocks) row = p.mask_blocks + b * p.mb_stride[0] + h * p.mb_stride[1];
-    tiles0.n = kv_tiles_for(q0, min(q0 + 128, p.Tq), p);
-    tiles1.n = kv_tiles_for(q0 + 128, min(q0 + 256, p.Tq), p);
+    tiles0.n = kv_tile_count(q0, min(q0 + 128, p.Tq), p.Tq, p.Tk, p.causal, p.causal_off);
+    tiles1.n = kv_tile_count(q0 + 128, min(q0 + 256, p.Tq), p.Tq, p.Tk, p.causal, p.causal_off);
     tiles0.map = (row && tiles0.n > 0) ? row + static_cast<int64_t>(q0 / 128) * p.nkb : nullptr;
     tiles1.map = (row && tiles1.n > 0) ? row + static_cast<int64_t>(q0 / 128 + 1) * p.nkb : nullptr;
   }

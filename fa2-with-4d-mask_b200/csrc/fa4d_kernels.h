@@ -95,6 +95,39 @@ struct BwdParams {
   float* dk_part;
   float* dv_part;
   int64_t part_stride;
+  // 1: dQ is computed by dq_kernel (deterministic mode); this kernel skips its dQ
+  // products and the drain.
+  int32_t skip_dq;
+};
+
+// Deterministic dQ: one CTA per 128-row query tile of one (batch, head) walks its key
+// tiles in order (see fa4d_dq.cu).
+struct DqParams {
+  CUtensorMap tm_q;   // dims (D, Tq, Hq, B), box (64, 128, 1, 1)
+  CUtensorMap tm_do;
+  CUtensorMap tm_k;   // dims (D, Tk, Hk, B), box (64, 128, 1, 1)
+  CUtensorMap tm_v;
+  const float* lse;
+  const float* delta;
+  void* dq;
+  int64_t dq_stride[3];
+  const uint8_t* mask;
+  const float* score;
+  int64_t mask_stride[3];
+  int64_t score_stride[3];
+  const uint8_t* mask_blocks;
+  int64_t mb_stride[2];
+  int32_t nkb;
+  const uint32_t* mask_bits;  // prepared row bits, as in FwdParams
+  int64_t mbits_stride[2];
+  int32_t mask_vec, score_vec;
+  int32_t B, Tq, Tk, Hq, Hk;
+  int32_t lse_ld;
+  int32_t causal;
+  int32_t causal_off;
+  float scale_log2;
+  float scale;
+  int* status;
 };
 
 // dK, dV (input dtype, caller strides) from the split-group partial slices.
@@ -165,6 +198,7 @@ cudaError_t launch_bwd(const BwdParams& p, int D, bool bf16, bool has_mask, bool
 cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dkv_convert(const DkvConvertParams& p, bool bf16, cudaStream_t s);
+cudaError_t launch_dq(const DqParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);
 cudaError_t launch_mask_blocks(const MaskBlocksParams& p, cudaStream_t s);
 cudaError_t launch_mask_prepare(const MaskPrepParams& p, cudaStream_t s);
 cudaError_t launch_wait_timeout_check(int* status, long long limit, cudaStream_t s);

@@ -15,9 +15,11 @@ Differences that do not change results: BHSD inputs are passed to the kernels as
 strided views instead of contiguous copies (a copy is made only when the strides
 cannot be described by a TMA tensor map), and all three gradients come back in the
 input dtype (the reference returns dQ in fp32 and lets autograd cast it,
-python/fa2.py:556).  ``use_atomic_backward`` is accepted for compatibility; both
-values run the same backward, in which dK/dV are summed over the GQA group inside
-the kernel and dQ is accumulated in fp32.
+python/fa2.py:556).  dK/dV are summed over the GQA group inside the kernel (no dK/dV
+atomics or per-head buffers for either setting).  ``use_atomic_backward=True`` (the
+default) accumulates dQ with fp32 additions in arrival order, like the reference's
+atomic kernel; ``False`` selects the bit-reproducible backward, where a separate pass
+computes dQ for each query tile by walking the key tiles in a fixed order.
 
 A bool mask is first prepared once (``fa4d_mask_prepare``): a block map (each
 128 x 128 block EMPTY, PARTIAL or FULL) that the forward and backward kernels use
@@ -171,7 +173,8 @@ class _flash_attention_with_4d_mask(torch.autograd.Function):
         if ctx.bhsd_input:
             dO = dO.transpose(1, 2)
         dO = _lib.as_tma(dO)
-        dQ, dK, dV = _lib.backward(dO, q, k, v, O, LSE, mask, score, ctx.scale, ctx.mode, blocks=ctx.blocks)
+        dQ, dK, dV = _lib.backward(dO, q, k, v, O, LSE, mask, score, ctx.scale, ctx.mode, blocks=ctx.blocks,
+                                   deterministic=ctx.use_atomic_backward is False)
         if ctx.bhsd_input:
             dQ, dK, dV = dQ.transpose(1, 2), dK.transpose(1, 2), dV.transpose(1, 2)
         return dQ, dK, dV, None, None, None, None, None, None, None, None

@@ -116,7 +116,8 @@ def tilelang_flash_attention(
         scale: softmax scale, ``head_dim ** -0.5`` by default.
         is_causal: causal attention without a materialised mask.
         attention_mask_is_scaled: divide a float ``attention_mask`` by ``scale``.
-        use_atomic_backward: accepted for compatibility (one backward serves both).
+        use_atomic_backward: True (default) accumulates dQ with fp32 additions in
+            arrival order; False gives a bit-reproducible backward.
         causal_align: "top_left" (reference semantics) or "bottom_right".
         doc_ids: optional per-token document ids (int) of packed sequences, [B or 1,
             T] or a (doc_q, doc_k) pair; keeps (q, k) with equal, non-negative ids.

@@ -115,7 +115,10 @@ typedef struct fa4d_bwd_args {
   int32_t dtype;
   int32_t causal;
   float scale;
-  int32_t deterministic;   /* reserved, must be 0 */
+  int32_t deterministic;   /* 1: bit-reproducible backward — dQ is computed by a
+                            * separate pass (one CTA per query tile walking the key
+                            * tiles in order, accumulating in tensor memory) instead
+                            * of fp32 additions in arrival order; 0: default */
   void* workspace;         /* device scratch, >= fa4d_bwd_workspace_size() bytes, 256-B aligned */
   size_t workspace_bytes;
   const uint8_t* mask_blocks;      /* optional, as in fa4d_fwd_args */

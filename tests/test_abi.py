@@ -113,14 +113,14 @@ def test_null_args_pointer():
     assert lib.fa4d_bwd(None, None) == _lib.FA4D_ERR_INVALID
 
 
-def test_bwd_rejects_reserved_flag_and_small_workspace():
+def test_bwd_rejects_bad_flag_and_small_workspace():
     lib = _lib.load_library()
     a = _lib.BwdArgs()
     a.q = a.k = a.v = a.o = a.dout = a.lse = a.dq = a.dk = a.dv = 0x1000
     a.B, a.Tq, a.Tk, a.Hq, a.Hk, a.D = 1, 128, 128, 2, 1, 128
     a.dtype, a.causal, a.scale = _lib.FA4D_BF16, 0, 0.088
-    a.deterministic = 1
-    assert lib.fa4d_bwd(ctypes.byref(a), None) == _lib.FA4D_ERR_UNSUPPORTED
+    a.deterministic = 2
+    assert lib.fa4d_bwd(ctypes.byref(a), None) == _lib.FA4D_ERR_INVALID
     a.deterministic = 0
     a.workspace, a.workspace_bytes = 0x1000, 16
     assert lib.fa4d_bwd(ctypes.byref(a), None) == _lib.FA4D_ERR_WORKSPACE
