@@ -304,6 +304,7 @@ def _run_ours(args, _lib):
     }
     if args.extra and world == 1:
         line["extra"] = extra_measurements(_lib, dev, peaks)
+        line["extra"]["library_context_cfg2"] = library_context(dev, peaks)
     if e2e is not None:
         line["e2e"] = e2e
     if world == 1 and not args.no_cpu_baseline:
@@ -377,7 +378,7 @@ def extra_measurements(_lib, dev, peaks):
     out = {}
     peak = peaks["bf16_tflops"]
 
-    def fb(b, tq, tk, hq, hk, d, causal_mode, mask=None, score=None, iters=5):
+    def fb(b, tq, tk, hq, hk, d, causal_mode, mask=None, score=None, iters=5, deterministic=False):
         """(fwd ms, bwd ms) with the mask prepared once beforehand (block map + packed bits,
         as the op caches it per mask); the preparation itself is timed by map_ms()."""
         q, k, v, do = (x.transpose(1, 2) for x in _dev_inputs(dev, b, tq, tk, hq, hk, d, seed=3))
@@ -385,7 +386,8 @@ def extra_measurements(_lib, dev, peaks):
         bm = _lib.mask_prepare(mask) if mask is not None else None
         tf = time_fn(lambda: _lib.forward(q, k, v, mask, score, sc, causal_mode, blocks=bm), iters)
         o, lse = _lib.forward(q, k, v, mask, score, sc, causal_mode, blocks=bm)
-        tb = time_fn(lambda: _lib.backward(do, q, k, v, o, lse, mask, score, sc, causal_mode, blocks=bm), iters)
+        tb = time_fn(lambda: _lib.backward(do, q, k, v, o, lse, mask, score, sc, causal_mode, blocks=bm,
+                                           deterministic=deterministic), iters)
         return tf, tb
 
     def map_ms(mask):
@@ -397,6 +399,10 @@ def extra_measurements(_lib, dev, peaks):
                           "fwd_bwd_ms": round(tf + tb, 4), "fwd_bwd_tflops": round(fbf / (tf + tb) / 1e9, 1),
                           "fwd_frac": round(ff / tf / 1e9 / peak, 4),
                           "fwd_bwd_frac": round(fbf / (tf + tb) / 1e9 / peak, 4)}
+    tf, tb = fb(B, T, T, HQ, HK, D, _lib.CAUSAL_NONE, iters=3, deterministic=True)
+    fbf = fwd_bwd_flops(B, HQ, T, T, D, False)
+    out["cfg2_deterministic_bwd"] = {"fwd_bwd_ms": round(tf + tb, 4), "bwd_ms": round(tb, 4),
+                                     "fwd_bwd_tflops": round(fbf / (tf + tb) / 1e9, 1)}
     # cfg4: ALiBi-style fp32 score + Bernoulli(0.9) bool mask, MHA, non-causal (HBM-bound)
     b4, t4, h4 = 1, 4096, 16
     score = _alibi_score(dev, b4, h4, t4, t4)
@@ -428,8 +434,64 @@ def extra_measurements(_lib, dev, peaks):
     # cfg5: MQA, bshd, bottom-right causal, one GPU's shard of 16 (B=2)
     tf, tb = fb(2, 1024, 4096, 64, 1, 64, _lib.CAUSAL_BOTTOM_RIGHT, iters=3)
     ff, fbf = fwd_flops(2, 64, 1024, 4096, 64, True), fwd_bwd_flops(2, 64, 1024, 4096, 64, True)
+    tbd = fb(2, 1024, 4096, 64, 1, 64, _lib.CAUSAL_BOTTOM_RIGHT, iters=3, deterministic=True)[1]
     out["cfg5_mqa_shard_b2"] = {"fwd_ms": round(tf, 4), "fwd_bwd_ms": round(tf + tb, 4),
-                                "fwd_bwd_tflops_convention": round(fbf / (tf + tb) / 1e9, 1)}
+                                "fwd_bwd_tflops_convention": round(fbf / (tf + tb) / 1e9, 1),
+                                "fwd_bwd_ms_use_atomic_backward_false": round(tf + tbd, 4)}
+    return out
+
+
+def library_context(dev, peaks):
+    """Context only (not this library's work): the same config-2 shape through torch's
+    scaled_dot_product_attention (whatever backend torch picks on this GPU) and, when
+    it loads and runs on this GPU, flash_attn 2.x — fwd and fwd+bwd, non-causal and
+    causal, bf16, CUDA events, median of 5 after 2 warm-ups."""
+    out = {}
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    mk = lambda shape: torch.randn(shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    q, k, v, do = mk((B, T, HQ, D)), mk((B, T, HK, D)), mk((B, T, HK, D)), mk((B, T, HQ, D))
+
+    def measure(run_fwd, name):
+        res = {}
+        for causal in (False, True):
+            c = 0.5 if causal else 1.0
+            try:
+                tf = time_fn(lambda: run_fwd(causal, False), 5)
+                tfb = time_fn(lambda: run_fwd(causal, True), 5)
+            except Exception as exc:  # context only: report and go on
+                res["error"] = f"{type(exc).__name__}: {str(exc)[:160]}"
+                break
+            tag = "causal" if causal else "noncausal"
+            res[f"{tag}_fwd_tflops"] = round(4.0 * B * HQ * T * T * D * c / tf / 1e9, 1)
+            res[f"{tag}_fwd_bwd_tflops"] = round(14.0 * B * HQ * T * T * D * c / tfb / 1e9, 1)
+        out[name] = res
+
+    import torch.nn.functional as F
+
+    qb, kb, vb, dob = (x.transpose(1, 2) for x in (q, k, v, do))
+
+    def sdpa(causal, backward):
+        if not backward:
+            with torch.no_grad():
+                return F.scaled_dot_product_attention(qb, kb, vb, is_causal=causal, enable_gqa=True)
+        qq, kk, vv = (x.detach().requires_grad_(True) for x in (qb, kb, vb))
+        F.scaled_dot_product_attention(qq, kk, vv, is_causal=causal, enable_gqa=True).backward(dob)
+
+    measure(sdpa, "torch_sdpa")
+    try:
+        from flash_attn import flash_attn_func
+    except Exception as exc:
+        out["flash_attn"] = {"error": f"import failed: {type(exc).__name__}"}
+    else:
+        def fa(causal, backward):
+            if not backward:
+                with torch.no_grad():
+                    return flash_attn_func(q, k, v, causal=causal)
+            qq, kk, vv = (x.detach().requires_grad_(True) for x in (q, k, v))
+            flash_attn_func(qq, kk, vv, causal=causal).backward(do)
+
+        measure(fa, "flash_attn")
     return out
 
 
