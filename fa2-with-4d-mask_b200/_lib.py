@@ -433,13 +433,20 @@ def forward(
     scale: float,
     causal: int,
     blocks=None,
+    out: Optional[torch.Tensor] = None,
 ) -> tuple:
     """Runs fa4d_fwd (with the mask's BlockMap or PreparedMask when given).  q: [B, Tq, Hq, D] view, k/v: [B, Tk, Hk, D] views (TMA-friendly).
-    Returns (O [B, Tq, Hq, D] contiguous, LSE [B, Hq, lse_row_stride(Tq)] fp32)."""
+    Returns (O [B, Tq, Hq, D], LSE [B, Hq, lse_row_stride(Tq)] fp32); O is ``out`` when
+    given (any [B, Tq, Hq, D] view with 16-byte aligned rows), else a new tensor."""
     lib = load_library()
     B, Tq, Hq, D = q.shape
     Tk, Hk = k.shape[1], k.shape[2]
-    o = torch.empty((B, Tq, Hq, D), dtype=q.dtype, device=q.device)
+    if out is not None:
+        if tuple(out.shape) != (B, Tq, Hq, D) or out.dtype != q.dtype or out.device != q.device:
+            raise ValueError(f"out must be a {q.dtype} tensor of shape {(B, Tq, Hq, D)} on {q.device}")
+        o = out
+    else:
+        o = torch.empty((B, Tq, Hq, D), dtype=q.dtype, device=q.device)
     lse = torch.empty((B, Hq, lse_row_stride(Tq)), dtype=torch.float32, device=q.device)
     a = FwdArgs()
     a.q, a.k, a.v, a.o, a.lse = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr()
@@ -477,22 +484,29 @@ def backward(
     stages=None,
     blocks=None,
     deterministic: bool = False,
+    grads: Optional[tuple] = None,
 ) -> tuple:
-    """Runs fa4d_bwd on [B, T, H, D] views.  Returns (dQ, dK, dV) contiguous in the
-    input dtype, dK/dV summed over the GQA group.
+    """Runs fa4d_bwd on [B, T, H, D] views.  Returns (dQ, dK, dV) in the input
+    dtype, dK/dV summed over the GQA group.
 
     ``stages`` optionally replaces the single fa4d_bwd call by a list of callables
     ``f(name, launch)``; each receives the stage name ("preprocess", "main",
     "dq_convert") and a zero-argument function that enqueues that stage, so a caller
     can bracket each stage (e.g. with CUDA events).  ``deterministic`` selects the
     bit-reproducible backward (dQ from a separate in-order pass; the third stage
-    is then that pass)."""
+    is then that pass).  ``grads`` optionally gives the (dQ, dK, dV) output views
+    to write into (16-byte aligned rows), as ``out`` does for the forward."""
     lib = load_library()
     B, Tq, Hq, D = q.shape
     Tk, Hk = k.shape[1], k.shape[2]
-    dq = torch.empty((B, Tq, Hq, D), dtype=q.dtype, device=q.device)
-    dk = torch.empty((B, Tk, Hk, D), dtype=q.dtype, device=q.device)
-    dv = torch.empty((B, Tk, Hk, D), dtype=q.dtype, device=q.device)
+    shapes = ((B, Tq, Hq, D), (B, Tk, Hk, D), (B, Tk, Hk, D))
+    if grads is not None:
+        for g, shp, name in zip(grads, shapes, ("dq", "dk", "dv")):
+            if tuple(g.shape) != shp or g.dtype != q.dtype or g.device != q.device:
+                raise ValueError(f"{name} must be a {q.dtype} tensor of shape {shp} on {q.device}")
+        dq, dk, dv = grads
+    else:
+        dq, dk, dv = (torch.empty(shp, dtype=q.dtype, device=q.device) for shp in shapes)
     ws_bytes = int(lib.fa4d_bwd_workspace_size_ex(B, Tq, Tk, Hq, Hk, D))
     ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=q.device)
     a = BwdArgs()

@@ -177,6 +177,12 @@ PrepLayout use_prepared_map(P& p, const void* prepared, int Bm, int Hm, int Tq, 
   return L;
 }
 
+// Width the kernels compute at for head dim D.  D = 96 runs the D = 128 kernels: the
+// tensor maps (extent 96) zero-fill columns 96..127 of every Q, K, V and dO tile, so
+// those columns of S contribute nothing and those of O, dQ, dK, dV come out zero; the
+// kernels store only the first 96.  Accumulator workspaces use the compute width.
+int compute_dim(int D) { return D == 96 ? 128 : D; }
+
 int check_common(int B, int Tq, int Tk, int Hq, int Hk, int D, int dtype, int causal, float scale) {
   if (B < 1 || Tq < 1 || Tk < 1 || Hq < 1 || Hk < 1)
     return fail(FA4D_ERR_INVALID, "sizes must be positive (B=%d Tq=%d Tk=%d Hq=%d Hk=%d)", B, Tq, Tk, Hq, Hk);
@@ -186,7 +192,7 @@ int check_common(int B, int Tq, int Tk, int Hq, int Hk, int D, int dtype, int ca
   if ((Tq + 255) / 256 > 65535 || (Tk + 127) / 128 > 65535)
     return fail(FA4D_ERR_UNSUPPORTED, "sequence too long for the launch grid (Tq <= 16M, Tk <= 8M)");
   if (Tq > (1 << 30) || Tk > (1 << 30)) return fail(FA4D_ERR_INVALID, "sequence length too large");
-  if (D != 64 && D != 128) return fail(FA4D_ERR_UNSUPPORTED, "head dim %d is not built (64, 128)", D);
+  if (D != 64 && D != 96 && D != 128) return fail(FA4D_ERR_UNSUPPORTED, "head dim %d is not built (64, 96, 128)", D);
   if (dtype != FA4D_BF16 && dtype != FA4D_F16) return fail(FA4D_ERR_INVALID, "dtype %d is not bf16/f16", dtype);
   if (causal < FA4D_CAUSAL_NONE || causal > FA4D_CAUSAL_BOTTOM_RIGHT)
     return fail(FA4D_ERR_INVALID, "causal mode %d is unknown", causal);
@@ -249,7 +255,7 @@ extern "C" {
 int64_t fa4d_lse_row_stride(int32_t Tq) { return lse_ld_of(Tq); }
 
 size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D) {
-  const size_t dq = static_cast<size_t>(B) * Hq * lse_ld_of(Tq) * D * sizeof(float);
+  const size_t dq = static_cast<size_t>(B) * Hq * lse_ld_of(Tq) * compute_dim(D) * sizeof(float);
   const size_t dq_al = (dq + 255) / 256 * 256;
   const size_t delta = static_cast<size_t>(B) * Hq * lse_ld_of(Tq) * sizeof(float);
   return dq_al + (delta + 255) / 256 * 256;
@@ -257,7 +263,7 @@ size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D) {
 
 size_t fa4d_bwd_workspace_size_ex(int32_t B, int32_t Tq, int32_t Tk, int32_t Hq, int32_t Hk, int32_t D) {
   const int S = (B > 0 && Tk > 0 && Hq > 0 && Hk > 0 && Hq % Hk == 0) ? group_split(B, Tk, Hq, Hk) : 1;
-  return fa4d_bwd_workspace_size(B, Tq, Hq, D) + (S > 1 ? 2 * part_bytes(S, B, Tk, Hk, D) : 0);
+  return fa4d_bwd_workspace_size(B, Tq, Hq, D) + (S > 1 ? 2 * part_bytes(S, B, Tk, Hk, compute_dim(D)) : 0);
 }
 
 const char* fa4d_last_error(void) { return g_last_error.c_str(); }
@@ -465,8 +471,9 @@ int fa4d_fwd(const fa4d_fwd_args* a, void* stream) {
   if (a->score) {
     p.bias_tma = encode_bias(&p.tm_score, a->score, a->B, a->Hq, a->Tq, a->Tk, a->score_stride, 4);
   }
-  cudaError_t e = fa4d::launch_fwd(p, a->D, bf16, a->mask != nullptr || a->mask_prepared != nullptr, a->score != nullptr,
-                                   static_cast<cudaStream_t>(stream));
+  p.d_out = a->D;
+  cudaError_t e = fa4d::launch_fwd(p, compute_dim(a->D), bf16, a->mask != nullptr || a->mask_prepared != nullptr,
+                                   a->score != nullptr, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "forward launch failed: %s", cudaGetErrorString(e));
   return ok();
 }
@@ -508,14 +515,15 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   const bool bf16 = a->dtype == FA4D_BF16;
   const int64_t lse_ld = lse_ld_of(a->Tq);
   float* dq_acc = static_cast<float*>(a->workspace);
-  const size_t dq_bytes = static_cast<size_t>(a->B) * a->Hq * lse_ld * a->D * sizeof(float);
+  const int Dc = compute_dim(a->D);
+  const size_t dq_bytes = static_cast<size_t>(a->B) * a->Hq * lse_ld * Dc * sizeof(float);
   float* delta = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + (dq_bytes + 255) / 256 * 256);
   int* status = status_word_ptr();
   if (!status) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
 
   memset(plan, 0, sizeof(*plan));
   plan->bf16 = bf16;
-  plan->D = a->D;
+  plan->D = Dc;
   plan->has_mask = a->mask != nullptr || a->mask_prepared != nullptr;
   plan->has_score = a->score != nullptr;
   fa4d::BwdParams& p = plan->main;
@@ -526,6 +534,7 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   p.lse = a->lse;
   p.delta = delta;
   p.dq_acc = dq_acc;
+  p.d_out = a->D;
   p.dk = a->dk;
   p.dv = a->dv;
   p.mask = a->mask;
@@ -568,11 +577,11 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   {
     const int S = group_split(a->B, a->Tk, a->Hq, a->Hk);
     const size_t base_ws = fa4d_bwd_workspace_size(a->B, a->Tq, a->Hq, a->D);
-    const size_t pb = part_bytes(S, a->B, a->Tk, a->Hk, a->D);
+    const size_t pb = part_bytes(S, a->B, a->Tk, a->Hk, Dc);
     if (S > 1 && a->workspace_bytes >= base_ws + 2 * pb) {
       {
         p.g_split = S;
-        p.part_stride = static_cast<int64_t>(a->B) * a->Tk * a->Hk * a->D;
+        p.part_stride = static_cast<int64_t>(a->B) * a->Tk * a->Hk * Dc;
         p.dk_part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + base_ws);
         p.dv_part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + base_ws + pb);
         fa4d::DkvConvertParams& kp = plan->dkv;
@@ -589,7 +598,8 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
         kp.B = a->B;
         kp.Tk = a->Tk;
         kp.Hk = a->Hk;
-        kp.D = a->D;
+        kp.D = Dc;
+        kp.d_out = a->D;
       }
     }
   }
@@ -607,6 +617,7 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
     d.lse = a->lse;
     d.delta = delta;
     d.dq = a->dq;
+    d.d_out = a->D;
     d.mask = a->mask;
     d.score = a->score;
     for (int i = 0; i < 3; ++i) {
@@ -655,7 +666,8 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   pp.B = a->B;
   pp.Tq = a->Tq;
   pp.Hq = a->Hq;
-  pp.D = a->D;
+  pp.D = Dc;
+  pp.d_out = a->D;
   pp.lse_ld = static_cast<int32_t>(lse_ld);
 
   fa4d::ConvertParams& cp = plan->convert;
@@ -665,7 +677,8 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   cp.B = a->B;
   cp.Tq = a->Tq;
   cp.Hq = a->Hq;
-  cp.D = a->D;
+  cp.D = Dc;
+  cp.d_out = a->D;
   cp.lse_ld = static_cast<int32_t>(lse_ld);
   cp.scale = a->scale;
   return FA4D_OK;

@@ -561,7 +561,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         uint32_t v[32];
         tmem_ld32(tA + 32 * c, v);
         tmem_wait_ld();
-        if (k_valid) {
+        if (k_valid && 32 * c < p.d_out) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
@@ -573,7 +573,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       }
     } else if (k_valid && !any_work) {
 #pragma unroll
-      for (int u = 0; u < D / 8; ++u) reinterpret_cast<uint4*>(dst_row)[u] = make_uint4(0, 0, 0, 0);
+      for (int u = 0; u < D / 8; ++u)
+        if (8 * u < p.d_out) reinterpret_cast<uint4*>(dst_row)[u] = make_uint4(0, 0, 0, 0);
     }
     tc_fence_before();
     }
@@ -634,8 +635,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   }
 }
 
-// Delta[b, h, t] = sum_d O * dO (0 for padding rows) and zeroing of the dQ accumulator
-// row (b, h, t), layout [B, Hq, lse_ld, D].  One warp per (b, t, h).
+// Delta[b, h, t] = sum over the d_out columns of O * dO (0 for padding rows) and
+// zeroing of the dQ accumulator row (b, h, t), layout [B, Hq, lse_ld, D] with D the
+// compute width.  One warp per (b, t, h).
 template <int D, bool kBF16>
 __global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
   const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -647,7 +649,7 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
   const int b = static_cast<int>(w / (static_cast<int64_t>(p.Hq) * p.lse_ld));
   constexpr int E = D / 32;  // elements per lane (2 or 4)
   float acc = 0.f;
-  if (t < p.Tq) {
+  if (t < p.Tq && lane * E < p.d_out) {
     const uint16_t* o = reinterpret_cast<const uint16_t*>(p.o) + b * p.o_stride[0] +
                         static_cast<int64_t>(t) * p.o_stride[1] + h * p.o_stride[2] + lane * E;
     const uint16_t* g = reinterpret_cast<const uint16_t*>(p.dout) + b * p.do_stride[0] +
@@ -664,6 +666,8 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
       const float2 o0 = unpack2<kBF16>(ov), g0 = unpack2<kBF16>(gv);
       acc = o0.x * g0.x + o0.y * g0.y;
     }
+  }
+  if (t < p.Tq) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
     if (p.dq_acc) {  // null in deterministic mode (dQ is not accumulated)
@@ -683,7 +687,7 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
 template <bool kBF16>
 __global__ void __launch_bounds__(256) dkv_convert_kernel(const DkvConvertParams p) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int per_row = p.D / 8;
+  const int per_row = p.d_out / 8;
   const int64_t rows = static_cast<int64_t>(p.B) * p.Tk * p.Hk;
   if (i >= 2 * rows * per_row) return;
   const bool is_v = i >= rows * per_row;
@@ -711,7 +715,7 @@ __global__ void __launch_bounds__(256) dkv_convert_kernel(const DkvConvertParams
 template <bool kBF16>
 __global__ void __launch_bounds__(256) dq_convert_kernel(const ConvertParams p) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int per_row = p.D / 8;
+  const int per_row = p.d_out / 8;
   const int64_t total = static_cast<int64_t>(p.B) * p.Tq * p.Hq * per_row;
   if (i >= total) return;
   const int d8 = static_cast<int>(i % per_row);
@@ -775,7 +779,7 @@ cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s) {
 }
 
 cudaError_t launch_dkv_convert(const DkvConvertParams& p, bool bf16, cudaStream_t s) {
-  const int64_t total = 2 * static_cast<int64_t>(p.B) * p.Tk * p.Hk * (p.D / 8);
+  const int64_t total = 2 * static_cast<int64_t>(p.B) * p.Tk * p.Hk * (p.d_out / 8);
   const int64_t blocks = (total + 255) / 256;
   if (bf16) dkv_convert_kernel<true><<<blocks, 256, 0, s>>>(p);
   else dkv_convert_kernel<false><<<blocks, 256, 0, s>>>(p);
@@ -783,7 +787,7 @@ cudaError_t launch_dkv_convert(const DkvConvertParams& p, bool bf16, cudaStream_
 }
 
 cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s) {
-  const int64_t total = static_cast<int64_t>(p.B) * p.Tq * p.Hq * (p.D / 8);
+  const int64_t total = static_cast<int64_t>(p.B) * p.Tq * p.Hq * (p.d_out / 8);
   const int64_t blocks = (total + 255) / 256;
   if (bf16) dq_convert_kernel<true><<<blocks, 256, 0, s>>>(p);
   else dq_convert_kernel<false><<<blocks, 256, 0, s>>>(p);

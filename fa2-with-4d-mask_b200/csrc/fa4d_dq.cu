@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
         uint32_t v[32];
         tmem_ld32(tmem + lane_base + kColDQ + 32 * c, v);
         tmem_wait_ld();
-        if (q_valid) {
+        if (q_valid && 32 * c < p.d_out) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
@@ -334,7 +334,8 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
       }
     } else if (q_valid) {
 #pragma unroll
-      for (int w = 0; w < D / 8; ++w) reinterpret_cast<uint4*>(dst)[w] = make_uint4(0u, 0u, 0u, 0u);
+      for (int w = 0; w < D / 8; ++w)
+        if (8 * w < p.d_out) reinterpret_cast<uint4*>(dst)[w] = make_uint4(0u, 0u, 0u, 0u);
     }
     tc_fence_before();
   }

@@ -573,7 +573,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         uint32_t o[32];
         tmem_ld32(tO + 32 * c, o);
         tmem_wait_ld();
-        if (q_valid) {
+        if (q_valid && 32 * c < p.d_out) {
           uint32_t pk[16];
 #pragma unroll
           for (int k = 0; k < 16; ++k)
@@ -587,7 +587,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       const uint32_t nan2 = p.empty_rows_zero ? 0u : pack2<kBF16>(NAN, NAN);
       uint4* dst = reinterpret_cast<uint4*>(o_row);
 #pragma unroll
-      for (int v = 0; v < D / 8; ++v) dst[v] = make_uint4(nan2, nan2, nan2, nan2);
+      for (int v = 0; v < D / 8; ++v)
+        if (8 * v < p.d_out) dst[v] = make_uint4(nan2, nan2, nan2, nan2);
     }
     if (q_valid) {
       const float lse = (l_run > 0.f) ? (__log2f(l_run) + m_run) : kNegInf;

@@ -48,6 +48,9 @@ struct FwdParams {
   // 1: rows that keep no key get O = 0 instead of NaN (document-id mode, where such
   // rows are padding).
   int32_t empty_rows_zero;
+  // Head dim of the tensors (<= the kernel's compute width D; the tensor maps zero-fill
+  // columns d_out..D-1, so those columns compute zeros and are not stored).
+  int32_t d_out;
 };
 
 // Backward: one CTA owns 128 keys of one (batch, KV head), loops over every
@@ -98,6 +101,7 @@ struct BwdParams {
   // 1: dQ is computed by dq_kernel (deterministic mode); this kernel skips its dQ
   // products and the drain.
   int32_t skip_dq;
+  int32_t d_out;  // head dim of dK / dV (as in FwdParams); dq_acc and the slices use D
 };
 
 // Deterministic dQ: one CTA per 128-row query tile of one (batch, head) walks its key
@@ -128,6 +132,7 @@ struct DqParams {
   float scale_log2;
   float scale;
   int* status;
+  int32_t d_out;  // head dim of dQ (as in FwdParams)
 };
 
 // dK, dV (input dtype, caller strides) from the split-group partial slices.
@@ -140,7 +145,8 @@ struct DkvConvertParams {
   void* dv;
   int64_t dk_stride[3];
   int64_t dv_stride[3];
-  int32_t B, Tk, Hk, D;
+  int32_t B, Tk, Hk, D;  // D: row length of the slices (the compute width)
+  int32_t d_out;         // head dim of dK / dV
 };
 
 // Block-occupancy pre-pass: blocks[((b * Hm + h) * nqb + qb) * nkb + kb] =
@@ -179,8 +185,9 @@ struct PrepParams {
   float* dq_acc;
   int64_t o_stride[3];
   int64_t do_stride[3];
-  int32_t B, Tq, Hq, D;
+  int32_t B, Tq, Hq, D;  // D: row length of dq_acc (the compute width)
   int32_t lse_ld;
+  int32_t d_out;         // head dim of O / dO
 };
 
 // dQ (input dtype, caller strides) = dQ accumulator [B, Hq, lse_ld, D].
@@ -188,9 +195,10 @@ struct ConvertParams {
   const float* dq_acc;
   void* dq;
   int64_t dq_stride[3];
-  int32_t B, Tq, Hq, D;
+  int32_t B, Tq, Hq, D;  // D: row length of dq_acc (the compute width)
   int32_t lse_ld;
   float scale;
+  int32_t d_out;         // head dim of dQ
 };
 
 cudaError_t launch_fwd(const FwdParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);

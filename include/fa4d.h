@@ -43,7 +43,7 @@ enum fa4d_causal { FA4D_CAUSAL_NONE = 0, FA4D_CAUSAL_TOP_LEFT = 1, FA4D_CAUSAL_B
 enum fa4d_status {
   FA4D_OK = 0,
   FA4D_ERR_INVALID = -1,     /* bad pointer, shape, stride or enum value */
-  FA4D_ERR_UNSUPPORTED = -2, /* valid but not built: head dim not in {64, 128} */
+  FA4D_ERR_UNSUPPORTED = -2, /* valid but not built: head dim not in {64, 96, 128} */
   FA4D_ERR_CUDA = -3,        /* a CUDA runtime call or kernel launch failed */
   FA4D_ERR_DRIVER = -4,      /* cuTensorMapEncodeTiled unavailable or failed */
   FA4D_ERR_LAYOUT = -5,      /* strides/base not 16-byte aligned for TMA: pass a contiguous copy */
@@ -131,8 +131,9 @@ typedef struct fa4d_bwd_args {
 int64_t fa4d_lse_row_stride(int32_t Tq);
 
 /* Bytes of device scratch fa4d_bwd needs: an fp32 dQ accumulator
- * [B, Hq, fa4d_lse_row_stride(Tq), D] and the fp32 row dot products
- * Delta [B, Hq, fa4d_lse_row_stride(Tq)]. */
+ * [B, Hq, fa4d_lse_row_stride(Tq), Dc] and the fp32 row dot products
+ * Delta [B, Hq, fa4d_lse_row_stride(Tq)], where Dc is the width the kernels compute
+ * at (D, except 128 for D = 96). */
 size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D);
 
 /* Workspace bytes including the backward's group-split buffers.  When one CTA per

@@ -39,6 +39,8 @@ CASES = [
          mask="random_full"),
     dict(name="bottom_right_rect", B=1, Tq=64, Tk=200, Hq=2, Hk=1, D=64, bottom_right=True),
     dict(name="mqa_causal_d128", B=1, Tq=72, Tk=72, Hq=3, Hk=1, D=128, is_causal=True),
+    dict(name="score_causal_d96", B=1, Tq=80, Tk=136, Hq=2, Hk=1, D=96, is_causal=True, score="randn_full",
+         mask="random_h1"),
 ]
 
 
@@ -131,6 +133,7 @@ def make_case(c: dict, eager_ref, wrapper_mod) -> dict:
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--reference", default="/root/reference", help="reference source tree")
+    ap.add_argument("--only", nargs="*", help="write only these cases (each case has its own seed)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from benchmark.precision_check import eager_ref  # noqa: E402  (reference oracle)
@@ -143,6 +146,8 @@ def main() -> int:
 
     torch.manual_seed(0)
     for c in CASES:
+        if args.only and c["name"] not in args.only:
+            continue
         rec = make_case(c, eager_ref, wrapper_mod)
         path = HERE / f"{c['name']}.npz"
         np.savez_compressed(path, **rec)

@@ -76,6 +76,8 @@ def test_host_size_helpers():
     delta = 1 * 32 * 8192 * 4
     assert lib.fa4d_bwd_workspace_size(1, 8192, 32, 128) == dq + delta
     assert lib.fa4d_bwd_workspace_size(1, 1, 1, 64) % 256 == 0
+    # Head dim 96 computes at width 128: its dQ accumulator rows hold 128 floats.
+    assert lib.fa4d_bwd_workspace_size(1, 8192, 32, 96) == lib.fa4d_bwd_workspace_size(1, 8192, 32, 128)
 
 
 def _fwd_args(**kw):
@@ -91,7 +93,8 @@ def _fwd_args(**kw):
 @pytest.mark.parametrize(
     "kw,code",
     [
-        (dict(D=96), _lib.FA4D_ERR_UNSUPPORTED),
+        (dict(D=80), _lib.FA4D_ERR_UNSUPPORTED),
+        (dict(D=256), _lib.FA4D_ERR_UNSUPPORTED),
         (dict(Hq=3, Hk=2), _lib.FA4D_ERR_INVALID),
         (dict(B=0), _lib.FA4D_ERR_INVALID),
         (dict(dtype=7), _lib.FA4D_ERR_INVALID),

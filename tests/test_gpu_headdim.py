@@ -1,0 +1,92 @@
+"""GPU: head dim 96 against the oracle, through the public API.
+
+D = 96 runs the D = 128 kernels on tiles whose columns 96..127 the tensor maps fill
+with zeros; only the first 96 columns of O, dQ, dK and dV are stored.  The cases cover
+each kernel variant that this reaches (dense, causal, GQA, bool mask + fp32 score,
+document ids, the split-group and deterministic backward, fp16, BSHD with bottom-right
+causal), plus a direct check that nothing is written past column 96 of each output row.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import inputs as I
+from test_gpu_parity import DEV, _fp32_oracle_and_status, check, oracle, run_api  # noqa: F401
+
+from fa2_with_4d_mask_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+D = 96
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_dense_gqa_odd_length(causal):
+    q, k, v, do = I.qkv(2, 333, 333, 8, 2, D, seed=90)
+    check(run_api(q, k, v, do, is_causal=causal), oracle(q, k, v, do, causal=causal, device="cpu"), f"D96 c={causal}")
+
+
+def test_longer_sequence_causal():
+    q, k, v, do = I.qkv(1, 2048, 2048, 8, 2, D, seed=91)
+    check(run_api(q, k, v, do, is_causal=True), oracle(q, k, v, do, causal=True), "D96 T2048")
+
+
+def test_mask_and_score():
+    B, T, H = 1, 640, 4
+    q, k, v, do = I.qkv(B, T, T, H, H, D, seed=92)
+    mask = I.random_mask(B, H, T, T, 0.9, seed=93)
+    score = I.alibi_score(B, H, T, T, seed=94)
+    got = run_api(q, k, v, do, mask=mask.to(DEV), score=score.to(DEV))
+    check(got, oracle(q, k, v, do, mask=mask, score=score), "D96 mask+score")
+
+
+def test_document_ids():
+    B, T = 2, 768
+    q, k, v, do = I.qkv(B, T, T, 4, 1, D, seed=95)
+    ids = I.packed_doc_ids(B, T, min_len=100, max_len=300, seed=96)
+    got = run_api(q, k, v, do, doc_ids=ids.to(DEV), is_causal=True)
+    check(got, oracle(q, k, v, do, mask=I.doc_mask(ids, ids), causal=True), "D96 docs")
+
+
+@pytest.mark.parametrize("atomic", [True, False])
+def test_mqa_bshd_bottom_right_split_and_deterministic(atomic):
+    """MQA with few key tiles takes the split-group backward (fp32 slices of width
+    128); use_atomic_backward=False takes the deterministic dQ pass."""
+    B, Tq, Tk, Hq, Hk = 2, 200, 384, 16, 1
+    q, k, v, do = I.qkv(B, Tq, Tk, Hq, Hk, D, seed=97)
+    got = run_api(q, k, v, do, layout="bshd", is_causal=True, causal_align="bottom_right",
+                  use_atomic_backward=atomic)
+    check(got, oracle(q, k, v, do, causal=True, offset=Tk - Tq), f"D96 mqa atomic={atomic}")
+
+
+def test_fp16():
+    q, k, v, do = I.qkv(1, 300, 300, 4, 2, D, seed=98, dtype=torch.float16)
+    check(run_api(q, k, v, do, is_causal=True), oracle(q, k, v, do, causal=True, device="cpu"), "D96 fp16")
+
+
+@pytest.mark.parametrize("deterministic", [False, True])
+def test_stores_stay_inside_the_head(deterministic):
+    """O, dQ, dK and dV written into 96-column views of 128-column buffers: the kernels
+    compute 128 columns, and columns 96..127 of every row must keep their sentinel."""
+    B, T, Hq, Hk = 1, 300, 4, 2
+    bhsd = I.qkv(B, T, T, Hq, Hk, D, seed=99)
+    q, k, v, do = (x.transpose(1, 2).to(DEV) for x in bhsd)  # [B, T, H, D]
+    sentinel = 7.0
+
+    def wide(H):
+        return torch.full((B, T, H, 128), sentinel, dtype=torch.bfloat16, device=DEV)
+
+    o_w, dq_w, dk_w, dv_w = wide(Hq), wide(Hq), wide(Hk), wide(Hk)
+    sc = D ** -0.5
+    o, lse = _lib.forward(q, k, v, None, None, sc, _lib.CAUSAL_TOP_LEFT, out=o_w[..., :D])
+    _lib.backward(do, q, k, v, o, lse, None, None, sc, _lib.CAUSAL_TOP_LEFT, deterministic=deterministic,
+                  grads=(dq_w[..., :D], dk_w[..., :D], dv_w[..., :D]))
+    torch.cuda.synchronize()
+    for name, t in (("O", o_w), ("dQ", dq_w), ("dK", dk_w), ("dV", dv_w)):
+        assert (t[..., D:] == sentinel).all(), f"{name} written past column {D}"
+        assert torch.isfinite(t[..., :D]).all() and not (t[..., :D] == sentinel).all(), name
+    ref = oracle(*bhsd, causal=True, device="cpu")
+    got = tuple(t[..., :D].transpose(1, 2) for t in (o_w, dq_w, dk_w, dv_w))
+    check(got, ref, "D96 strided outputs")

@@ -52,7 +52,7 @@ def test_golden_set_covers_the_semantics():
     assert any(m["layout"] == "bshd" for m in metas)
     assert any(m["Tq"] != m["Tk"] for m in metas)
     assert any(m["Tq"] % 128 for m in metas)
-    assert {m["D"] for m in metas} >= {64, 128}
+    assert {m["D"] for m in metas} >= {64, 96, 128}
     assert any(m["Hq"] > m["Hk"] for m in metas) and any(m["Hk"] == 1 and m["Hq"] > 1 for m in metas)
 
 
