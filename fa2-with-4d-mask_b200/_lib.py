@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "fa4d_mask_prepare_size",
     "fa4d_check_wait_timeout",
     "fa4d_bwd_workspace_size_ex",
+    "fa4d_bwd_group_split",
     "fa4d_mask_prepare_docs",
 )
 DEV_TIMEOUT_FWD, DEV_TIMEOUT_BWD, DEV_TIMEOUT_CHECK = 1, 2, 4
@@ -160,6 +161,8 @@ def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
     lib.fa4d_bwd_workspace_size.restype = ctypes.c_size_t
     lib.fa4d_bwd_workspace_size_ex.argtypes = [ctypes.c_int32] * 6
     lib.fa4d_bwd_workspace_size_ex.restype = ctypes.c_size_t
+    lib.fa4d_bwd_group_split.argtypes = [ctypes.c_int32] * 7
+    lib.fa4d_bwd_group_split.restype = ctypes.c_int32
     lib.fa4d_fwd.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
     lib.fa4d_fwd.restype = ctypes.c_int
     for name in ("fa4d_bwd", "fa4d_bwd_preprocess", "fa4d_bwd_main", "fa4d_bwd_dq_convert", "fa4d_bwd_noalloc"):

@@ -6,6 +6,8 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
+#include <cmath>
 #include <mutex>
 #include <string>
 
@@ -220,17 +222,55 @@ size_t part_bytes(int S, int B, int Tk, int Hk, int D) {
 
 int sm_count();
 
-// Group split of the backward: when one CTA per (key tile, KV head, batch) would leave
-// SMs idle (MQA, short key sequences), the query-head group is split over S CTAs
-// (a power of two dividing the group size, at most 8) until the grid covers about two
-// CTAs per SM.
-int group_split(int B, int Tk, int Hq, int Hk) {
+// Group split of the backward: the query-head group of each (key tile, KV head, batch)
+// is split over S CTAs (a power of two dividing the group size, at most 8) when that
+// shortens the estimated run.  A CTA takes G / S heads x its key tile's query tiles
+// (about 1.5 us per 64-row tile at D = 128, 0.9 us at D = 64) plus about 5 us of fixed
+// cost; a split adds the fp32 partial slices of dK and dV (written, then summed by
+// dkv_convert_kernel) at about 6 TB/s.  When every key tile has about the same number of
+// query tiles (no causal limit, or a band as in bottom-right alignment with Tq < Tk),
+// the grid runs in ceil(CTAs / SMs) equal waves, so splitting also fills a last wave
+// that would run mostly empty (512 CTAs on 148 SMs: 3.46 waves, the fourth under half
+// full).  Otherwise the longest-first grid order balances the SMs and the estimate is
+// the larger of the total work per SM and the longest CTA, so only grids too small for
+// the GPU (MQA, short key sequences) are split.
+int group_split(int B, int Tq, int Tk, int Hq, int Hk, int D, int causal) {
   const int G = Hq / Hk;
-  const int64_t base = static_cast<int64_t>((Tk + 127) / 128) * Hk * B;
-  const int64_t want = 2 * static_cast<int64_t>(sm_count());
-  int S = 1;
-  while (S < 8 && G % (2 * S) == 0 && base * S < want && static_cast<int64_t>(Hk) * 2 * S <= 65535) S *= 2;
-  return S;
+  const int nkb = (Tk + 127) / 128;
+  const double base = static_cast<double>(nkb) * Hk * B;
+  const double sms = sm_count();
+  const double tile_us = D > 64 ? 1.5 : 0.9;
+  const int nqt = (Tq + 63) / 64;
+  // Query tiles per key tile: mean and maximum.
+  double mean_nq = nqt, max_nq = nqt;
+  if (causal) {
+    const long long off = causal_offset(causal, Tq, Tk);
+    double sum = 0.0;
+    max_nq = 0.0;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const long long qmin = 128LL * kb - off;
+      const int first = qmin <= 0 ? 0 : static_cast<int>(qmin / 64);
+      const double n = first < nqt ? nqt - first : 0;
+      sum += n;
+      max_nq = n > max_nq ? n : max_nq;
+    }
+    mean_nq = sum / nkb;
+  }
+  const bool uniform = max_nq <= 1.2 * mean_nq;
+  const double kv_elems = static_cast<double>(B) * Tk * Hk * D;
+  double best = 0.0;
+  int best_s = 1;
+  for (int S = 1; S <= 8 && G % S == 0 && static_cast<int64_t>(Hk) * S <= 65535; S *= 2) {
+    const double per_head = static_cast<double>(G) / S * tile_us;
+    double t = uniform ? std::ceil(base * S / sms) * (per_head * mean_nq + 5.0)
+                       : std::max(base * S / sms * (per_head * mean_nq + 5.0), per_head * max_nq + 5.0);
+    if (S > 1) t += kv_elems * 2.0 * (8.0 * S + 2.0) / 6.0e6;
+    if (S == 1 || t < 0.98 * best) {
+      best = t;
+      best_s = S;
+    }
+  }
+  return best_s;
 }
 
 // SM count of the current device (cached per device).
@@ -261,8 +301,17 @@ size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D) {
   return dq_al + (delta + 255) / 256 * 256;
 }
 
+int32_t fa4d_bwd_group_split(int32_t B, int32_t Tq, int32_t Tk, int32_t Hq, int32_t Hk, int32_t D, int32_t causal) {
+  if (B <= 0 || Tq <= 0 || Tk <= 0 || Hq <= 0 || Hk <= 0 || Hq % Hk != 0) return 0;
+  if (causal < FA4D_CAUSAL_NONE || causal > FA4D_CAUSAL_BOTTOM_RIGHT) return 0;
+  return group_split(B, Tq, Tk, Hq, Hk, D, causal);
+}
+
 size_t fa4d_bwd_workspace_size_ex(int32_t B, int32_t Tq, int32_t Tk, int32_t Hq, int32_t Hk, int32_t D) {
-  const int S = (B > 0 && Tk > 0 && Hq > 0 && Hk > 0 && Hq % Hk == 0) ? group_split(B, Tk, Hq, Hk) : 1;
+  // The causal mode is not an argument here: size for the largest split any mode picks.
+  int S = 1;
+  if (B > 0 && Tq > 0 && Tk > 0 && Hq > 0 && Hk > 0 && Hq % Hk == 0)
+    for (int c = FA4D_CAUSAL_NONE; c <= FA4D_CAUSAL_BOTTOM_RIGHT; ++c) S = std::max(S, group_split(B, Tq, Tk, Hq, Hk, D, c));
   return fa4d_bwd_workspace_size(B, Tq, Hq, D) + (S > 1 ? 2 * part_bytes(S, B, Tk, Hk, compute_dim(D)) : 0);
 }
 
@@ -575,7 +624,7 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   // fa4d_bwd_workspace_size_ex; otherwise one CTA per key tile takes the whole group.
   p.g_split = 1;
   {
-    const int S = group_split(a->B, a->Tk, a->Hq, a->Hk);
+    const int S = group_split(a->B, a->Tq, a->Tk, a->Hq, a->Hk, a->D, a->causal);
     const size_t base_ws = fa4d_bwd_workspace_size(a->B, a->Tq, a->Hq, a->D);
     const size_t pb = part_bytes(S, a->B, a->Tk, a->Hk, Dc);
     if (S > 1 && a->workspace_bytes >= base_ws + 2 * pb) {

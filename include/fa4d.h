@@ -136,15 +136,22 @@ int64_t fa4d_lse_row_stride(int32_t Tq);
  * at (D, except 128 for D = 96). */
 size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D);
 
-/* Workspace bytes including the backward's group-split buffers.  When one CTA per
- * (key tile, KV head, batch) would leave SMs idle (MQA, short key sequences), fa4d_bwd
- * splits each KV head's query-head group over S CTAs (S a power of two, at most 8,
- * chosen from the sizes and the current device's SM count); each writes its fp32
- * partial dK/dV into its own slice and the slices are added in a fixed order, so the
- * result does not depend on scheduling.  A workspace of fa4d_bwd_workspace_size()
- * bytes (no room for the slices) makes fa4d_bwd run unsplit.  Returns
- * fa4d_bwd_workspace_size() when no split would be used. */
+/* Workspace bytes including the backward's group-split buffers.  fa4d_bwd may split
+ * each KV head's query-head group over S CTAs (S a power of two, at most 8, chosen by
+ * fa4d_bwd_group_split from the sizes, the causal mode and the current device's SM
+ * count): when one CTA per (key tile, KV head, batch) would leave SMs idle (MQA, short
+ * key sequences), or when equal-work CTAs would leave the grid's last wave mostly
+ * empty.  Each CTA writes its fp32 partial dK/dV into its own slice and the slices are
+ * added in a fixed order, so the result does not depend on scheduling.  The size
+ * covers the largest split of any causal mode.  A workspace of
+ * fa4d_bwd_workspace_size() bytes (no room for the slices) makes fa4d_bwd run
+ * unsplit.  Returns fa4d_bwd_workspace_size() when no split would be used. */
 size_t fa4d_bwd_workspace_size_ex(int32_t B, int32_t Tq, int32_t Tk, int32_t Hq, int32_t Hk, int32_t D);
+
+/* The group split S fa4d_bwd uses for these sizes and causal mode on the current
+ * device when the workspace has fa4d_bwd_workspace_size_ex() bytes (1: unsplit);
+ * 0 for invalid sizes. */
+int32_t fa4d_bwd_group_split(int32_t B, int32_t Tq, int32_t Tk, int32_t Hq, int32_t Hk, int32_t D, int32_t causal);
 
 /* Forward: O = softmax(((Q K^T + score) * scale) masked) V and LSE.
  * Replaces the launch of flash_attention_fwd_with_4d_mask at

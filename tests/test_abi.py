@@ -10,6 +10,7 @@ import shutil
 import subprocess
 
 import pytest
+import torch
 
 from conftest import ROOT
 from fa2_with_4d_mask_b200 import _lib  # noqa: F401  (loaded through tilelang_fa2_4d_mask)
@@ -78,6 +79,24 @@ def test_host_size_helpers():
     assert lib.fa4d_bwd_workspace_size(1, 1, 1, 64) % 256 == 0
     # Head dim 96 computes at width 128: its dQ accumulator rows hold 128 floats.
     assert lib.fa4d_bwd_workspace_size(1, 8192, 32, 96) == lib.fa4d_bwd_workspace_size(1, 8192, 32, 128)
+
+
+def test_group_split_choices():
+    """The backward's group split on a 148-SM B200 (also the host-side default when no
+    device is visible): equal-work grids are split to fill the last wave, causal grids
+    (balanced by the grid order) only when too small for the GPU."""
+    lib = _lib.load_library()
+    if torch.cuda.is_available() and torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("choices below are for 148 SMs")
+    assert lib.fa4d_bwd_group_split(1, 8192, 8192, 32, 8, 128, _lib.CAUSAL_NONE) == 2  # 512 CTAs: 3.46 waves
+    assert lib.fa4d_bwd_group_split(1, 8192, 8192, 32, 8, 128, _lib.CAUSAL_TOP_LEFT) == 1
+    assert lib.fa4d_bwd_group_split(16, 1024, 4096, 64, 1, 64, _lib.CAUSAL_BOTTOM_RIGHT) == 2  # a band: equal work
+    assert lib.fa4d_bwd_group_split(1, 512, 512, 8, 2, 64, _lib.CAUSAL_TOP_LEFT) == 4  # 8 CTAs
+    assert lib.fa4d_bwd_group_split(1, 4096, 4096, 16, 16, 128, _lib.CAUSAL_NONE) == 1  # group of one
+    assert lib.fa4d_bwd_group_split(1, 128, 128, 3, 2, 64, _lib.CAUSAL_NONE) == 0  # invalid
+    # The workspace covers the largest split of any causal mode.
+    base = lib.fa4d_bwd_workspace_size(1, 8192, 32, 128)
+    assert lib.fa4d_bwd_workspace_size_ex(1, 8192, 8192, 32, 8, 128) > base
 
 
 def _fwd_args(**kw):
