@@ -24,6 +24,7 @@
 // completion -> P -> MMA -> dS -> MMA) overlaps the other tile's work.
 // TMEM (512 columns): S^T x2 [0,128), X x2 [128,256) (a tile's dP^T, later its
 // dQ^T), dV [256,256+D), dK [256+D,256+2D).  All MMAs are kind::f16, fp32 accumulate.
+#include <algorithm>
 #include <cfloat>
 
 #include "fa4d.h"
@@ -635,103 +636,101 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   }
 }
 
-// Delta[b, h, t] = sum over the d_out columns of O * dO (0 for padding rows) and
-// zeroing of the dQ accumulator row (b, h, t), layout [B, Hq, lse_ld, D] with D the
-// compute width.  One warp per (b, t, h).
+// Delta[b, h, t] = sum over the d_out columns of O * dO (0 for padding rows t >= Tq)
+// and zeroing of the dQ accumulator rows (b, h, t < Tq), layout [B, Hq, lse_ld, D]
+// with D the compute width.  One block per (b, t); each thread takes 8 columns of one
+// head (one 16-byte load of O and of dO) and the D / 8 threads of a head reduce the
+// row with shuffles.
 template <int D, bool kBF16>
-__global__ void __launch_bounds__(256) bwd_prep_kernel(const PrepParams p) {
-  const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const int64_t rows = static_cast<int64_t>(p.B) * p.lse_ld * p.Hq;
-  if (w >= rows) return;
-  const int h = static_cast<int>(w % p.Hq);
-  const int t = static_cast<int>((w / p.Hq) % p.lse_ld);
-  const int b = static_cast<int>(w / (static_cast<int64_t>(p.Hq) * p.lse_ld));
-  constexpr int E = D / 32;  // elements per lane (2 or 4)
-  float acc = 0.f;
-  if (t < p.Tq && lane * E < p.d_out) {
-    const uint16_t* o = reinterpret_cast<const uint16_t*>(p.o) + b * p.o_stride[0] +
-                        static_cast<int64_t>(t) * p.o_stride[1] + h * p.o_stride[2] + lane * E;
-    const uint16_t* g = reinterpret_cast<const uint16_t*>(p.dout) + b * p.do_stride[0] +
-                        static_cast<int64_t>(t) * p.do_stride[1] + h * p.do_stride[2] + lane * E;
-    if constexpr (E == 4) {
-      const uint2 ov = *reinterpret_cast<const uint2*>(o);
-      const uint2 gv = *reinterpret_cast<const uint2*>(g);
-      const float2 o0 = unpack2<kBF16>(ov.x), o1 = unpack2<kBF16>(ov.y);
-      const float2 g0 = unpack2<kBF16>(gv.x), g1 = unpack2<kBF16>(gv.y);
-      acc = o0.x * g0.x + o0.y * g0.y + o1.x * g1.x + o1.y * g1.y;
-    } else {
-      const uint32_t ov = *reinterpret_cast<const uint32_t*>(o);
-      const uint32_t gv = *reinterpret_cast<const uint32_t*>(g);
-      const float2 o0 = unpack2<kBF16>(ov), g0 = unpack2<kBF16>(gv);
-      acc = o0.x * g0.x + o0.y * g0.y;
-    }
-  }
-  if (t < p.Tq) {
+__global__ void __launch_bounds__(1024) bwd_prep_kernel(const PrepParams p) {
+  constexpr int kTPR = D / 8;  // threads per head row
+  const int b = blockIdx.x / p.lse_ld;
+  const int t = blockIdx.x - b * p.lse_ld;
+  const int total = p.Hq * kTPR;
+  const bool row_live = t < p.Tq;
+  // Uniform trip count for the whole block, so every lane reaches the shuffles.
+  for (int c0 = 0; c0 < total; c0 += blockDim.x) {
+    const int c = c0 + static_cast<int>(threadIdx.x);
+    const bool live = c < total;
+    const int h = c / kTPR, part = c % kTPR;
+    float acc = 0.f;
+    if (live && row_live) {
+      if (8 * part < p.d_out) {
+        const uint4 ov = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.o) + b * p.o_stride[0] +
+                                                         static_cast<int64_t>(t) * p.o_stride[1] + h * p.o_stride[2] +
+                                                         8 * part);
+        const uint4 gv = *reinterpret_cast<const uint4*>(
+            reinterpret_cast<const uint16_t*>(p.dout) + b * p.do_stride[0] + static_cast<int64_t>(t) * p.do_stride[1] +
+            h * p.do_stride[2] + 8 * part);
+        const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (p.dq_acc) {  // null in deterministic mode (dQ is not accumulated)
-      float* dq = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t) * D + lane * E;
-      if constexpr (E == 4)
-        *reinterpret_cast<float4*>(dq) = make_float4(0.f, 0.f, 0.f, 0.f);
-      else
-        *reinterpret_cast<float2*>(dq) = make_float2(0.f, 0.f);
+        for (int i = 0; i < 4; ++i) {
+          const float2 o2 = unpack2<kBF16>(ow[i]), g2 = unpack2<kBF16>(gw[i]);
+          acc += o2.x * g2.x + o2.y * g2.y;
+        }
+      }
+      if (p.dq_acc) {  // null in deterministic mode (dQ is not accumulated)
+        float4* dq = reinterpret_cast<float4*>(p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t) * D +
+                                               8 * part);
+        dq[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+        dq[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     }
+#pragma unroll
+    for (int off = kTPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (live && part == 0) p.delta[(static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t] = acc;
   }
-  if (lane == 0) p.delta[(static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t] = acc;
 }
 
 // dK, dV (input dtype, caller strides) = sum over the split slices [n_split][B, Tk, Hk,
 // D] of the split-group backward's fp32 partials (dK already scaled), added in slice
-// order so the result does not depend on scheduling; 8 elements per thread.
+// order so the result does not depend on scheduling.  One block per (b, t) row and
+// tensor (blockIdx.y: 0 dK, 1 dV); each thread sums 8 columns of one head.
 template <bool kBF16>
-__global__ void __launch_bounds__(256) dkv_convert_kernel(const DkvConvertParams p) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(1024) dkv_convert_kernel(const DkvConvertParams p) {
   const int per_row = p.d_out / 8;
-  const int64_t rows = static_cast<int64_t>(p.B) * p.Tk * p.Hk;
-  if (i >= 2 * rows * per_row) return;
-  const bool is_v = i >= rows * per_row;
-  const int64_t j = is_v ? i - rows * per_row : i;
-  const int d8 = static_cast<int>(j % per_row);
-  const int64_t row = j / per_row;  // (b, t, h) with h fastest
-  const int h = static_cast<int>(row % p.Hk);
-  const int t = static_cast<int>((row / p.Hk) % p.Tk);
-  const int b = static_cast<int>(row / (static_cast<int64_t>(p.Hk) * p.Tk));
-  const float* base = (is_v ? p.dv_part : p.dk_part) + row * p.D + d8 * 8;
-  float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
-  for (int sidx = 0; sidx < p.n_split; ++sidx) {
-    const float4* src = reinterpret_cast<const float4*>(base + sidx * p.part_stride);
-    const float4 x = src[0], y = src[1];
-    a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
-    c.x += y.x; c.y += y.y; c.z += y.z; c.w += y.w;
-  }
+  const int b = blockIdx.x / p.Tk;
+  const int t = blockIdx.x - b * p.Tk;
+  const bool is_v = blockIdx.y != 0;
+  const float* base = (is_v ? p.dv_part : p.dk_part) + (static_cast<int64_t>(b) * p.Tk + t) * p.Hk * p.D;
   const int64_t* st = is_v ? p.dv_stride : p.dk_stride;
-  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(is_v ? p.dv : p.dk) + b * st[0] +
-                                        static_cast<int64_t>(t) * st[1] + h * st[2] + d8 * 8);
-  *dst = make_uint4(pack2<kBF16>(a.x, a.y), pack2<kBF16>(a.z, a.w), pack2<kBF16>(c.x, c.y), pack2<kBF16>(c.z, c.w));
+  uint16_t* out = reinterpret_cast<uint16_t*>(is_v ? p.dv : p.dk) + b * st[0] + static_cast<int64_t>(t) * st[1];
+  for (int c = static_cast<int>(threadIdx.x); c < p.Hk * per_row; c += blockDim.x) {
+    const int h = c / per_row, d8 = c - h * per_row;
+    const float* src = base + h * p.D + d8 * 8;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), e = a;
+    for (int sidx = 0; sidx < p.n_split; ++sidx) {
+      const float4* s4 = reinterpret_cast<const float4*>(src + sidx * p.part_stride);
+      const float4 x = s4[0], y = s4[1];
+      a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+      e.x += y.x; e.y += y.y; e.z += y.z; e.w += y.w;
+    }
+    *reinterpret_cast<uint4*>(out + h * st[2] + d8 * 8) =
+        make_uint4(pack2<kBF16>(a.x, a.y), pack2<kBF16>(a.z, a.w), pack2<kBF16>(e.x, e.y), pack2<kBF16>(e.z, e.w));
+  }
 }
 
-// dQ (input dtype, caller strides) = scale * dq_acc [B, Hq, lse_ld, D], 8 elements per thread.
+// dQ (input dtype, caller strides) = scale * dq_acc [B, Hq, lse_ld, D] over the d_out
+// columns.  One block per 32 rows of one (b, h), so each block reads one contiguous
+// 32 x D run of the accumulator; each thread converts 8 columns of a row at a time.
 template <bool kBF16>
 __global__ void __launch_bounds__(256) dq_convert_kernel(const ConvertParams p) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int per_row = p.d_out / 8;
-  const int64_t total = static_cast<int64_t>(p.B) * p.Tq * p.Hq * per_row;
-  if (i >= total) return;
-  const int d8 = static_cast<int>(i % per_row);
-  const int64_t row = i / per_row;  // (b, t, h) with h fastest
-  const int h = static_cast<int>(row % p.Hq);
-  const int t = static_cast<int>((row / p.Hq) % p.Tq);
-  const int b = static_cast<int>(row / (static_cast<int64_t>(p.Hq) * p.Tq));
-  const float4* src = reinterpret_cast<const float4*>(
-      p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t) * p.D + d8 * 8);
-  const float4 a = src[0], c = src[1];
+  const int t0 = blockIdx.x * 32;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const float* src = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + t0) * p.D;
+  uint16_t* dst = reinterpret_cast<uint16_t*>(p.dq) + b * p.dq_stride[0] + h * p.dq_stride[2];
   const float sc = p.scale;  // dQ = scale * dS K (dS is accumulated without the scale)
-  uint4 out = make_uint4(pack2<kBF16>(a.x * sc, a.y * sc), pack2<kBF16>(a.z * sc, a.w * sc),
-                         pack2<kBF16>(c.x * sc, c.y * sc), pack2<kBF16>(c.z * sc, c.w * sc));
-  uint16_t* dst = reinterpret_cast<uint16_t*>(p.dq) + b * p.dq_stride[0] + static_cast<int64_t>(t) * p.dq_stride[1] +
-                  h * p.dq_stride[2] + d8 * 8;
-  *reinterpret_cast<uint4*>(dst) = out;
+  for (int c = static_cast<int>(threadIdx.x); c < 32 * per_row; c += blockDim.x) {
+    const int r = c / per_row, d8 = c - r * per_row;
+    if (t0 + r >= p.Tq) break;  // rows only grow with c
+    const float4* s4 = reinterpret_cast<const float4*>(src + static_cast<int64_t>(r) * p.D + d8 * 8);
+    const float4 a = s4[0], e = s4[1];
+    *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(t0 + r) * p.dq_stride[1] + d8 * 8) =
+        make_uint4(pack2<kBF16>(a.x * sc, a.y * sc), pack2<kBF16>(a.z * sc, a.w * sc),
+                   pack2<kBF16>(e.x * sc, e.y * sc), pack2<kBF16>(e.z * sc, e.w * sc));
+  }
 }
 
 template <int D, bool kBF16, bool kMask, bool kScore>
@@ -763,15 +762,19 @@ cudaError_t launch_bwd(const BwdParams& p, int D, bool bf16, bool has_mask, bool
   return cudaErrorInvalidValue;
 }
 
+// Threads per block for a row of `chunks` 8-column pieces: whole warps, at most 1024.
+int row_block(int chunks) { return std::min(1024, (chunks + 31) / 32 * 32); }
+
 cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s) {
-  const int64_t rows = static_cast<int64_t>(p.B) * p.lse_ld * p.Hq;
-  const int64_t blocks = (rows * 32 + 255) / 256;
+  const int64_t blocks = static_cast<int64_t>(p.B) * p.lse_ld;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidValue;  // one block per (b, t) row
+  const int threads = row_block(p.Hq * (p.D / 8));
   if (p.D == 128) {
-    if (bf16) bwd_prep_kernel<128, true><<<blocks, 256, 0, s>>>(p);
-    else bwd_prep_kernel<128, false><<<blocks, 256, 0, s>>>(p);
+    if (bf16) bwd_prep_kernel<128, true><<<blocks, threads, 0, s>>>(p);
+    else bwd_prep_kernel<128, false><<<blocks, threads, 0, s>>>(p);
   } else if (p.D == 64) {
-    if (bf16) bwd_prep_kernel<64, true><<<blocks, 256, 0, s>>>(p);
-    else bwd_prep_kernel<64, false><<<blocks, 256, 0, s>>>(p);
+    if (bf16) bwd_prep_kernel<64, true><<<blocks, threads, 0, s>>>(p);
+    else bwd_prep_kernel<64, false><<<blocks, threads, 0, s>>>(p);
   } else {
     return cudaErrorInvalidValue;
   }
@@ -779,18 +782,19 @@ cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s) {
 }
 
 cudaError_t launch_dkv_convert(const DkvConvertParams& p, bool bf16, cudaStream_t s) {
-  const int64_t total = 2 * static_cast<int64_t>(p.B) * p.Tk * p.Hk * (p.d_out / 8);
-  const int64_t blocks = (total + 255) / 256;
-  if (bf16) dkv_convert_kernel<true><<<blocks, 256, 0, s>>>(p);
-  else dkv_convert_kernel<false><<<blocks, 256, 0, s>>>(p);
+  const int64_t rows = static_cast<int64_t>(p.B) * p.Tk;
+  if (rows > 0x7fffffff) return cudaErrorInvalidValue;  // one block per (b, t) row
+  const dim3 grid(static_cast<unsigned>(rows), 2);
+  const int threads = row_block(p.Hk * (p.d_out / 8));
+  if (bf16) dkv_convert_kernel<true><<<grid, threads, 0, s>>>(p);
+  else dkv_convert_kernel<false><<<grid, threads, 0, s>>>(p);
   return cudaGetLastError();
 }
 
 cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s) {
-  const int64_t total = static_cast<int64_t>(p.B) * p.Tq * p.Hq * (p.d_out / 8);
-  const int64_t blocks = (total + 255) / 256;
-  if (bf16) dq_convert_kernel<true><<<blocks, 256, 0, s>>>(p);
-  else dq_convert_kernel<false><<<blocks, 256, 0, s>>>(p);
+  const dim3 grid((p.Tq + 31) / 32, p.Hq, p.B);
+  if (bf16) dq_convert_kernel<true><<<grid, 256, 0, s>>>(p);
+  else dq_convert_kernel<false><<<grid, 256, 0, s>>>(p);
   return cudaGetLastError();
 }
 
