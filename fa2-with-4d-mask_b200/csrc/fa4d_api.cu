@@ -234,29 +234,42 @@ int sm_count();
 // full).  Otherwise the longest-first grid order balances the SMs and the estimate is
 // the larger of the total work per SM and the longest CTA, so only grids too small for
 // the GPU (MQA, short key sequences) are split.
+// Query tiles (64 rows) per 128-key tile of the backward: mean and maximum over the
+// key tiles, and whether they are about equal (every key tile within 1.2 x the mean).
+struct KeyTileWork {
+  double mean_nq, max_nq;
+  bool equal;
+};
+KeyTileWork key_tile_work(int Tq, int Tk, int causal) {
+  const int nkb = (Tk + 127) / 128;
+  const int nqt = (Tq + 63) / 64;
+  KeyTileWork w{static_cast<double>(nqt), static_cast<double>(nqt), true};
+  if (causal) {
+    const long long off = causal_offset(causal, Tq, Tk);
+    double sum = 0.0;
+    w.max_nq = 0.0;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const long long qmin = 128LL * kb - off;
+      const int first = qmin <= 0 ? 0 : static_cast<int>(qmin / 64);
+      const double n = first < nqt ? nqt - first : 0;
+      sum += n;
+      w.max_nq = n > w.max_nq ? n : w.max_nq;
+    }
+    w.mean_nq = sum / nkb;
+  }
+  w.equal = w.max_nq <= 1.2 * w.mean_nq;
+  return w;
+}
+
 int group_split(int B, int Tq, int Tk, int Hq, int Hk, int D, int causal) {
   const int G = Hq / Hk;
   const int nkb = (Tk + 127) / 128;
   const double base = static_cast<double>(nkb) * Hk * B;
   const double sms = sm_count();
   const double tile_us = D > 64 ? 1.5 : 0.9;
-  const int nqt = (Tq + 63) / 64;
-  // Query tiles per key tile: mean and maximum.
-  double mean_nq = nqt, max_nq = nqt;
-  if (causal) {
-    const long long off = causal_offset(causal, Tq, Tk);
-    double sum = 0.0;
-    max_nq = 0.0;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const long long qmin = 128LL * kb - off;
-      const int first = qmin <= 0 ? 0 : static_cast<int>(qmin / 64);
-      const double n = first < nqt ? nqt - first : 0;
-      sum += n;
-      max_nq = n > max_nq ? n : max_nq;
-    }
-    mean_nq = sum / nkb;
-  }
-  const bool uniform = max_nq <= 1.2 * mean_nq;
+  const KeyTileWork w = key_tile_work(Tq, Tk, causal);
+  const double mean_nq = w.mean_nq, max_nq = w.max_nq;
+  const bool uniform = w.equal;
   const double kv_elems = static_cast<double>(B) * Tk * Hk * D;
   double best = 0.0;
   int best_s = 1;
@@ -622,6 +635,8 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   if (a->score) p.score_pf = encode_bias(&p.tm_score, a->score, a->B, a->Hq, a->Tq, a->Tk, a->score_stride, 4, 64);
   // Group split (see group_split), used when the caller's workspace was sized with
   // fa4d_bwd_workspace_size_ex; otherwise one CTA per key tile takes the whole group.
+  // Equal-work grids without a block map run key tiles fastest (see BwdParams).
+  p.kb_fastest = (!p.mask_blocks && key_tile_work(a->Tq, a->Tk, a->causal).equal) ? 1 : 0;
   p.g_split = 1;
   {
     const int S = group_split(a->B, a->Tq, a->Tk, a->Hq, a->Hk, a->D, a->causal);

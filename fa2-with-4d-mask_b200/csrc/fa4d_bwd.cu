@@ -168,12 +168,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   const int lane = threadIdx.x & 31;
   // Grid (Hk x group split, key tiles, B), dispatched x-fastest: all heads of one key
   // tile go out together, and under a causal mask the first key tiles (which see the
-  // most queries) go first.  blockIdx.x = KV head x split: the CTA takes query heads
+  // most queries) go first.  KV head x split: the CTA takes query heads
   // [h_first, h_first + G) of its KV head's group (G = Hq / Hk / g_split).
-  const int kb = blockIdx.y;
+  // With p.kb_fastest the grid is (key tiles, KV head x split, B) instead.
+  const int kb = p.kb_fastest ? blockIdx.x : blockIdx.y;
+  const int hx = p.kb_fastest ? blockIdx.y : blockIdx.x;
   const int k0 = kb * 128;
-  const int hk = blockIdx.x / p.g_split;
-  const int split = blockIdx.x - hk * p.g_split;
+  const int hk = hx / p.g_split;
+  const int split = hx - hk * p.g_split;
   const int b = blockIdx.z;
   const int G = p.Hq / p.Hk / p.g_split;
   const int h_first = hk * (p.Hq / p.Hk) + split * G;
@@ -739,7 +741,8 @@ cudaError_t launch_bwd_t(const BwdParams& p, cudaStream_t s) {
   auto kern = bwd_kernel<D, kBF16, kMask, kScore>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.Hk * p.g_split, (p.Tk + 127) / 128, p.B);
+  const unsigned nkb = (p.Tk + 127) / 128, nh = p.Hk * p.g_split;
+  const dim3 grid = p.kb_fastest ? dim3(nkb, nh, p.B) : dim3(nh, nkb, p.B);
   kern<<<grid, kBwdThreads, L::kAlloc, s>>>(p);
   return cudaGetLastError();
 }

@@ -102,6 +102,11 @@ struct BwdParams {
   // products and the drain.
   int32_t skip_dq;
   int32_t d_out;  // head dim of dK / dV (as in FwdParams); dq_acc and the slices use D
+  // 1: grid (key tiles, KV head x split, B), key tiles fastest, so a wave covers whole
+  // heads and each dQ accumulator tile receives all its key tiles' additions while it
+  // is in L2 (equal-work grids); 0: grid (KV head x split, key tiles, B), the longest
+  // key tiles first (causal and block-sparse grids).
+  int32_t kb_fastest;
 };
 
 // Deterministic dQ: one CTA per 128-row query tile of one (batch, head) walks its key
