@@ -44,9 +44,9 @@ B, T, HQ, HK, D = 1, 8192, 32, 8, 128
 WORKLOAD = "cfg2: B1 Tq=Tk=8192 Hq32 Hk8 D128 bf16 non-causal, fwd+bwd per GPU"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per launch of the backward main kernel at this workload:
-# dram__bytes_read.sum 377,699,584 + dram__bytes_write.sum 157,557,760 from one ncu
+# dram__bytes_read.sum 313,795,328 + dram__bytes_write.sum 222,457,088 from one ncu
 # capture of this bench command (profiles/launches_cfg2_fwd_bwd.md).
-NCU_BWD_MAIN_TRAFFIC = 535257344
+NCU_BWD_MAIN_TRAFFIC = 536252416
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -298,7 +298,10 @@ def _run_ours(args, _lib):
             "algorithmic": "10*B*Hq*Tq*Tk*D FLOP per launch (bwd share of the 14x convention)",
             "traffic": NCU_BWD_MAIN_TRAFFIC,
         },
-        "gpu_launches": 4 * args.steps,
+        # fwd, preprocess, main, dQ convert, plus the split-slice sum when the
+        # backward's group split is on for this workload.
+        "gpu_launches": (4 + (_lib.load_library().fa4d_bwd_group_split(B, T, T, HQ, HK, D, _lib.CAUSAL_NONE) > 1))
+        * args.steps,
         "device_status": status,
         "clocks": clocks,
     }
