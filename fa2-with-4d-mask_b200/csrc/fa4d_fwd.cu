@@ -403,10 +403,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], i & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * c]));
-      tmem_wait_ld();
 
       const int kbase = kt * 128;
       const bool need_bounds = kbase + 128 > p.Tk;
@@ -414,106 +410,40 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       // Interior tile with nothing to add or mask (warp-uniform): the row max is taken
       // on raw S and the scale is folded into the exponent's FMA below.
       const bool fast = !kScore && !use_mask && !need_bounds && !need_causal && p.scale_log2 > 0.f;
-      float m_tile = kNegInf;
+      // Online softmax with lazy rescaling of O; returns the max the exponents use.
+      auto online_update = [&](float m_tile) {
+        const float m_new = fmaxf(m_run, m_tile);
+        const bool need = m_new > m_run + kRescaleThreshold;
+        float alpha = 1.f;
+        if (need) {
+          alpha = ex2(m_run - m_new);  // m_run == -inf -> 0
+          l_run *= alpha;
+          m_run = m_new;
+        }
+        if (i > 0 && __any_sync(0xffffffffu, need)) {
+          // The slot's previous PV has completed (this tile's S was issued after it).
+#pragma unroll
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t o[16];
+            tmem_ld16(tO + 16 * c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 16; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+            tmem_st16(tO + 16 * c, o);
+          }
+        }
+        return (m_run == kNegInf) ? 0.f : m_run;
+      };
+      float rowsum = 0.f;
       if (fast) {
+        uint32_t sr[128];  // the whole row of S
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * c]));
+        tmem_wait_ld();
         float m4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
 #pragma unroll
         for (int k = 0; k < 128; ++k) m4[k & 3] = fmaxf(m4[k & 3], __uint_as_float(sr[k]));
-        m_tile = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
-      } else {
-        if (kMask && use_mask && !bits_row) {
-          // No prepared bits: read this row's 128 mask bytes from global memory.
-          const uint4 v = mask_words_from_bytes(mask_row, kbase, p.Tk, p.mask_vec);
-          mw[0] = v.x;
-          mw[1] = v.y;
-          mw[2] = v.z;
-          mw[3] = v.w;
-        }
-        if (need_bounds || need_causal) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) mw[c] &= low_bits(key_lim - (kbase + 32 * c));
-        }
-        float m4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
-        // x = (s + score) * scale, -inf where the keep bit is clear; the score is
-        // consumed four values at a time so few registers are live beside S.
-        auto apply4 = [&](int e0, float a0, float a1, float a2, float a3, uint32_t w) {
-          const float av[4] = {a0, a1, a2, a3};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int e = e0 + j;
-            float x = __uint_as_float(sr[e]);
-            if constexpr (kScore) x += av[j];
-            x *= p.scale_log2;
-            x = ((w >> (e & 31)) & 1u) ? x : kNegInf;
-            sr[e] = __float_as_uint(x);
-            m4[j] = fmaxf(m4[j], x);
-          }
-        };
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int kc = kbase + 32 * c;
-          const uint32_t w = mw[c];
-          if constexpr (kScore) {
-            if (p.bias_tma) {
-              const int e = g % R;
-              ok = __all_sync(0xffffffffu, mbar_wait(&full[e], (g / R) & 1, abort_flag));
-              if (!ok) break;
-#pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                const float4 v = lds_f4(ring_row + e * kRingEntry + ((u ^ sw) << 4));
-                apply4(32 * c + 4 * u, v.x, v.y, v.z, v.w, w);
-              }
-              mbar_arrive(&empty[e]);
-              ++g;
-            } else if (p.score_vec && kc + 31 < p.Tk) {
-#pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                const float4 v = __ldg(reinterpret_cast<const float4*>(score_row + kc) + u);
-                apply4(32 * c + 4 * u, v.x, v.y, v.z, v.w, w);
-              }
-            } else {
-#pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                const int k4 = kc + 4 * u;
-                apply4(32 * c + 4 * u, (k4 < p.Tk) ? __ldg(score_row + k4) : 0.f,
-                       (k4 + 1 < p.Tk) ? __ldg(score_row + k4 + 1) : 0.f,
-                       (k4 + 2 < p.Tk) ? __ldg(score_row + k4 + 2) : 0.f,
-                       (k4 + 3 < p.Tk) ? __ldg(score_row + k4 + 3) : 0.f, w);
-              }
-            }
-          } else {
-#pragma unroll
-            for (int u = 0; u < 8; ++u) apply4(32 * c + 4 * u, 0.f, 0.f, 0.f, 0.f, w);
-          }
-        }
-        if (!ok) break;
-        m_tile = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-      }
-
-      // Online softmax with lazy rescaling of O.
-      const float m_new = fmaxf(m_run, m_tile);
-      const bool need = m_new > m_run + kRescaleThreshold;
-      float alpha = 1.f;
-      if (need) {
-        alpha = ex2(m_run - m_new);  // m_run == -inf -> 0
-        l_run *= alpha;
-        m_run = m_new;
-      }
-      if (i > 0 && __any_sync(0xffffffffu, need)) {
-        // The slot's previous PV has completed (this tile's S was issued after it).
-#pragma unroll
-        for (int c = 0; c < D / 16; ++c) {
-          uint32_t o[16];
-          tmem_ld16(tO + 16 * c, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int k = 0; k < 16; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-          tmem_st16(tO + 16 * c, o);
-        }
-      }
-      const float m_use = (m_run == kNegInf) ? 0.f : m_run;
-      float rowsum = 0.f;
-      if (fast) {
+        const float m_use = online_update(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2);
         // exp2(s * scale * log2(e) - m) on pairs of packed fp32; every kPolyEvery-th
         // pair on the FMA pipe (ex2_poly2) so the MUFU unit is not the limit.
         const uint64_t sc2 = f2(p.scale_log2, p.scale_log2), nm2 = f2(-m_use, -m_use);
@@ -535,17 +465,107 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         const float2 rs = f2_split(rs2);
         rowsum = rs.x + rs.y;
       } else {
+        if (kMask && use_mask && !bits_row) {
+          // No prepared bits: read this row's 128 mask bytes from global memory.
+          const uint4 v = mask_words_from_bytes(mask_row, kbase, p.Tk, p.mask_vec);
+          mw[0] = v.x;
+          mw[1] = v.y;
+          mw[2] = v.z;
+          mw[3] = v.w;
+        }
+        if (need_bounds || need_causal) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
+          for (int c = 0; c < 4; ++c) mw[c] &= low_bits(key_lim - (kbase + 32 * c));
+        }
+        float m4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
+        // x = (s + score) * scale, -inf where the keep bit is clear, in two halves of
+        // 64 keys: each half is read from TMEM, transformed and written back, so only 64
+        // values are live beside the mask words and the score state (the whole row in
+        // registers spilled).  The score is consumed four values at a time.
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const float p0 = ex2(__uint_as_float(sr[32 * c + 2 * k]) - m_use);
-            const float p1 = ex2(__uint_as_float(sr[32 * c + 2 * k + 1]) - m_use);
-            rowsum += p0 + p1;
-            pk[k] = pack2<kBF16>(p0, p1);
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t xr[64];
+          tmem_ld32(tS + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&xr[0]));
+          tmem_ld32(tS + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&xr[32]));
+          tmem_wait_ld();
+          auto apply4 = [&](int e0, float a0, float a1, float a2, float a3, uint32_t w) {
+            const float av[4] = {a0, a1, a2, a3};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int e = e0 + j;
+              float x = __uint_as_float(xr[e]);
+              if constexpr (kScore) x += av[j];
+              x *= p.scale_log2;
+              x = ((w >> (e & 31)) & 1u) ? x : kNegInf;
+              xr[e] = __float_as_uint(x);
+              m4[j] = fmaxf(m4[j], x);
+            }
+          };
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const int c = 2 * hh + cc;
+            const int kc = kbase + 32 * c;
+            const uint32_t w = mw[c];
+            if constexpr (kScore) {
+              if (p.bias_tma) {
+                const int e = g % R;
+                ok = __all_sync(0xffffffffu, mbar_wait(&full[e], (g / R) & 1, abort_flag));
+                if (!ok) break;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  const float4 v = lds_f4(ring_row + e * kRingEntry + ((u ^ sw) << 4));
+                  apply4(32 * cc + 4 * u, v.x, v.y, v.z, v.w, w);
+                }
+                mbar_arrive(&empty[e]);
+                ++g;
+              } else if (p.score_vec && kc + 31 < p.Tk) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  const float4 v = __ldg(reinterpret_cast<const float4*>(score_row + kc) + u);
+                  apply4(32 * cc + 4 * u, v.x, v.y, v.z, v.w, w);
+                }
+              } else {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  const int k4 = kc + 4 * u;
+                  apply4(32 * cc + 4 * u, (k4 < p.Tk) ? __ldg(score_row + k4) : 0.f,
+                         (k4 + 1 < p.Tk) ? __ldg(score_row + k4 + 1) : 0.f,
+                         (k4 + 2 < p.Tk) ? __ldg(score_row + k4 + 2) : 0.f,
+                         (k4 + 3 < p.Tk) ? __ldg(score_row + k4 + 3) : 0.f, w);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int u = 0; u < 8; ++u) apply4(32 * cc + 4 * u, 0.f, 0.f, 0.f, 0.f, w);
+            }
           }
-          tmem_st16(tS + 16 * c, pk);
+          if (!ok) break;
+          tmem_st32(tS + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&xr[0]));
+          tmem_st32(tS + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&xr[32]));
+        }
+        if (!ok) break;
+        tmem_wait_st();  // the transformed row is read back below
+        const float m_use = online_update(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+        // The transformed row comes back in halves; P of keys 64 hh .. 64 hh + 63 goes
+        // to columns 32 hh .. 32 hh + 31, whose x values have been read by then.
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t xr[64];
+          tmem_ld32(tS + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&xr[0]));
+          tmem_ld32(tS + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&xr[32]));
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const float p0 = ex2(__uint_as_float(xr[32 * c + 2 * k]) - m_use);
+              const float p1 = ex2(__uint_as_float(xr[32 * c + 2 * k + 1]) - m_use);
+              rowsum += p0 + p1;
+              pk[k] = pack2<kBF16>(p0, p1);
+            }
+            tmem_st16(tS + 32 * hh + 16 * c, pk);
+          }
         }
       }
       l_run += rowsum;
