@@ -491,14 +491,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
           auto apply4 = [&](int e0, float a0, float a1, float a2, float a3, uint32_t w) {
             const float av[4] = {a0, a1, a2, a3};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < 4; j += 2) {
               const int e = e0 + j;
-              float x = __uint_as_float(xr[e]);
-              if constexpr (kScore) x += av[j];
-              x *= p.scale_log2;
-              x = ((w >> (e & 31)) & 1u) ? x : kNegInf;
-              xr[e] = __float_as_uint(x);
-              m4[j] = fmaxf(m4[j], x);
+              float x0, x1;
+              if constexpr (kScore) {
+                // (s + score) * scale on a packed fp32 pair (same rounding as scalar).
+                const float2 x = f2_split(fmul2(fadd2(f2(__uint_as_float(xr[e]), __uint_as_float(xr[e + 1])),
+                                                      f2(av[j], av[j + 1])),
+                                                f2(p.scale_log2, p.scale_log2)));
+                x0 = x.x;
+                x1 = x.y;
+              } else {
+                x0 = __uint_as_float(xr[e]) * p.scale_log2;
+                x1 = __uint_as_float(xr[e + 1]) * p.scale_log2;
+              }
+              x0 = ((w >> (e & 31)) & 1u) ? x0 : kNegInf;
+              x1 = ((w >> ((e + 1) & 31)) & 1u) ? x1 : kNegInf;
+              xr[e] = __float_as_uint(x0);
+              xr[e + 1] = __float_as_uint(x1);
+              m4[j] = fmaxf(m4[j], x0);
+              m4[j + 1] = fmaxf(m4[j + 1], x1);
             }
           };
 #pragma unroll
@@ -548,6 +560,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         const float m_use = online_update(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
         // The transformed row comes back in halves; P of keys 64 hh .. 64 hh + 63 goes
         // to columns 32 hh .. 32 hh + 31, whose x values have been read by then.
+        const uint64_t nm2 = f2(m_use, m_use);
+        uint64_t rs2 = f2(0.f, 0.f);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           uint32_t xr[64];
@@ -559,13 +573,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             uint32_t pk[16];
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
-              const float p0 = ex2(__uint_as_float(xr[32 * c + 2 * k]) - m_use);
-              const float p1 = ex2(__uint_as_float(xr[32 * c + 2 * k + 1]) - m_use);
-              rowsum += p0 + p1;
+              float p0, p1;
+              if constexpr (kScore) {
+                // Packed pairs with a score (no spills there); scalar otherwise, which
+                // compiles the dense kernel's rare edge tiles as before.
+                const float2 a = f2_split(
+                    fsub2(f2(__uint_as_float(xr[32 * c + 2 * k]), __uint_as_float(xr[32 * c + 2 * k + 1])), nm2));
+                p0 = ex2(a.x);
+                p1 = ex2(a.y);
+                rs2 = fadd2(rs2, f2(p0, p1));
+              } else {
+                p0 = ex2(__uint_as_float(xr[32 * c + 2 * k]) - m_use);
+                p1 = ex2(__uint_as_float(xr[32 * c + 2 * k + 1]) - m_use);
+                rowsum += p0 + p1;
+              }
               pk[k] = pack2<kBF16>(p0, p1);
             }
             tmem_st16(tS + 32 * hh + 16 * c, pk);
           }
+        }
+        if constexpr (kScore) {
+          const float2 rs = f2_split(rs2);
+          rowsum = rs.x + rs.y;
         }
       }
       l_run += rowsum;
