@@ -150,6 +150,9 @@ def _run_ours(args, _lib):
     if world > 1:
         import torch.distributed as dist
 
+        # NCCL writes its version banner to stdout at INFO/VERSION levels; keep stdout
+        # to the one JSON line unless the caller asked for NCCL logs.
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     peaks, peak_src = load_peaks()
 
