@@ -407,6 +407,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       const int h = h_first + cur.g();
       const int q0 = cur.q0();
       const bool use_mask = kMask && cur.state() == 1;  // warp-uniform
+      // This key's score for the tile's 64 queries, requested before the wait for S so
+      // the loads (L2 hits: the producer prefetched the tile) overlap it.
+      float scv[kScore ? 64 : 1];
+      if constexpr (kScore) {
+        const float* sc = p.score + b * p.score_stride[0] + h * p.score_stride[1] + kc;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) scv[c] = __ldg(sc + min(q0 + c, p.Tq - 1) * p.score_stride[2]);
+      }
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], par, abort_flag) &&
                                        mbar_wait(&q_full[qs], (it / kQStages) & 1, abort_flag));
       if (!ok) break;
@@ -416,9 +424,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       const bool need_bounds = (q0 + 64 > p.Tq) || (k0 + 128 > p.Tk);
       const bool fast = !use_mask && !kScore && !need_causal && !need_bounds;  // warp-uniform
       const float4* l4 = reinterpret_cast<const float4*>(sLSE + qs * 64);
-      const float* score_col = nullptr;
       const uint8_t* mask_col = nullptr;
-      if (kScore) score_col = p.score + b * p.score_stride[0] + h * p.score_stride[1] + kc;
       if (kMask) mask_col = p.mask + b * p.mask_stride[0] + h * p.mask_stride[1] + kc;
       // Keep flags of the tile's 64 queries for this key (bit c = query q0 + c): mask,
       // query bound, key bound and causal limit, applied as whole-word masks.
@@ -468,7 +474,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
           for (int i = 0; i < 32; ++i) {
             const int c = 32 * half + i;
             float x = __uint_as_float(sr[i]);
-            if constexpr (kScore) x += __ldg(score_col + min(q0 + c, p.Tq - 1) * p.score_stride[2]);
+            if constexpr (kScore) x += scv[c];
             const float e = ex2(fmaf(x, p.scale_log2, -sLSE[qs * 64 + c]));
             pv[c] = ((w >> i) & 1u) ? e : 0.f;
           }
