@@ -1,6 +1,6 @@
 """Generates tests/golden/*.npz from the reference project itself.
 
-Runs only where the reference source tree is available (default path given by
+Runs only where the reference source tree is available (its path is given with
 --reference).  For every case it calls the reference's own user wrapper
 ``tilelang_flash_attention`` (python/modeling_attention.py:70-147) with the kernel
 call replaced by the reference's own correctness oracle ``eager_ref``
@@ -132,7 +132,7 @@ def make_case(c: dict, eager_ref, wrapper_mod) -> dict:
 
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference", help="reference source tree")
+    ap.add_argument("--reference", required=True, help="reference source tree (the project's checkout)")
     ap.add_argument("--only", nargs="*", help="write only these cases (each case has its own seed)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
