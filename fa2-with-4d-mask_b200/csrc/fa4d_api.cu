@@ -194,11 +194,19 @@ int check_common(int B, int Tq, int Tk, int Hq, int Hk, int D, int dtype, int ca
   if ((Tq + 255) / 256 > 65535 || (Tk + 127) / 128 > 65535)
     return fail(FA4D_ERR_UNSUPPORTED, "sequence too long for the launch grid (Tq <= 16M, Tk <= 8M)");
   if (Tq > (1 << 30) || Tk > (1 << 30)) return fail(FA4D_ERR_INVALID, "sequence length too large");
-  if (D != 64 && D != 96 && D != 128) return fail(FA4D_ERR_UNSUPPORTED, "head dim %d is not built (64, 96, 128)", D);
+  if (D != 64 && D != 96 && D != 128 && D != 256)
+    return fail(FA4D_ERR_UNSUPPORTED, "head dim %d is not built (64, 96, 128, 256)", D);
   if (dtype != FA4D_BF16 && dtype != FA4D_F16) return fail(FA4D_ERR_INVALID, "dtype %d is not bf16/f16", dtype);
   if (causal < FA4D_CAUSAL_NONE || causal > FA4D_CAUSAL_BOTTOM_RIGHT)
     return fail(FA4D_ERR_INVALID, "causal mode %d is unknown", causal);
   if (!(scale == scale)) return fail(FA4D_ERR_INVALID, "scale is NaN");
+  return FA4D_OK;
+}
+
+// Head dims the backward is built for: dK and dV of a 128-key tile at D = 256 would
+// take all 512 TMEM columns, so that head dim is forward only.
+int check_bwd_dim(int D) {
+  if (D == 256) return fail(FA4D_ERR_UNSUPPORTED, "head dim 256: the backward is not built (forward only)");
   return FA4D_OK;
 }
 
@@ -564,6 +572,7 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse)
     return fail(FA4D_ERR_INVALID, "q, k, v, o, dout and lse are required");
   if (a->deterministic != 0 && a->deterministic != 1) return fail(FA4D_ERR_INVALID, "deterministic must be 0 or 1");
+  if ((rc = check_bwd_dim(a->D))) return rc;
   if ((rc = check_rows16(a->dq, a->dq_stride, "dq"))) return rc;
   if ((rc = check_rows16(a->dk, a->dk_stride, "dk"))) return rc;
   if ((rc = check_rows16(a->dv, a->dv_stride, "dv"))) return rc;
@@ -842,6 +851,7 @@ int fa4d_bwd_noalloc(const fa4d_bwd_args* a, void* stream) {
   if (!a) return fail(FA4D_ERR_INVALID, "args is NULL");
   int rc = check_common(a->B, a->Tq, a->Tk, a->Hq, a->Hk, a->D, a->dtype, a->causal, a->scale);
   if (rc) return rc;
+  if ((rc = check_bwd_dim(a->D))) return rc;
   const size_t need = fa4d_bwd_workspace_size(a->B, a->Tq, a->Hq, a->D);
   if (need > kNoAllocScratchBytes)
     return fail(FA4D_ERR_WORKSPACE,

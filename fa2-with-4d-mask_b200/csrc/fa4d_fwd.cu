@@ -57,16 +57,20 @@ constexpr int kRingEntry = 16384;
 template <int D, bool kMask, bool kScore>
 struct FwdLayout {
   static constexpr int kTile = 128 * D * 2;  // one 128-row tile of 16-bit elements
+  // Query slots per CTA.  At D=256 one slot's S (128 columns) and O (256) take 384 of
+  // the 512 TMEM columns and its Q, K and V tiles 192 KB of shared memory, so the CTA
+  // has one slot and single-stage K/V (the second slot's warps stay idle).
+  static constexpr int kSlots = D == 256 ? 1 : 2;
   // With a score at D=128 the score staging rings take the room of one K/V stage.
-  static constexpr int kKVStages = (kScore && D == 128) ? 1 : 2;
-  static constexpr int kQ = 0;  // 2 query slots
-  static constexpr int kK = kQ + 2 * kTile;
+  static constexpr int kKVStages = (D == 256 || (kScore && D == 128)) ? 1 : 2;
+  static constexpr int kQ = 0;  // kSlots query slots
+  static constexpr int kK = kQ + kSlots * kTile;
   static constexpr int kV = kK + kKVStages * kTile;
-  static constexpr int kRing = kV + kKVStages * kTile;  // [2 slots][kRingDepth] entries
+  static constexpr int kRing = kV + kKVStages * kTile;  // [kSlots][kRingDepth] entries
   static constexpr int kRingRoom = 232448 - 1024 - 512 - kRing;
-  static constexpr int kRingFit = kRingRoom / (2 * kRingEntry);
+  static constexpr int kRingFit = kRingRoom / (kSlots * kRingEntry);
   static constexpr int kRingDepth = kScore ? (kRingFit < 4 ? kRingFit : 4) : 0;
-  static constexpr int kBar = kRing + 2 * kRingDepth * kRingEntry;
+  static constexpr int kBar = kRing + kSlots * kRingDepth * kRingEntry;
   static constexpr int kNumBars = 16 + 4 * kRingDepth;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
@@ -136,14 +140,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
   const int h = blockIdx.x;
   const int b = blockIdx.z;
   const int hk = h / (p.Hq / p.Hk);
-  const int q0 = qblk * 256;
+  const int q0 = qblk * 128 * L::kSlots;
 
   SlotTiles<kMask> tiles0, tiles1;
   {
     const uint8_t* row = nullptr;
     if (kMask && p.mask_blocks) row = p.mask_blocks + b * p.mb_stride[0] + h * p.mb_stride[1];
     tiles0.n = kv_tile_count(q0, min(q0 + 128, p.Tq), p.Tq, p.Tk, p.causal, p.causal_off);
-    tiles1.n = kv_tile_count(q0 + 128, min(q0 + 256, p.Tq), p.Tq, p.Tk, p.causal, p.causal_off);
+    tiles1.n = L::kSlots == 2 ? kv_tile_count(q0 + 128, min(q0 + 256, p.Tq), p.Tq, p.Tk, p.causal, p.causal_off) : 0;
     tiles0.map = (row && tiles0.n > 0) ? row + static_cast<int64_t>(q0 / 128) * p.nkb : nullptr;
     tiles1.map = (row && tiles1.n > 0) ? row + static_cast<int64_t>(q0 / 128 + 1) * p.nkb : nullptr;
   }
@@ -192,9 +196,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       uint8_t* sQ = smem + L::kQ;
       uint8_t* sK = smem + L::kK;
       uint8_t* sV = smem + L::kV;
-      mbar_arrive_expect_tx(q_full, 2 * L::kTile);
+      mbar_arrive_expect_tx(q_full, L::kSlots * L::kTile);
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+      for (int t = 0; t < L::kSlots; ++t)
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
           tma_load_4d(sQ + t * L::kTile + c * 16384, &p.tm_q, q_full, c * 64, q0 + 128 * t, h, b);
@@ -341,6 +345,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     }
     __syncwarp();
     }
+  } else if ((warp - 4) >> 2 >= L::kSlots) {
+    regs_inc<kFwdRegsSoftmax>();  // a slot this CTA does not have (D=256): nothing to do
   } else {
     regs_inc<kFwdRegsSoftmax>();
     // ------------------------------------------------------------ softmax + epilogue
@@ -660,7 +666,7 @@ cudaError_t launch_fwd_t(const FwdParams& p, cudaStream_t s) {
   auto kern = fwd_kernel<D, kBF16, kMask, kScore>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.Hq, (p.Tq + 255) / 256, p.B);
+  dim3 grid(p.Hq, (p.Tq + 128 * L::kSlots - 1) / (128 * L::kSlots), p.B);
   kern<<<grid, kFwdThreads, L::kAlloc, s>>>(p);
   return cudaGetLastError();
 }
@@ -680,6 +686,8 @@ cudaError_t launch_fwd(const FwdParams& p, int D, bool bf16, bool has_mask, bool
                             : launch_fwd_d<128, false>(p, has_mask, has_score, s);
   if (D == 64) return bf16 ? launch_fwd_d<64, true>(p, has_mask, has_score, s)
                            : launch_fwd_d<64, false>(p, has_mask, has_score, s);
+  if (D == 256) return bf16 ? launch_fwd_d<256, true>(p, has_mask, has_score, s)
+                            : launch_fwd_d<256, false>(p, has_mask, has_score, s);
   return cudaErrorInvalidValue;
 }
 

@@ -113,7 +113,7 @@ def _fwd_args(**kw):
     "kw,code",
     [
         (dict(D=80), _lib.FA4D_ERR_UNSUPPORTED),
-        (dict(D=256), _lib.FA4D_ERR_UNSUPPORTED),
+        (dict(D=512), _lib.FA4D_ERR_UNSUPPORTED),
         (dict(Hq=3, Hk=2), _lib.FA4D_ERR_INVALID),
         (dict(B=0), _lib.FA4D_ERR_INVALID),
         (dict(dtype=7), _lib.FA4D_ERR_INVALID),
@@ -146,3 +146,8 @@ def test_bwd_rejects_bad_flag_and_small_workspace():
     a.deterministic = 0
     a.workspace, a.workspace_bytes = 0x1000, 16
     assert lib.fa4d_bwd(ctypes.byref(a), None) == _lib.FA4D_ERR_WORKSPACE
+    # Head dim 256 is forward only: every backward entry refuses it before device work.
+    a.D = 256
+    for entry in ("fa4d_bwd", "fa4d_bwd_noalloc", "fa4d_bwd_main"):
+        assert getattr(lib, entry)(ctypes.byref(a), None) == _lib.FA4D_ERR_UNSUPPORTED, entry
+        assert b"256" in lib.fa4d_last_error()

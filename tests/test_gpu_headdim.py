@@ -90,3 +90,71 @@ def test_stores_stay_inside_the_head(deterministic):
     ref = oracle(*bhsd, causal=True, device="cpu")
     got = tuple(t[..., :D].transpose(1, 2) for t in (o_w, dq_w, dk_w, dv_w))
     check(got, ref, "D96 strided outputs")
+
+
+# ---------------------------------------------------------------- head dim 256 (forward only)
+D256 = 256
+
+
+def _fwd_only(q, k, v, layout="bhsd", **kw):
+    """O from the public wrapper without autograd; q/k/v given BHSD."""
+    from conftest import from_layout, to_layout
+    import tilelang_fa2_4d_mask as api
+
+    with torch.no_grad():
+        out = api.tilelang_flash_attention(*(to_layout(x.to(DEV), layout) for x in (q, k, v)), layout=layout, **kw)
+    return from_layout(out, layout)
+
+
+def _check_out(out, ref, what):
+    from conftest import out_err
+    from test_gpu_parity import O_MAX, O_MEAN
+
+    mx, mean = out_err(out, ref)
+    bound = max(O_MEAN, 2.0 ** -8 * float(ref.float().abs().mean()))
+    assert mx <= O_MAX and mean <= bound, f"{what} O max_abs={mx:.3e} mean_abs={mean:.3e}"
+
+
+def _ref_out(q, k, v, mask=None, score=None, causal=False, offset=0):
+    from oracle.eager import attention_ref
+
+    return attention_ref(q.float(), k.float(), v.float(), mask, score, scale=q.shape[-1] ** -0.5, is_causal=causal,
+                         causal_offset=offset)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_d256_forward_dense_gqa(causal):
+    q, k, v, _ = I.qkv(2, 333, 333, 4, 2, D256, seed=100)
+    _check_out(_fwd_only(q, k, v, is_causal=causal), _ref_out(q, k, v, causal=causal), f"D256 c={causal}")
+
+
+def test_d256_forward_long_causal_and_fp16():
+    q, k, v, _ = I.qkv(1, 1024, 1024, 8, 2, D256, seed=101)
+    _check_out(_fwd_only(q, k, v, is_causal=True), _ref_out(q, k, v, causal=True), "D256 T1024")
+    q, k, v, _ = I.qkv(1, 300, 300, 2, 1, D256, seed=102, dtype=torch.float16)
+    _check_out(_fwd_only(q, k, v), _ref_out(q, k, v), "D256 fp16")
+
+
+def test_d256_forward_mask_score_and_docs():
+    B, T, H = 1, 640, 4
+    q, k, v, _ = I.qkv(B, T, T, H, H, D256, seed=103)
+    mask = I.random_mask(B, H, T, T, 0.9, seed=104)
+    score = I.alibi_score(B, H, T, T, seed=105)
+    _check_out(_fwd_only(q, k, v, mask=mask.to(DEV), score=score.to(DEV)), _ref_out(q, k, v, mask=mask, score=score),
+               "D256 mask+score")
+    ids = I.packed_doc_ids(B, T, min_len=100, max_len=300, seed=106)
+    _check_out(_fwd_only(q, k, v, doc_ids=ids.to(DEV), is_causal=True),
+               _ref_out(q, k, v, mask=I.doc_mask(ids, ids), causal=True), "D256 docs")
+
+
+def test_d256_forward_bshd_bottom_right():
+    Tq, Tk = 200, 384
+    q, k, v, _ = I.qkv(2, Tq, Tk, 4, 1, D256, seed=107)
+    out = _fwd_only(q, k, v, layout="bshd", is_causal=True, causal_align="bottom_right")
+    _check_out(out, _ref_out(q, k, v, causal=True, offset=Tk - Tq), "D256 bshd bottom-right")
+
+
+def test_d256_backward_is_refused():
+    q, k, v, do = I.qkv(1, 128, 128, 2, 1, D256, seed=108)
+    with pytest.raises(ValueError, match="head dim 256"):
+        run_api(q, k, v, do)
