@@ -22,6 +22,8 @@
 // Mask tiles (PARTIAL blocks only) and score chunks reach shared memory by TMA
 // through a per-slot ring, so the softmax threads read them with 16-B shared loads
 // instead of waiting on global memory.
+// At D=256 the CTA has one slot (S0 and O0 [256,512) fill TMEM's 512 columns) and
+// warps 8-11 stay idle.
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
 // P (16-bit) overwrites the first 64 columns of S and feeds the PV MMA from TMEM.
 #include <cfloat>
