@@ -138,6 +138,7 @@ def run_ours(args):
 
 def _run_ours(args, _lib):
     import tilelang_fa2_4d_mask as api
+    from fa2_with_4d_mask_b200 import shard
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -156,9 +157,12 @@ def _run_ours(args, _lib):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     peaks, peak_src = load_peaks()
 
-    # Rank r owns batch element r of the global batch (weak scaling).
+    # Rank r owns batch element r of the global batch (weak scaling): with B = 1 per
+    # rank, the rank's (batch, KV head) units are exactly that element's KV heads.
+    (seg,) = shard.segments(world * B, HK, rank, world)
+    assert (seg.b, seg.hk0, seg.hk1) == (rank * B, 0, HK)
     g = torch.Generator(device=dev)
-    g.manual_seed(1000 + rank)
+    g.manual_seed(1000 + seg.b)
     mk = lambda shape: torch.randn(shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
     q = mk((B, T, HQ, D))
     k = mk((B, T, HK, D))
@@ -234,16 +238,14 @@ def _run_ours(args, _lib):
     ms = {k2: sum(a.elapsed_time(b) for a, b in v2) / max(1, len(v2)) for k2, v2 in rec.items()}
     ms["step_eager"] = ms.pop("step")
     ms["step"] = sum(a.elapsed_time(b) for a, b in steps_ev) / len(steps_ev)
-    step_ms = torch.tensor([ms["step"]], device=dev, dtype=torch.float64)
+    t_step = shard.max_over_ranks(ms["step"], dist, dev)
     if dist:
-        dist.all_reduce(step_ms, op=dist.ReduceOp.MAX)
         # Verification only (outside the timed region): per-rank output checksums.
         chk = o.float().abs().sum().reshape(1)
         allchk = [torch.zeros_like(chk) for _ in range(world)]
         dist.all_gather(allchk, chk)
         if rank == 0 and not all(torch.isfinite(c).all() for c in allchk):
             raise SystemExit("non-finite output on some rank")
-    t_step = float(step_ms.item())
     per_rank = fwd_bwd_flops(B, HQ, T, T, D, False)
     value = world * per_rank / (t_step * 1e-3) / 1e12
     status = _lib.device_status(dev)
@@ -509,6 +511,8 @@ def run_e2e(api, dev, args, dist=None, world=1):
     and step i-1's download overlap step i's compute (PCIe is full duplex).  Every rank
     runs it on its own batch element; the step time is the max over ranks and the value
     is whole-job (all ranks' FLOPs)."""
+    from fa2_with_4d_mask_b200 import shard
+
     g = torch.Generator()
     g.manual_seed(77)
     host = lambda shape: torch.randn(shape, generator=g).to(torch.bfloat16).pin_memory()
@@ -569,10 +573,7 @@ def run_e2e(api, dev, args, dist=None, world=1):
     comp.wait_stream(down)
     b.record(comp)
     torch.cuda.synchronize(dev)
-    t = torch.tensor([a.elapsed_time(b) / args.e2e_steps], device=dev, dtype=torch.float64)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms = shard.max_over_ranks(a.elapsed_time(b) / args.e2e_steps, dist, dev)
     return {"value": round(world * fwd_bwd_flops(B, HQ, T, T, D, False) / (ms * 1e-3) / 1e12, 2), "unit": UNIT,
             "ms_per_step": round(ms, 4), "h2d_bytes_per_step": world * h2d, "d2h_bytes_per_step": world * d2h,
             "path": "tilelang_flash_attention + autograd backward; each step uploads its pinned inputs and "
