@@ -203,10 +203,11 @@ int check_common(int B, int Tq, int Tk, int Hq, int Hk, int D, int dtype, int ca
   return FA4D_OK;
 }
 
-// Head dims the backward is built for: dK and dV of a 128-key tile at D = 256 would
-// take all 512 TMEM columns, so that head dim is forward only.
-int check_bwd_dim(int D) {
-  if (D == 256) return fail(FA4D_ERR_UNSUPPORTED, "head dim 256: the backward is not built (forward only)");
+// Backward modes built per head dim: at D = 256 the deterministic dQ kernel (one CTA
+// per 128-row query tile, its dQ accumulator alone 256 TMEM columns) is not built.
+int check_bwd_dim(int D, int deterministic) {
+  if (D == 256 && deterministic)
+    return fail(FA4D_ERR_UNSUPPORTED, "head dim 256: deterministic dQ is not built (use deterministic = 0)");
   return FA4D_OK;
 }
 
@@ -272,9 +273,10 @@ KeyTileWork key_tile_work(int Tq, int Tk, int causal) {
 int group_split(int B, int Tq, int Tk, int Hq, int Hk, int D, int causal) {
   const int G = Hq / Hk;
   const int nkb = (Tk + 127) / 128;
-  const double base = static_cast<double>(nkb) * Hk * B;
+  // At D = 256 a CTA pair shares each key tile (one per half of the output columns).
+  const double base = static_cast<double>(nkb) * Hk * B * (D == 256 ? 2 : 1);
   const double sms = sm_count();
-  const double tile_us = D > 64 ? 1.5 : 0.9;
+  const double tile_us = D == 256 ? 2.0 : (D > 64 ? 1.5 : 0.9);
   const KeyTileWork w = key_tile_work(Tq, Tk, causal);
   const double mean_nq = w.mean_nq, max_nq = w.max_nq;
   const bool uniform = w.equal;
@@ -572,7 +574,8 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse)
     return fail(FA4D_ERR_INVALID, "q, k, v, o, dout and lse are required");
   if (a->deterministic != 0 && a->deterministic != 1) return fail(FA4D_ERR_INVALID, "deterministic must be 0 or 1");
-  if ((rc = check_bwd_dim(a->D))) return rc;
+  if ((rc = check_bwd_dim(a->D, a->deterministic))) return rc;
+  if (a->D == 256 && (rc = check_rows16(a->v, a->v_stride, "v"))) return rc;
   if ((rc = check_rows16(a->dq, a->dq_stride, "dq"))) return rc;
   if ((rc = check_rows16(a->dk, a->dk_stride, "dk"))) return rc;
   if ((rc = check_rows16(a->dv, a->dv_stride, "dv"))) return rc;
@@ -608,11 +611,13 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   p.d_out = a->D;
   p.dk = a->dk;
   p.dv = a->dv;
+  p.v = a->v;
   p.mask = a->mask;
   p.score = a->score;
   for (int i = 0; i < 3; ++i) {
     p.dk_stride[i] = a->dk_stride[i];
     p.dv_stride[i] = a->dv_stride[i];
+    p.v_stride[i] = a->v_stride[i];
     p.mask_stride[i] = a->mask_stride[i];
     p.score_stride[i] = a->score_stride[i];
   }
@@ -851,7 +856,7 @@ int fa4d_bwd_noalloc(const fa4d_bwd_args* a, void* stream) {
   if (!a) return fail(FA4D_ERR_INVALID, "args is NULL");
   int rc = check_common(a->B, a->Tq, a->Tk, a->Hq, a->Hk, a->D, a->dtype, a->causal, a->scale);
   if (rc) return rc;
-  if ((rc = check_bwd_dim(a->D))) return rc;
+  if ((rc = check_bwd_dim(a->D, a->deterministic))) return rc;
   const size_t need = fa4d_bwd_workspace_size(a->B, a->Tq, a->Hq, a->D);
   if (need > kNoAllocScratchBytes)
     return fail(FA4D_ERR_WORKSPACE,

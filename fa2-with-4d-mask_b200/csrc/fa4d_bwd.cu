@@ -30,6 +30,7 @@
 #include "fa4d.h"
 #include "fa4d_kernels.h"
 #include "fa4d_ptx.cuh"
+#include "fa4d_tiles.cuh"
 
 namespace fa4d {
 
@@ -107,36 +108,6 @@ __device__ __forceinline__ void issue_dq(uint32_t tD, uint32_t sK, uint32_t sDS)
     mma_ss(tD, sw128_desc(sK + kk * 2048, 16384, 1024), sw128_desc(sDS + kk * 2048, 8192, 1024), idesc,
            kk > 0 ? 1u : 0u);
 }
-
-// The (query head g of the GQA group, 64-row query tile) pairs a key tile visits, in
-// order g-major, minus those whose 128 x 128 block the mask's block map marks EMPTY
-// (block-sparse skipping; the reference visits every pair, python/fa2.py:242).
-template <bool kMask>
-struct QTiles {
-  const uint8_t* map;  // block map at (head 0 of the group, query block 0, this key block), or null
-  int64_t head_stride, row_stride;
-  int nq, first_qt, N;  // N = G * nq pairs before skipping
-  int lin;              // current pair g * nq + qi; lin >= N past the end
-  __device__ __forceinline__ int g() const { return lin / nq; }
-  __device__ __forceinline__ int q0() const { return (first_qt + lin % nq) * 64; }
-  // 0: skip; 1: visit and apply the mask; 2: visit, the mask keeps every pair.
-  __device__ __forceinline__ int state() const {
-    if (!kMask) return 2;
-    if (!map) return 1;
-    const int gg = lin / nq;
-    const int v = __ldg(map + gg * head_stride + ((first_qt + lin - gg * nq) >> 1) * row_stride);
-    return v == 0 ? 0 : (v == 2 ? 2 : 1);
-  }
-  __device__ __forceinline__ bool valid() const { return lin < N; }
-  __device__ __forceinline__ void skip_empty() {
-    if (kMask && map)
-      while (lin < N && state() == 0) ++lin;
-  }
-  __device__ __forceinline__ void advance() {
-    ++lin;
-    skip_empty();
-  }
-};
 
 template <int D, bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_constant__ BwdParams p) {
@@ -768,6 +739,7 @@ cudaError_t launch_bwd(const BwdParams& p, int D, bool bf16, bool has_mask, bool
                             : launch_bwd_d<128, false>(p, has_mask, has_score, s);
   if (D == 64) return bf16 ? launch_bwd_d<64, true>(p, has_mask, has_score, s)
                            : launch_bwd_d<64, false>(p, has_mask, has_score, s);
+  if (D == 256) return launch_bwd256(p, bf16, has_mask, has_score, s);
   return cudaErrorInvalidValue;
 }
 
@@ -784,6 +756,9 @@ cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s) {
   } else if (p.D == 64) {
     if (bf16) bwd_prep_kernel<64, true><<<blocks, threads, 0, s>>>(p);
     else bwd_prep_kernel<64, false><<<blocks, threads, 0, s>>>(p);
+  } else if (p.D == 256) {
+    if (bf16) bwd_prep_kernel<256, true><<<blocks, threads, 0, s>>>(p);
+    else bwd_prep_kernel<256, false><<<blocks, threads, 0, s>>>(p);
   } else {
     return cudaErrorInvalidValue;
   }

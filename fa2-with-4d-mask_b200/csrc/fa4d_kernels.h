@@ -107,6 +107,10 @@ struct BwdParams {
   // is in L2 (equal-work grids); 0: grid (KV head x split, key tiles, B), the longest
   // key tiles first (causal and block-sparse grids).
   int32_t kb_fastest;
+  // V itself (16-bit, strides (b, t, h) in elements, rows 16-B aligned): the D = 256
+  // kernel copies each key's V row into tensor memory with plain loads.
+  const void* v;
+  int64_t v_stride[3];
 };
 
 // Deterministic dQ: one CTA per 128-row query tile of one (batch, head) walks its key
@@ -208,6 +212,7 @@ struct ConvertParams {
 
 cudaError_t launch_fwd(const FwdParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);
 cudaError_t launch_bwd(const BwdParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);
+cudaError_t launch_bwd256(const BwdParams& p, bool bf16, bool has_mask, bool has_score, cudaStream_t s);
 cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dkv_convert(const DkvConvertParams& p, bool bf16, cudaStream_t s);

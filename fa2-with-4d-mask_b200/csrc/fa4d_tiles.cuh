@@ -1,6 +1,7 @@
 // fa4d_tiles.cuh — which 128-key tiles a 128-row query tile visits (key bound, causal
 // limit, EMPTY blocks of the mask's block map) and the keep bits of a mask row read as
-// bytes; shared by the forward and the deterministic dQ kernels.
+// bytes; shared by the forward and the deterministic dQ kernels; and the (query head,
+// 64-row query tile) pairs a 128-key tile of the backward visits.
 #pragma once
 
 #include <cstdint>
@@ -43,6 +44,36 @@ struct SlotTiles {
     int kt = n - 1;
     while (kt >= 0 && state(kt) == 0) --kt;
     return kt;
+  }
+};
+
+// The (query head g of the GQA group, 64-row query tile) pairs a key tile visits, in
+// order g-major, minus those whose 128 x 128 block the mask's block map marks EMPTY
+// (block-sparse skipping; the reference visits every pair, python/fa2.py:242).
+template <bool kMask>
+struct QTiles {
+  const uint8_t* map;  // block map at (head 0 of the group, query block 0, this key block), or null
+  int64_t head_stride, row_stride;
+  int nq, first_qt, N;  // N = G * nq pairs before skipping
+  int lin;              // current pair g * nq + qi; lin >= N past the end
+  __device__ __forceinline__ int g() const { return lin / nq; }
+  __device__ __forceinline__ int q0() const { return (first_qt + lin % nq) * 64; }
+  // 0: skip; 1: visit and apply the mask; 2: visit, the mask keeps every pair.
+  __device__ __forceinline__ int state() const {
+    if (!kMask) return 2;
+    if (!map) return 1;
+    const int gg = lin / nq;
+    const int v = __ldg(map + gg * head_stride + ((first_qt + lin - gg * nq) >> 1) * row_stride);
+    return v == 0 ? 0 : (v == 2 ? 2 : 1);
+  }
+  __device__ __forceinline__ bool valid() const { return lin < N; }
+  __device__ __forceinline__ void skip_empty() {
+    if (kMask && map)
+      while (lin < N && state() == 0) ++lin;
+  }
+  __device__ __forceinline__ void advance() {
+    ++lin;
+    skip_empty();
   }
 };
 

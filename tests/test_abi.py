@@ -146,8 +146,11 @@ def test_bwd_rejects_bad_flag_and_small_workspace():
     a.deterministic = 0
     a.workspace, a.workspace_bytes = 0x1000, 16
     assert lib.fa4d_bwd(ctypes.byref(a), None) == _lib.FA4D_ERR_WORKSPACE
-    # Head dim 256 is forward only: every backward entry refuses it before device work.
+    # Head dim 256: the backward passes the head-dim check (and fails on the workspace
+    # here); its deterministic mode is refused by every backward entry before device work.
     a.D = 256
+    assert lib.fa4d_bwd(ctypes.byref(a), None) == _lib.FA4D_ERR_WORKSPACE
+    a.deterministic = 1
     for entry in ("fa4d_bwd", "fa4d_bwd_noalloc", "fa4d_bwd_main"):
         assert getattr(lib, entry)(ctypes.byref(a), None) == _lib.FA4D_ERR_UNSUPPORTED, entry
         assert b"256" in lib.fa4d_last_error()

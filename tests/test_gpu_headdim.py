@@ -1,10 +1,15 @@
-"""GPU: head dim 96 against the oracle, through the public API.
+"""GPU: head dims 96 and 256 against the oracle, through the public API.
 
 D = 96 runs the D = 128 kernels on tiles whose columns 96..127 the tensor maps fill
 with zeros; only the first 96 columns of O, dQ, dK and dV are stored.  The cases cover
 each kernel variant that this reaches (dense, causal, GQA, bool mask + fp32 score,
 document ids, the split-group and deterministic backward, fp16, BSHD with bottom-right
 causal), plus a direct check that nothing is written past column 96 of each output row.
+
+D = 256 runs its own kernels: the forward with one 128-row query slot per CTA, the
+backward with a CTA pair per key tile, each CTA owning half of the dK / dV / dQ
+columns.  The same variants are covered, except the deterministic backward, which is
+not built at this head dim and must be refused.
 """
 
 from __future__ import annotations
@@ -92,7 +97,7 @@ def test_stores_stay_inside_the_head(deterministic):
     check(got, ref, "D96 strided outputs")
 
 
-# ---------------------------------------------------------------- head dim 256 (forward only)
+# ---------------------------------------------------------------- head dim 256
 D256 = 256
 
 
@@ -154,7 +159,51 @@ def test_d256_forward_bshd_bottom_right():
     _check_out(out, _ref_out(q, k, v, causal=True, offset=Tk - Tq), "D256 bshd bottom-right")
 
 
-def test_d256_backward_is_refused():
-    q, k, v, do = I.qkv(1, 128, 128, 2, 1, D256, seed=108)
+@pytest.mark.parametrize("causal", [False, True])
+def test_d256_backward_dense_gqa_odd_length(causal):
+    q, k, v, do = I.qkv(2, 333, 333, 4, 2, D256, seed=110)
+    check(run_api(q, k, v, do, is_causal=causal), oracle(q, k, v, do, causal=causal, device="cpu"),
+          f"D256 bwd c={causal}")
+
+
+def test_d256_backward_longer_causal():
+    q, k, v, do = I.qkv(1, 1024, 1024, 8, 2, D256, seed=111)
+    check(run_api(q, k, v, do, is_causal=True), oracle(q, k, v, do, causal=True), "D256 bwd T1024")
+
+
+def test_d256_backward_mask_and_score():
+    B, T, H = 1, 640, 4
+    q, k, v, do = I.qkv(B, T, T, H, H, D256, seed=112)
+    mask = I.random_mask(B, H, T, T, 0.9, seed=113)
+    score = I.alibi_score(B, H, T, T, seed=114)
+    got = run_api(q, k, v, do, mask=mask.to(DEV), score=score.to(DEV))
+    check(got, oracle(q, k, v, do, mask=mask, score=score), "D256 bwd mask+score")
+
+
+def test_d256_backward_document_ids():
+    B, T = 2, 768
+    q, k, v, do = I.qkv(B, T, T, 4, 1, D256, seed=115)
+    ids = I.packed_doc_ids(B, T, min_len=100, max_len=300, seed=116)
+    got = run_api(q, k, v, do, doc_ids=ids.to(DEV), is_causal=True)
+    check(got, oracle(q, k, v, do, mask=I.doc_mask(ids, ids), causal=True), "D256 bwd docs")
+
+
+def test_d256_backward_mqa_bshd_bottom_right_split():
+    """MQA with few key tiles takes the split-group backward (fp32 slices of width 256,
+    each CTA of a pair writing its half)."""
+    B, Tq, Tk, Hq, Hk = 2, 200, 384, 16, 1
+    assert _lib.load_library().fa4d_bwd_group_split(B, Tq, Tk, Hq, Hk, D256, _lib.CAUSAL_BOTTOM_RIGHT) > 1
+    q, k, v, do = I.qkv(B, Tq, Tk, Hq, Hk, D256, seed=117)
+    got = run_api(q, k, v, do, layout="bshd", is_causal=True, causal_align="bottom_right")
+    check(got, oracle(q, k, v, do, causal=True, offset=Tk - Tq), "D256 bwd mqa split")
+
+
+def test_d256_backward_fp16():
+    q, k, v, do = I.qkv(1, 300, 300, 4, 2, D256, seed=118, dtype=torch.float16)
+    check(run_api(q, k, v, do, is_causal=True), oracle(q, k, v, do, causal=True, device="cpu"), "D256 bwd fp16")
+
+
+def test_d256_deterministic_backward_is_refused():
+    q, k, v, do = I.qkv(1, 128, 128, 2, 1, D256, seed=119)
     with pytest.raises(ValueError, match="head dim 256"):
-        run_api(q, k, v, do)
+        run_api(q, k, v, do, use_atomic_backward=False)
