@@ -203,14 +203,6 @@ int check_common(int B, int Tq, int Tk, int Hq, int Hk, int D, int dtype, int ca
   return FA4D_OK;
 }
 
-// Backward modes built per head dim: at D = 256 the deterministic dQ kernel (one CTA
-// per 128-row query tile, its dQ accumulator alone 256 TMEM columns) is not built.
-int check_bwd_dim(int D, int deterministic) {
-  if (D == 256 && deterministic)
-    return fail(FA4D_ERR_UNSUPPORTED, "head dim 256: deterministic dQ is not built (use deterministic = 0)");
-  return FA4D_OK;
-}
-
 // Row pointers of a [.., D] output written with 16-byte stores.
 int check_rows16(const void* ptr, const int64_t st[3], const char* name) {
   if (!ptr) return fail(FA4D_ERR_INVALID, "%s is NULL", name);
@@ -574,7 +566,6 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse)
     return fail(FA4D_ERR_INVALID, "q, k, v, o, dout and lse are required");
   if (a->deterministic != 0 && a->deterministic != 1) return fail(FA4D_ERR_INVALID, "deterministic must be 0 or 1");
-  if ((rc = check_bwd_dim(a->D, a->deterministic))) return rc;
   if (a->D == 256 && (rc = check_rows16(a->v, a->v_stride, "v"))) return rc;
   if ((rc = check_rows16(a->dq, a->dq_stride, "dq"))) return rc;
   if ((rc = check_rows16(a->dk, a->dk_stride, "dk"))) return rc;
@@ -682,7 +673,9 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
     }
   }
 
-  if (a->deterministic) {
+  // At D = 256 dQ always comes from the ordered pass: the D = 256 main kernel has no
+  // dQ products (measured slower there than the separate pass).
+  if (a->deterministic || a->D == 256) {
     // dQ from its own kernel (one CTA per query tile, key tiles in order); the main
     // kernel skips its dQ products and nothing is accumulated.
     plan->deterministic = true;
@@ -690,8 +683,10 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
     fa4d::DqParams& d = plan->dq;
     if ((rc = encode_bthd(&d.tm_q, a->q, a->B, a->Tq, a->Hq, a->D, a->q_stride, 128, bf16, "q"))) return rc;
     if ((rc = encode_bthd(&d.tm_do, a->dout, a->B, a->Tq, a->Hq, a->D, a->do_stride, 128, bf16, "dout"))) return rc;
-    if ((rc = encode_bthd(&d.tm_k, a->k, a->B, a->Tk, a->Hk, a->D, a->k_stride, 128, bf16, "k"))) return rc;
-    if ((rc = encode_bthd(&d.tm_v, a->v, a->B, a->Tk, a->Hk, a->D, a->v_stride, 128, bf16, "v"))) return rc;
+    // Key tiles are loaded whole, or in 64-row halves at D = 256 (fa4d_dq256.cu).
+    const int kv_rows = a->D == 256 ? 64 : 128;
+    if ((rc = encode_bthd(&d.tm_k, a->k, a->B, a->Tk, a->Hk, a->D, a->k_stride, kv_rows, bf16, "k"))) return rc;
+    if ((rc = encode_bthd(&d.tm_v, a->v, a->B, a->Tk, a->Hk, a->D, a->v_stride, kv_rows, bf16, "v"))) return rc;
     d.lse = a->lse;
     d.delta = delta;
     d.dq = a->dq;
@@ -736,7 +731,7 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   pp.o = a->o;
   pp.dout = a->dout;
   pp.delta = delta;
-  pp.dq_acc = a->deterministic ? nullptr : dq_acc;
+  pp.dq_acc = plan->deterministic ? nullptr : dq_acc;
   for (int i = 0; i < 3; ++i) {
     pp.o_stride[i] = a->o_stride[i];
     pp.do_stride[i] = a->do_stride[i];
@@ -856,7 +851,6 @@ int fa4d_bwd_noalloc(const fa4d_bwd_args* a, void* stream) {
   if (!a) return fail(FA4D_ERR_INVALID, "args is NULL");
   int rc = check_common(a->B, a->Tq, a->Tk, a->Hq, a->Hk, a->D, a->dtype, a->causal, a->scale);
   if (rc) return rc;
-  if ((rc = check_bwd_dim(a->D, a->deterministic))) return rc;
   const size_t need = fa4d_bwd_workspace_size(a->B, a->Tq, a->Hq, a->D);
   if (need > kNoAllocScratchBytes)
     return fail(FA4D_ERR_WORKSPACE,

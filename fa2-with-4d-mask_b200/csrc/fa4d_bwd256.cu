@@ -5,12 +5,14 @@
 // factor `scale`, applied to dK in its epilogue and to dQ at conversion).  At D = 256
 // the dK and dV accumulators of a 128-key tile would take all 512 TMEM columns, so the
 // output columns are split: CTA pair (ch = 0, 1) shares one 128-key tile of one
-// (batch, KV head) and CTA ch owns columns [128 ch, 128 ch + 128) of dK, dV and dQ.
+// (batch, KV head) and CTA ch owns columns [128 ch, 128 ch + 128) of dK and dV.
 // Both CTAs of a pair compute the full S^T = K Q^T and dP^T = V dO^T (contraction over
-// all 256 columns); each then does its half of dV += P^T dO, dK += dS^T Q and
-// dQ^T = K^T dS^T.
+// all 256 columns); each then does its half of dV += P^T dO and dK += dS^T Q.
+// dQ comes from the ordered pass (dq256_kernel, fa4d_dq256.cu) at this head dim: with
+// one S / dP buffer pair, adding dQ^T here (its product and drain between one tile's
+// dS and the next tile's dP) ran slower than the separate pass.
 //
-// CTA = 128 keys x one (batch, KV head) x one column half; 512 threads:
+// CTA = 128 keys x one (batch, KV head) x one column half; 384 threads:
 //   warp 0       TMA producer (K once; Q, dO, LSE, Delta per 64-row query tile,
 //                2-stage ring)
 //   warp 1       tcgen05.mma issuer
@@ -18,12 +20,10 @@
 //   warps 4-7    queries 0-31 of every tile (one thread per key row), then dV out;
 //                at the start they copy V columns 0-127 into TMEM
 //   warps 8-11   queries 32-63 of every tile, then dK out; V columns 128-255
-//   warps 12-15  dQ drain: TMEM -> shared staging -> bulk reduce-add into global
 // TMEM (512 columns): S^T [0,64) (P^T of queries 0-31 then 32-63 is written over
-// columns [0,16) and [32,48)), X [64,128) (dP^T, later dQ^T), V [128,256) (16-bit
-// pairs, the A operand of dP^T), dV half [256,384), dK half [384,512).
-// Shared memory: K 64 KB, Q and dO 2 x 32 KB each, dS^T 16 KB, a 32 x 128 fp32 dQ
-// staging tile 16 KB, LSE / Delta: 226 KB.
+// columns [0,16) and [32,48)), dP^T [64,128), V [128,256) (16-bit pairs, the A
+// operand of dP^T), dV half [256,384), dK half [384,512).
+// Shared memory: K 64 KB, Q and dO 2 x 32 KB each, dS^T 16 KB, LSE / Delta: 210 KB.
 #include <algorithm>
 
 #include "fa4d.h"
@@ -35,35 +35,33 @@ namespace fa4d {
 
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 384;
 constexpr int kStages = 2;
-// Register split (launch: 512 threads x 128 = 65536): producer/MMA warpgroup 88,
-// P/dS warpgroups 152, dQ drain 112 -> 128*88 + 256*152 + 128*112 = 64512.
-constexpr uint32_t kRegsLaunch = 128, kRegsCtl = 88, kRegsSoftmax = 152, kRegsDrain = 112;
-static_assert(128 * kRegsCtl + 256 * kRegsSoftmax + 128 * kRegsDrain <= kThreads * kRegsLaunch,
+// Register split (launch: 384 threads x 168 = 64512): producer/MMA warpgroup 112,
+// P/dS warpgroups 192 -> 128*112 + 256*192 = 63488.
+constexpr uint32_t kRegsLaunch = 168, kRegsCtl = 112, kRegsSoftmax = 192;
+static_assert(128 * kRegsCtl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch,
               "register split exceeds the launch allocation");
 
 struct Layout {
   static constexpr int kKT = 128 * 256 * 2;  // K tile (128 keys x 256)
   static constexpr int kQT = 64 * 256 * 2;   // Q or dO tile (64 queries x 256)
   static constexpr int kDS = 128 * 64 * 2;   // dS^T tile (128 keys x 64 queries, 16-bit)
-  static constexpr int kDQS = 32 * 128 * 4;  // dQ staging (32 queries x 128 columns, fp32)
   static constexpr int kK = 0;
   static constexpr int kQ = kK + kKT;               // kStages stages
   static constexpr int kDO = kQ + kStages * kQT;    // kStages stages
   static constexpr int kDSb = kDO + kStages * kQT;
-  static constexpr int kDQs = kDSb + kDS;
-  static constexpr int kLSE = kDQs + kDQS;            // kStages x 64 floats
+  static constexpr int kLSE = kDSb + kDS;             // kStages x 64 floats
   static constexpr int kDelta = kLSE + kStages * 256;  // kStages x 64 floats
   static constexpr int kBar = kDelta + kStages * 256;
-  static constexpr int kNumBars = 18;
+  static constexpr int kNumBars = 13;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
   static_assert(kAlloc <= 232448, "shared memory beyond the 227 KB per-block limit");
 };
 
-constexpr uint32_t kColS = 0, kColX = 64, kColV = 128, kColDV = 256, kColDK = 384;
+constexpr uint32_t kColS = 0, kColDP = 64, kColV = 128, kColDV = 256, kColDK = 384;
 
 // S^T = K Q^T: M=128 keys, N=64 queries, K=256; both K-major (4 chunks of 64 columns).
 template <bool kBF16>
@@ -110,37 +108,23 @@ __device__ __forceinline__ void issue_dk(uint32_t tD, uint32_t sDS, uint32_t sQh
            (acc || kk > 0) ? 1u : 0u);
 }
 
-// dQ^T_half = K_half^T dS^T: M=128 columns, N=64 queries, K=128 keys; both MN-major.
-template <bool kBF16>
-__device__ __forceinline__ void issue_dq(uint32_t tD, uint32_t sKh, uint32_t sDS) {
-  constexpr uint32_t idesc = make_idesc(128, 64, kBF16, true, true);
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk)
-    mma_ss(tD, sw128_desc(sKh + kk * 2048, 16384, 1024), sw128_desc(sDS + kk * 2048, 8192, 1024), idesc,
-           kk > 0 ? 1u : 0u);
-}
-
 template <bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kThreads, 1) bwd256_kernel(const __grid_constant__ BwdParams p) {
   using L = Layout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  uint64_t* kv_full = bars + 0;     // K in shared memory (TMA)
-  uint64_t* v_full = bars + 1;      // V in TMEM (256 arrivals)
-  uint64_t* dkv_full = bars + 2;    // every dV / dK product done
+  uint64_t* kv_full = bars + 0;    // K in shared memory (TMA)
+  uint64_t* v_full = bars + 1;     // V in TMEM (256 arrivals)
+  uint64_t* dkv_full = bars + 2;   // every dV / dK product done
   uint64_t* mma_drain = bars + 3;
-  uint64_t* stage_free = bars + 4;  // dQ staging tile free (drain leader)
-  uint64_t* stage_full = bars + 5;  // dQ staging tile written (128 arrivals)
-  uint64_t* s_full = bars + 6;      // S^T of the tile is in TMEM
-  uint64_t* p_full = bars + 7;      // P^T written to TMEM (256 arrivals)
-  uint64_t* dp_full = bars + 8;     // dP^T of the tile is in TMEM
-  uint64_t* ds_full = bars + 9;     // dS^T written to shared memory (256 arrivals)
-  uint64_t* ds_empty = bars + 10;   // dS^T buffer free again
-  uint64_t* dq_full = bars + 11;    // dQ^T of the tile is in TMEM
-  uint64_t* dq_empty = bars + 12;   // drain has read dQ^T (128 arrivals)
-  uint64_t* q_full = bars + 13;     // [kStages]
-  uint64_t* q_empty = bars + 15;    // [kStages]
+  uint64_t* s_full = bars + 4;     // S^T of the tile is in TMEM
+  uint64_t* p_full = bars + 5;     // P^T written to TMEM (256 arrivals)
+  uint64_t* dp_full = bars + 6;    // dP^T of the tile is in TMEM
+  uint64_t* ds_full = bars + 7;    // dS^T written to shared memory (256 arrivals)
+  uint64_t* ds_empty = bars + 8;   // dS^T buffer free again
+  uint64_t* q_full = bars + 9;     // [kStages]
+  uint64_t* q_empty = bars + 11;   // [kStages]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -183,15 +167,11 @@ __global__ void __launch_bounds__(kThreads, 1) bwd256_kernel(const __grid_consta
     mbar_init(v_full, 256);
     mbar_init(dkv_full, 1);
     mbar_init(mma_drain, 1);
-    mbar_init(stage_free, 1);
-    mbar_init(stage_full, 128);
     mbar_init(s_full, 1);
     mbar_init(p_full, 256);
     mbar_init(dp_full, 1);
     mbar_init(ds_full, 256);
     mbar_init(ds_empty, 1);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 128);
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
@@ -252,14 +232,14 @@ __global__ void __launch_bounds__(kThreads, 1) bwd256_kernel(const __grid_consta
     } else if (warp == 1) {
       // ---------------------------------------------------------- MMA issuer
       // Per tile: dV after P^T, then S^T of the next tile (its P/dS warps start on it
-      // while dS^T of this tile is finished), dK and dQ after dS^T, then dP^T of the
-      // next tile once the drain has read this tile's dQ^T out of X.
+      // while dS^T of this tile is finished), dK after dS^T, then dP^T of the next tile
+      // (the P/dS warps read this tile's dP^T before dS^T was complete).
       if (any_work) {
         const uint32_t sK = smem_u32(smem + L::kK);
         const uint32_t sQ = smem_u32(smem + L::kQ);
         const uint32_t sDO = smem_u32(smem + L::kDO);
         const uint32_t sDS = smem_u32(smem + L::kDSb);
-        const uint32_t tS = tmem + kColS, tX = tmem + kColX, tV = tmem + kColV;
+        const uint32_t tS = tmem + kColS, tDP = tmem + kColDP, tV = tmem + kColV;
         auto wait = [&](uint64_t* bar, uint32_t parity) {
           return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
         };
@@ -269,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd256_kernel(const __grid_consta
           if (elect_one()) {
             issue_s<kBF16>(tS, sK, sQ);
             tc_commit(s_full);
-            issue_dp<kBF16>(tX, tV, sDO);
+            issue_dp<kBF16>(tDP, tV, sDO);
             tc_commit(dp_full);
           }
           __syncwarp();
@@ -303,24 +283,13 @@ __global__ void __launch_bounds__(kThreads, 1) bwd256_kernel(const __grid_consta
           if (elect_one()) {
             issue_dk<kBF16>(tmem + kColDK, sDS, sQ + qs * L::kQT + ch * 16384, it > 0);
             tc_commit(&q_empty[qs]);
-            if (!p.skip_dq) {
-              // dQ^T overwrites this tile's dP^T (read before ds_full).
-              issue_dq<kBF16>(tX, sK + ch * 32768, sDS);
-              tc_commit(dq_full);
-            }
             tc_commit(ds_empty);
-          }
-          __syncwarp();
-          if (nxt.valid()) {
-            if (!p.skip_dq) ok = wait(dq_empty, par);
-            if (!ok) break;
-            tc_fence_after();
-            if (elect_one()) {
-              issue_dp<kBF16>(tX, tV, sDO + qn * L::kQT);
+            if (nxt.valid()) {
+              issue_dp<kBF16>(tDP, tV, sDO + qn * L::kQT);
               tc_commit(dp_full);
             }
-            __syncwarp();
           }
+          __syncwarp();
           cur = nxt;
         }
         if (elect_one()) {
@@ -331,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd256_kernel(const __grid_consta
         wait(mma_drain, 0);
       }
     }
-  } else if (warp < 12) {
+  } else {
     regs_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ P, dS and dK/dV epilogue
     const int wg = (warp - 4) >> 2;  // queries 32*wg .. 32*wg+31 of every tile
@@ -462,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd256_kernel(const __grid_consta
         const float4* d4 = reinterpret_cast<const float4*>(sDelta + qs * 64 + 32 * wg);
         uint8_t* ds_row = smem + L::kDSb + r * 128;
         uint32_t sr[32];
-        tmem_ld32(tmem + lane_base + kColX + 32 * wg, sr);
+        tmem_ld32(tmem + lane_base + kColDP + 32 * wg, sr);
         tmem_wait_ld();
         uint32_t dsk[16];
 #pragma unroll
@@ -548,55 +517,6 @@ __global__ void __launch_bounds__(kThreads, 1) bwd256_kernel(const __grid_consta
       }
       tc_fence_before();
     }
-  } else {
-    regs_dec<kRegsDrain>();
-    // ------------------------------------------------------------ dQ drain
-    // dQ^T (M = 128 columns of this half) has column d of the half in lane d; each
-    // tile's 64 queries leave in two 32-query halves through the staging tile, one
-    // 512-B bulk reduce-add per query row.
-    const int d = (warp & 3) * 32 + lane;
-    const bool leader = (warp == 12 && lane == 0);
-    float* stage = reinterpret_cast<float*>(smem + L::kDQs);  // [32 queries][128]
-    QTiles<kMask> cur = first;
-    int n = 0;  // staging rounds so far (two per tile)
-    for (int it = 0; !p.skip_dq && cur.valid(); ++it, cur.advance()) {
-      const int h = h_first + cur.g();
-      const int q0 = cur.q0();
-      bool ok = __all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, abort_flag));
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t tDQ = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + kColX;
-      uint32_t v[64];
-      tmem_ld32(tDQ, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-      tmem_ld32(tDQ + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(dq_empty);
-#pragma unroll
-      for (int j = 0; j < 2; ++j, ++n) {
-        // The previous round's reductions must have finished reading the staging tile.
-        if (leader) {
-          bulk_wait_read_all();
-          mbar_arrive(stage_free);
-        }
-        ok = __all_sync(0xffffffffu, mbar_wait(stage_free, n & 1, abort_flag));
-        if (!ok) break;
-#pragma unroll
-        for (int c = 0; c < 32; ++c) stage[c * 128 + d] = __uint_as_float(v[32 * j + c]);
-        fence_async_smem();
-        mbar_arrive(stage_full);
-        if (leader && mbar_wait(stage_full, n & 1, abort_flag)) {
-          // Rows q0 + 32 j + c of head h, columns [128 ch, 128 ch + 128) of the
-          // [B, Hq, lse_ld, 256] accumulator (rows past Tq land in the padding).
-          float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + q0 + 32 * j) * 256 + 128 * ch;
-          for (int c = 0; c < 32; ++c) bulk_reduce_add_f32(dst + c * 256, stage + c * 128, 512);
-          bulk_commit();
-        }
-      }
-      if (!ok) break;
-    }
-    if (leader) bulk_wait_all();
-    tc_fence_before();
   }
 
   __syncthreads();

@@ -374,6 +374,7 @@ cudaError_t launch_dq(const DqParams& p, int D, bool bf16, bool has_mask, bool h
                             : launch_dq_d<128, false>(p, has_mask, has_score, s);
   if (D == 64) return bf16 ? launch_dq_d<64, true>(p, has_mask, has_score, s)
                            : launch_dq_d<64, false>(p, has_mask, has_score, s);
+  if (D == 256) return launch_dq256(p, bf16, has_mask, has_score, s);
   return cudaErrorInvalidValue;
 }
 

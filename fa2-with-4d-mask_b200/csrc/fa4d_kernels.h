@@ -114,11 +114,11 @@ struct BwdParams {
 };
 
 // Deterministic dQ: one CTA per 128-row query tile of one (batch, head) walks its key
-// tiles in order (see fa4d_dq.cu).
+// tiles in order (see fa4d_dq.cu, fa4d_dq256.cu).
 struct DqParams {
   CUtensorMap tm_q;   // dims (D, Tq, Hq, B), box (64, 128, 1, 1)
   CUtensorMap tm_do;
-  CUtensorMap tm_k;   // dims (D, Tk, Hk, B), box (64, 128, 1, 1)
+  CUtensorMap tm_k;   // dims (D, Tk, Hk, B), box (64, 128, 1, 1); (64, 64, 1, 1) at D = 256
   CUtensorMap tm_v;
   const float* lse;
   const float* delta;
@@ -217,6 +217,7 @@ cudaError_t launch_bwd_prep(const PrepParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dq_convert(const ConvertParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dkv_convert(const DkvConvertParams& p, bool bf16, cudaStream_t s);
 cudaError_t launch_dq(const DqParams& p, int D, bool bf16, bool has_mask, bool has_score, cudaStream_t s);
+cudaError_t launch_dq256(const DqParams& p, bool bf16, bool has_mask, bool has_score, cudaStream_t s);
 cudaError_t launch_mask_blocks(const MaskBlocksParams& p, cudaStream_t s);
 cudaError_t launch_mask_prepare(const MaskPrepParams& p, cudaStream_t s);
 cudaError_t launch_wait_timeout_check(int* status, long long limit, cudaStream_t s);

@@ -43,7 +43,7 @@ enum fa4d_causal { FA4D_CAUSAL_NONE = 0, FA4D_CAUSAL_TOP_LEFT = 1, FA4D_CAUSAL_B
 enum fa4d_status {
   FA4D_OK = 0,
   FA4D_ERR_INVALID = -1,     /* bad pointer, shape, stride or enum value */
-  FA4D_ERR_UNSUPPORTED = -2, /* valid but not built: head dim not in {64, 96, 128, 256}; deterministic backward at 256 */
+  FA4D_ERR_UNSUPPORTED = -2, /* valid but not built: head dim not in {64, 96, 128, 256} */
   FA4D_ERR_CUDA = -3,        /* a CUDA runtime call or kernel launch failed */
   FA4D_ERR_DRIVER = -4,      /* cuTensorMapEncodeTiled unavailable or failed */
   FA4D_ERR_LAYOUT = -5,      /* strides/base not 16-byte aligned for TMA: pass a contiguous copy */
@@ -118,8 +118,7 @@ typedef struct fa4d_bwd_args {
   int32_t deterministic;   /* 1: bit-reproducible backward — dQ is computed by a
                             * separate pass (one CTA per query tile walking the key
                             * tiles in order, accumulating in tensor memory) instead
-                            * of fp32 additions in arrival order; 0: default.
-                            * Not built at D = 256 (FA4D_ERR_UNSUPPORTED) */
+                            * of fp32 additions in arrival order; 0: default */
   void* workspace;         /* device scratch, >= fa4d_bwd_workspace_size() bytes, 256-B aligned */
   size_t workspace_bytes;
   const uint8_t* mask_blocks;      /* optional, as in fa4d_fwd_args */

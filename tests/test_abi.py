@@ -146,11 +146,9 @@ def test_bwd_rejects_bad_flag_and_small_workspace():
     a.deterministic = 0
     a.workspace, a.workspace_bytes = 0x1000, 16
     assert lib.fa4d_bwd(ctypes.byref(a), None) == _lib.FA4D_ERR_WORKSPACE
-    # Head dim 256: the backward passes the head-dim check (and fails on the workspace
-    # here); its deterministic mode is refused by every backward entry before device work.
+    # Head dim 256 is built for both backward modes: the call gets past the head-dim
+    # checks and fails on the workspace.
     a.D = 256
-    assert lib.fa4d_bwd(ctypes.byref(a), None) == _lib.FA4D_ERR_WORKSPACE
-    a.deterministic = 1
-    for entry in ("fa4d_bwd", "fa4d_bwd_noalloc", "fa4d_bwd_main"):
-        assert getattr(lib, entry)(ctypes.byref(a), None) == _lib.FA4D_ERR_UNSUPPORTED, entry
-        assert b"256" in lib.fa4d_last_error()
+    for det in (0, 1):
+        a.deterministic = det
+        assert lib.fa4d_bwd(ctypes.byref(a), None) == _lib.FA4D_ERR_WORKSPACE

@@ -8,8 +8,9 @@ causal), plus a direct check that nothing is written past column 96 of each outp
 
 D = 256 runs its own kernels: the forward with one 128-row query slot per CTA, the
 backward with a CTA pair per key tile, each CTA owning half of the dK / dV / dQ
-columns.  The same variants are covered, except the deterministic backward, which is
-not built at this head dim and must be refused.
+columns, and the deterministic dQ pass walking each key tile in two 64-key halves.
+The same variants are covered; the deterministic backward is also checked to repeat
+bit for bit.
 """
 
 from __future__ import annotations
@@ -203,7 +204,27 @@ def test_d256_backward_fp16():
     check(run_api(q, k, v, do, is_causal=True), oracle(q, k, v, do, causal=True, device="cpu"), "D256 bwd fp16")
 
 
-def test_d256_deterministic_backward_is_refused():
-    q, k, v, do = I.qkv(1, 128, 128, 2, 1, D256, seed=119)
-    with pytest.raises(ValueError, match="head dim 256"):
-        run_api(q, k, v, do, use_atomic_backward=False)
+@pytest.mark.parametrize("case", ["dense_causal", "mask_score", "bshd_bottom_right"])
+def test_d256_deterministic_backward(case):
+    """use_atomic_backward=False at D = 256: the dQ pass over 64-key halves (key
+    bound, causal limit, mask words split per half, score), against the oracle and
+    bit for bit against a second run."""
+    if case == "dense_causal":
+        q, k, v, do = I.qkv(2, 333, 333, 4, 2, D256, seed=119)
+        kw, ref_kw = dict(is_causal=True), dict(causal=True)
+    elif case == "mask_score":
+        B, T, H = 1, 400, 2
+        q, k, v, do = I.qkv(B, T, T, H, H, D256, seed=120)
+        mask = I.random_mask(B, H, T, T, 0.85, seed=121)
+        score = I.alibi_score(B, H, T, T, seed=122)
+        kw, ref_kw = dict(mask=mask.to(DEV), score=score.to(DEV)), dict(mask=mask, score=score)
+    else:
+        Tq, Tk = 200, 320
+        q, k, v, do = I.qkv(2, Tq, Tk, 8, 1, D256, seed=123)
+        kw = dict(layout="bshd", is_causal=True, causal_align="bottom_right")
+        ref_kw = dict(causal=True, offset=Tk - Tq)
+    a = run_api(q, k, v, do, use_atomic_backward=False, **kw)
+    b = run_api(q, k, v, do, use_atomic_backward=False, **kw)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+    check(a, oracle(q, k, v, do, device="cpu", **ref_kw), f"D256 deterministic {case}")
