@@ -446,6 +446,12 @@ def extra_measurements(_lib, dev, peaks):
     out["cfg5_mqa_shard_b2"] = {"fwd_ms": round(tf, 4), "fwd_bwd_ms": round(tf + tb, 4),
                                 "fwd_bwd_tflops_convention": round(fbf / (tf + tb) / 1e9, 1),
                                 "fwd_bwd_ms_use_atomic_backward_false": round(tf + tbd, 4)}
+    # Head dim 256 at config 2's shape (its own kernels: one-slot forward, column-split
+    # backward and the ordered dQ pass)
+    tf, tb = fb(B, T, T, HQ, HK, 256, _lib.CAUSAL_NONE, iters=3)
+    ff, fbf = fwd_flops(B, HQ, T, T, 256, False), fwd_bwd_flops(B, HQ, T, T, 256, False)
+    out["cfg2_shape_d256"] = {"fwd_ms": round(tf, 4), "fwd_tflops": round(ff / tf / 1e9, 1),
+                              "fwd_bwd_ms": round(tf + tb, 4), "fwd_bwd_tflops": round(fbf / (tf + tb) / 1e9, 1)}
     return out
 
 
