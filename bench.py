@@ -659,12 +659,16 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=10)
+    # End-to-end steps (default: --steps).  The first step's upload and the last step's
+    # download have no neighbour to overlap, so too few steps overstate their cost.
+    ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-extra", dest="extra", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.e2e_steps is None:
+        args.e2e_steps = args.steps
     if args.impl == "reference":
         line = run_reference(args)
     else:
