@@ -223,6 +223,15 @@ size_t part_bytes(int S, int B, int Tk, int Hk, int D) {
 
 int sm_count();
 
+// Bytes of the fp32 dQ accumulator [B, Hq, lse_ld, Dc] at the head of the backward
+// workspace, rounded to 256; none at D = 256, where dQ always comes from the ordered
+// pass (plan_bwd), which writes dQ directly.
+size_t dq_acc_bytes(int B, int Tq, int Hq, int D) {
+  if (D == 256) return 0;
+  const size_t dq = static_cast<size_t>(B) * Hq * lse_ld_of(Tq) * compute_dim(D) * sizeof(float);
+  return (dq + 255) / 256 * 256;
+}
+
 // Group split of the backward: the query-head group of each (key tile, KV head, batch)
 // is split over S CTAs (a power of two dividing the group size, at most 8) when that
 // shortens the estimated run.  A CTA takes G / S heads x its key tile's query tiles
@@ -310,8 +319,7 @@ extern "C" {
 int64_t fa4d_lse_row_stride(int32_t Tq) { return lse_ld_of(Tq); }
 
 size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D) {
-  const size_t dq = static_cast<size_t>(B) * Hq * lse_ld_of(Tq) * compute_dim(D) * sizeof(float);
-  const size_t dq_al = (dq + 255) / 256 * 256;
+  const size_t dq_al = dq_acc_bytes(B, Tq, Hq, D);
   const size_t delta = static_cast<size_t>(B) * Hq * lse_ld_of(Tq) * sizeof(float);
   return dq_al + (delta + 255) / 256 * 256;
 }
@@ -579,10 +587,9 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   if ((rc = bind_device_of(a->q, "q"))) return rc;
   const bool bf16 = a->dtype == FA4D_BF16;
   const int64_t lse_ld = lse_ld_of(a->Tq);
-  float* dq_acc = static_cast<float*>(a->workspace);
+  float* dq_acc = a->D == 256 ? nullptr : static_cast<float*>(a->workspace);  // see dq_acc_bytes
   const int Dc = compute_dim(a->D);
-  const size_t dq_bytes = static_cast<size_t>(a->B) * a->Hq * lse_ld * Dc * sizeof(float);
-  float* delta = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + (dq_bytes + 255) / 256 * 256);
+  float* delta = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + dq_acc_bytes(a->B, a->Tq, a->Hq, a->D));
   int* status = status_word_ptr();
   if (!status) return fail(FA4D_ERR_CUDA, "cannot locate the device status word");
 

@@ -89,14 +89,14 @@ __device__ __forceinline__ void issue_dv(uint32_t tD, uint32_t tP, uint32_t sDO,
     mma_ts(tD, tP + kk * 8, sw128_desc(sDO + kk * 2048, 8192, 1024), idesc, (acc || kk > 0) ? 1u : 0u);
 }
 
-// dK += dS^T Q : M=128 keys, N=D, K=64 queries; dS^T K-major in smem, Q MN-major.
+// dK += dS^T Q : M=128 keys, N=D, K=64 queries; dS^T from TMEM (16-bit pairs written
+// over the tile's dP^T columns), Q MN-major.
 template <int D, bool kBF16>
-__device__ __forceinline__ void issue_dk(uint32_t tD, uint32_t sDS, uint32_t sQ, bool acc) {
+__device__ __forceinline__ void issue_dk(uint32_t tD, uint32_t tDS, uint32_t sQ, bool acc) {
   constexpr uint32_t idesc = make_idesc(128, D, kBF16, false, true);
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk)
-    mma_ss(tD, sw128_desc(sDS + kk * 32, 16, 1024), sw128_desc(sQ + kk * 2048, 8192, 1024), idesc,
-           (acc || kk > 0) ? 1u : 0u);
+    mma_ts(tD, tDS + kk * 8, sw128_desc(sQ + kk * 2048, 8192, 1024), idesc, (acc || kk > 0) ? 1u : 0u);
 }
 
 // dQ^T = K^T dS^T : M=D, N=64 queries, K=128 keys; K MN-major, dS^T MN-major.
@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         if (!ok) break;
         tc_fence_after();
         if (elect_one()) {
-          issue_dk<D, kBF16>(tmem + kColDK, sDS + st * L::kDS, sQ + qs * L::kQT, it > 0);
+          issue_dk<D, kBF16>(tmem + kColDK, tmem + kColX + 64 * st, sQ + qs * L::kQT, it > 0);
           tc_commit(&q_empty[qs]);
           if (!p.skip_dq) {
             // dQ^T overwrites this tile's dP^T (read before ds_full).
@@ -483,12 +483,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
           dsk[2 * i + 1] = pack2<kBF16>(pv[c + 2] * (__uint_as_float(sr[4 * i + 2]) - t.z),
                                         pv[c + 3] * (__uint_as_float(sr[4 * i + 3]) - t.w));
         }
-        // Row r of the dS^T tile: 128 B in 8 chunks of 16 B, 128-B swizzled (chunk ^ (row % 8)).
+        // Row r of the dS^T tile: 128 B in 8 chunks of 16 B, 128-B swizzled (chunk ^ (row % 8)),
+        // the B operand of dQ^T; the same 16-bit pairs go to TMEM columns 16*half ..
+        // 16*half+15 of X (dP^T values this thread has read), the A operand of dK.
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc)
           *reinterpret_cast<uint4*>(ds_row + (((4 * half + cc) ^ (r & 7)) << 4)) =
               make_uint4(dsk[4 * cc], dsk[4 * cc + 1], dsk[4 * cc + 2], dsk[4 * cc + 3]);
+        tmem_st16(tmem + lane_base + kColX + 64 * st + 16 * half, dsk);
       }
+      tmem_wait_st();
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&ds_full[st]);

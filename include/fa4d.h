@@ -133,7 +133,8 @@ int64_t fa4d_lse_row_stride(int32_t Tq);
 /* Bytes of device scratch fa4d_bwd needs: an fp32 dQ accumulator
  * [B, Hq, fa4d_lse_row_stride(Tq), Dc] and the fp32 row dot products
  * Delta [B, Hq, fa4d_lse_row_stride(Tq)], where Dc is the width the kernels compute
- * at (D, except 128 for D = 96). */
+ * at (D, except 128 for D = 96).  At D = 256 there is no accumulator (dQ always comes
+ * from the ordered pass, which writes it directly). */
 size_t fa4d_bwd_workspace_size(int32_t B, int32_t Tq, int32_t Hq, int32_t D);
 
 /* Workspace bytes including the backward's group-split buffers.  fa4d_bwd may split

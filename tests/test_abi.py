@@ -79,6 +79,8 @@ def test_host_size_helpers():
     assert lib.fa4d_bwd_workspace_size(1, 1, 1, 64) % 256 == 0
     # Head dim 96 computes at width 128: its dQ accumulator rows hold 128 floats.
     assert lib.fa4d_bwd_workspace_size(1, 8192, 32, 96) == lib.fa4d_bwd_workspace_size(1, 8192, 32, 128)
+    # Head dim 256 has no dQ accumulator (the ordered dQ pass writes dQ): Delta only.
+    assert lib.fa4d_bwd_workspace_size(1, 8192, 32, 256) == delta
 
 
 def test_group_split_choices():
