@@ -38,10 +38,20 @@ namespace fa4d {
 namespace {
 
 constexpr int kFwdThreads = 384;
-// Register split (launch: 384 threads x 168 = 64512): producer/MMA warpgroup 112,
-// the two softmax warpgroups 192 -> 128*112 + 256*192 = 63488.
-constexpr uint32_t kFwdRegsLaunch = 168, kFwdRegsCtl = 112, kFwdRegsSoftmax = 192;
-static_assert(128 * kFwdRegsCtl + 256 * kFwdRegsSoftmax <= kFwdThreads * kFwdRegsLaunch,
+// Register split (launch: 384 threads x 168 = 64512): producer/MMA warpgroup 112, the
+// two softmax warpgroups 192 -> 128*112 + 256*192 = 63488.  The mask-only variants at
+// D = 64 / 128 take 96 / 200 (128*96 + 256*200 = 63488): at 192 their softmax code
+// spilled 96-108 bytes per thread, at 200 8-16, and the packed-document forward (config
+// 3) ran 2.9% faster; the dense and score variants ran 1-4% slower at 96 / 200, and at
+// D = 256 the control warps spilled at 96.
+template <int D, bool kMask, bool kScore>
+constexpr bool kFwdWideSoftmax = D != 256 && kMask && !kScore;
+template <int D, bool kMask, bool kScore>
+constexpr uint32_t kFwdRegsCtl = kFwdWideSoftmax<D, kMask, kScore> ? 96 : 112;
+template <int D, bool kMask, bool kScore>
+constexpr uint32_t kFwdRegsSoftmax = kFwdWideSoftmax<D, kMask, kScore> ? 200 : 192;
+constexpr uint32_t kFwdRegsLaunch = 168;
+static_assert(128 * 112 + 256 * 192 <= kFwdThreads * kFwdRegsLaunch && 128 * 96 + 256 * 200 <= kFwdThreads * kFwdRegsLaunch,
               "register split exceeds the launch allocation");
 constexpr float kNegInf = -INFINITY;
 // O is only rescaled when the running max grows by more than this (log2 units);
@@ -188,7 +198,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
   if (warp < 4) {
     // Each role starts with its register budget so the compiler allocates that
     // role's code under it.
-    regs_dec<kFwdRegsCtl>();
+    regs_dec<kFwdRegsCtl<D, kMask, kScore>>();
     if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && any_work) {
@@ -348,9 +358,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     __syncwarp();
     }
   } else if ((warp - 4) >> 2 >= L::kSlots) {
-    regs_inc<kFwdRegsSoftmax>();  // a slot this CTA does not have (D=256): nothing to do
+    regs_inc<kFwdRegsSoftmax<D, kMask, kScore>>();  // a slot this CTA does not have (D=256): nothing to do
   } else {
-    regs_inc<kFwdRegsSoftmax>();
+    regs_inc<kFwdRegsSoftmax<D, kMask, kScore>>();
     // ------------------------------------------------------------ softmax + epilogue
     const int t = (warp - 4) >> 2;
     const int row = (warp & 3) * 32 + lane;
