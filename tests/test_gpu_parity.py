@@ -108,6 +108,36 @@ def test_config2_full_size_one_kv_group(causal):
     assert torch.isfinite(out).all() and torch.isfinite(dq).all() and torch.isfinite(dk).all()
 
 
+@pytest.mark.parametrize("case", ["no_causal", "causal", "random_mask"])
+def test_reference_precision_check_cases(case):
+    """The reference's own correctness run (benchmark/precision_check.sh): B=1, T=8191
+    (not a tile multiple), Hq=32, Hk=8, D=128, bf16, forward and backward, cases
+    no_causal / causal / random_mask.  The random mask is Bernoulli(0.75) with the
+    (q, min(q, Tk-1)) entry kept (precision_check.py:110-117) and comes with an fp32
+    score of N(0, 0.1^2) (precision_check.py:128-129); both are drawn on the device, per
+    head.  Checked on KV group 3 (query heads 12..15) against the fp32 oracle."""
+    T = 8191
+    q, k, v, do = I.qkv(1, T, T, 32, 8, 128, seed=21)
+    kw, ref_kw = {}, {}
+    if case == "causal":
+        kw, ref_kw = dict(is_causal=True), dict(causal=True)
+    elif case == "random_mask":
+        g = torch.Generator(device=DEV)
+        g.manual_seed(22)
+        mask = torch.rand((1, 32, T, T), generator=g, device=DEV) < 0.75
+        qi = torch.arange(T, device=DEV)
+        mask[:, :, qi, qi] = True
+        score = 0.1 * torch.randn((1, 32, T, T), generator=g, device=DEV)
+        kw = dict(mask=mask, score=score)
+        ref_kw = dict(mask=mask[:, 12:16], score=score[:, 12:16])
+    out, dq, dk, dv = run_api(q, k, v, do, **kw)
+    del kw
+    hs = slice(12, 16)
+    ref = oracle(q[:, hs], k[:, 3:4], v[:, 3:4], do[:, hs], **ref_kw)
+    check((out[:, hs], dq[:, hs], dk[:, 3:4], dv[:, 3:4]), ref, f"precision_check {case}")
+    assert torch.isfinite(out).all() and torch.isfinite(dq).all() and torch.isfinite(dk).all()
+
+
 def test_config3_packed_documents():
     B, T = 1, 2048
     q, k, v, do = I.qkv(B, T, T, 8, 2, 128, seed=14)
