@@ -482,7 +482,52 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         }
         const float2 rs = f2_split(rs2);
         rowsum = rs.x + rs.y;
+      } else if constexpr (!kScore) {
+        // Masked or edge tile without a score: one pass over the whole row in registers.
+        // x = s * scale (log2 units), -inf where the keep bit is clear; every exponential
+        // on MUFU (ex2_poly clamps its argument and would leave cut keys a tiny weight).
+        if (kMask && use_mask && !bits_row) {
+          // No prepared bits: read this row's 128 mask bytes from global memory.
+          const uint4 v = mask_words_from_bytes(mask_row, kbase, p.Tk, p.mask_vec);
+          mw[0] = v.x;
+          mw[1] = v.y;
+          mw[2] = v.z;
+          mw[3] = v.w;
+        }
+        if (need_bounds || need_causal) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) mw[c] &= low_bits(key_lim - (kbase + 32 * c));
+        }
+        uint32_t xr[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&xr[32 * c]));
+        tmem_wait_ld();
+        float m4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
+#pragma unroll
+        for (int k = 0; k < 128; ++k) {
+          const float x = ((mw[k >> 5] >> (k & 31)) & 1u) ? __uint_as_float(xr[k]) * p.scale_log2 : kNegInf;
+          xr[k] = __float_as_uint(x);
+          m4[k & 3] = fmaxf(m4[k & 3], x);
+        }
+        const float m_use = online_update(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+        const uint64_t nm2 = f2(m_use, m_use);
+        uint64_t rs2 = f2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float2 a = f2_split(fsub2(f2(__uint_as_float(xr[32 * c + 2 * k]), __uint_as_float(xr[32 * c + 2 * k + 1])), nm2));
+            const float p0 = ex2(a.x), p1 = ex2(a.y);
+            rs2 = fadd2(rs2, f2(p0, p1));
+            pk[k] = pack2<kBF16>(p0, p1);
+          }
+          tmem_st16(tS + 16 * c, pk);
+        }
+        const float2 rs = f2_split(rs2);
+        rowsum = rs.x + rs.y;
       } else {
+        // Tile with a score (the variants with a score only reach this branch).
         if (kMask && use_mask && !bits_row) {
           // No prepared bits: read this row's 128 mask bytes from global memory.
           const uint4 v = mask_words_from_bytes(mask_row, kbase, p.Tk, p.mask_vec);
@@ -511,18 +556,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
 #pragma unroll
             for (int j = 0; j < 4; j += 2) {
               const int e = e0 + j;
-              float x0, x1;
-              if constexpr (kScore) {
-                // (s + score) * scale on a packed fp32 pair (same rounding as scalar).
-                const float2 x = f2_split(fmul2(fadd2(f2(__uint_as_float(xr[e]), __uint_as_float(xr[e + 1])),
-                                                      f2(av[j], av[j + 1])),
-                                                f2(p.scale_log2, p.scale_log2)));
-                x0 = x.x;
-                x1 = x.y;
-              } else {
-                x0 = __uint_as_float(xr[e]) * p.scale_log2;
-                x1 = __uint_as_float(xr[e + 1]) * p.scale_log2;
-              }
+              // (s + score) * scale on a packed fp32 pair (same rounding as scalar).
+              const float2 x = f2_split(fmul2(fadd2(f2(__uint_as_float(xr[e]), __uint_as_float(xr[e + 1])),
+                                                    f2(av[j], av[j + 1])),
+                                              f2(p.scale_log2, p.scale_log2)));
+              float x0 = x.x, x1 = x.y;
               x0 = ((w >> (e & 31)) & 1u) ? x0 : kNegInf;
               x1 = ((w >> ((e + 1) & 31)) & 1u) ? x1 : kNegInf;
               xr[e] = __float_as_uint(x0);
@@ -536,37 +574,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             const int c = 2 * hh + cc;
             const int kc = kbase + 32 * c;
             const uint32_t w = mw[c];
-            if constexpr (kScore) {
-              if (p.bias_tma) {
-                const int e = g % R;
-                ok = __all_sync(0xffffffffu, mbar_wait(&full[e], (g / R) & 1, abort_flag));
-                if (!ok) break;
+            if (p.bias_tma) {
+              const int e = g % R;
+              ok = __all_sync(0xffffffffu, mbar_wait(&full[e], (g / R) & 1, abort_flag));
+              if (!ok) break;
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                  const float4 v = lds_f4(ring_row + e * kRingEntry + ((u ^ sw) << 4));
-                  apply4(32 * cc + 4 * u, v.x, v.y, v.z, v.w, w);
-                }
-                mbar_arrive(&empty[e]);
-                ++g;
-              } else if (p.score_vec && kc + 31 < p.Tk) {
+              for (int u = 0; u < 8; ++u) {
+                const float4 v = lds_f4(ring_row + e * kRingEntry + ((u ^ sw) << 4));
+                apply4(32 * cc + 4 * u, v.x, v.y, v.z, v.w, w);
+              }
+              mbar_arrive(&empty[e]);
+              ++g;
+            } else if (p.score_vec && kc + 31 < p.Tk) {
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                  const float4 v = __ldg(reinterpret_cast<const float4*>(score_row + kc) + u);
-                  apply4(32 * cc + 4 * u, v.x, v.y, v.z, v.w, w);
-                }
-              } else {
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                  const int k4 = kc + 4 * u;
-                  apply4(32 * cc + 4 * u, (k4 < p.Tk) ? __ldg(score_row + k4) : 0.f,
-                         (k4 + 1 < p.Tk) ? __ldg(score_row + k4 + 1) : 0.f,
-                         (k4 + 2 < p.Tk) ? __ldg(score_row + k4 + 2) : 0.f,
-                         (k4 + 3 < p.Tk) ? __ldg(score_row + k4 + 3) : 0.f, w);
-                }
+              for (int u = 0; u < 8; ++u) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(score_row + kc) + u);
+                apply4(32 * cc + 4 * u, v.x, v.y, v.z, v.w, w);
               }
             } else {
 #pragma unroll
-              for (int u = 0; u < 8; ++u) apply4(32 * cc + 4 * u, 0.f, 0.f, 0.f, 0.f, w);
+              for (int u = 0; u < 8; ++u) {
+                const int k4 = kc + 4 * u;
+                apply4(32 * cc + 4 * u, (k4 < p.Tk) ? __ldg(score_row + k4) : 0.f,
+                       (k4 + 1 < p.Tk) ? __ldg(score_row + k4 + 1) : 0.f,
+                       (k4 + 2 < p.Tk) ? __ldg(score_row + k4 + 2) : 0.f,
+                       (k4 + 3 < p.Tk) ? __ldg(score_row + k4 + 3) : 0.f, w);
+              }
             }
           }
           if (!ok) break;
@@ -591,29 +624,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             uint32_t pk[16];
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
-              float p0, p1;
-              if constexpr (kScore) {
-                // Packed pairs with a score (no spills there); scalar otherwise, which
-                // compiles the dense kernel's rare edge tiles as before.
-                const float2 a = f2_split(
-                    fsub2(f2(__uint_as_float(xr[32 * c + 2 * k]), __uint_as_float(xr[32 * c + 2 * k + 1])), nm2));
-                p0 = ex2(a.x);
-                p1 = ex2(a.y);
-                rs2 = fadd2(rs2, f2(p0, p1));
-              } else {
-                p0 = ex2(__uint_as_float(xr[32 * c + 2 * k]) - m_use);
-                p1 = ex2(__uint_as_float(xr[32 * c + 2 * k + 1]) - m_use);
-                rowsum += p0 + p1;
-              }
+              const float2 a = f2_split(
+                  fsub2(f2(__uint_as_float(xr[32 * c + 2 * k]), __uint_as_float(xr[32 * c + 2 * k + 1])), nm2));
+              const float p0 = ex2(a.x), p1 = ex2(a.y);
+              rs2 = fadd2(rs2, f2(p0, p1));
               pk[k] = pack2<kBF16>(p0, p1);
             }
             tmem_st16(tS + 32 * hh + 16 * c, pk);
           }
         }
-        if constexpr (kScore) {
-          const float2 rs = f2_split(rs2);
-          rowsum = rs.x + rs.y;
-        }
+        const float2 rs = f2_split(rs2);
+        rowsum = rs.x + rs.y;
       }
       l_run += rowsum;
       tmem_wait_st();
