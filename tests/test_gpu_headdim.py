@@ -228,3 +228,14 @@ def test_d256_deterministic_backward(case):
     for x, y in zip(a, b):
         assert torch.equal(x, y)
     check(a, oracle(q, k, v, do, device="cpu", **ref_kw), f"D256 deterministic {case}")
+
+
+@pytest.mark.parametrize("Tq,Tk,causal", [(1, 1, False), (17, 17, True), (1, 257, False), (130, 65, True)])
+def test_d256_backward_tiny_and_rectangular(Tq, Tk, causal):
+    """Sequences shorter than one 64-key half, a single query row, and Tq > Tk (rows
+    that see only part of a tile), in both backward modes."""
+    q, k, v, do = I.qkv(1, Tq, Tk, 2, 1, D256, seed=130 + Tq)
+    ref = oracle(q, k, v, do, causal=causal, device="cpu")
+    for atomic in (True, False):
+        got = run_api(q, k, v, do, is_causal=causal, use_atomic_backward=atomic)
+        check(got, ref, f"D256 Tq={Tq} Tk={Tk} c={causal} atomic={atomic}")
