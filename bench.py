@@ -44,9 +44,9 @@ B, T, HQ, HK, D = 1, 8192, 32, 8, 128
 WORKLOAD = "cfg2: B1 Tq=Tk=8192 Hq32 Hk8 D128 bf16 non-causal, fwd+bwd per GPU"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per launch of the backward main kernel at this workload:
-# dram__bytes_read.sum 321,568,256 + dram__bytes_write.sum 229,699,584 from one ncu
+# dram__bytes_read.sum 314,331,392 + dram__bytes_write.sum 222,560,256 from one ncu
 # capture of this bench command (profiles/launches_cfg2_fwd_bwd.md).
-NCU_BWD_MAIN_TRAFFIC = 551267840
+NCU_BWD_MAIN_TRAFFIC = 536891648
 L2_FLUSH_BYTES = 256 << 20
 
 
