@@ -99,6 +99,15 @@ def test_group_split_choices():
     # The workspace covers the largest split of any causal mode.
     base = lib.fa4d_bwd_workspace_size(1, 8192, 32, 128)
     assert lib.fa4d_bwd_workspace_size_ex(1, 8192, 8192, 32, 8, 128) > base
+    # Head dim 256 runs a CTA pair per key tile: config 2's shape already makes 1024 CTAs
+    # (6.92 waves), a small MQA grid (12 CTAs) splits 8 ways.  Its workspace is Delta plus
+    # the two fp32 dK / dV slice sets, with no dQ accumulator.
+    assert lib.fa4d_bwd_group_split(1, 8192, 8192, 32, 8, 256, _lib.CAUSAL_NONE) == 1
+    assert lib.fa4d_bwd_group_split(2, 200, 384, 16, 1, 256, _lib.CAUSAL_BOTTOM_RIGHT) == 8
+    delta = 2 * 16 * 256 * 4
+    slices = 8 * 2 * 384 * 1 * 256 * 4
+    assert lib.fa4d_bwd_workspace_size(2, 200, 16, 256) == delta
+    assert lib.fa4d_bwd_workspace_size_ex(2, 200, 384, 16, 1, 256) == delta + 2 * slices
 
 
 def _fwd_args(**kw):
