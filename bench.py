@@ -43,11 +43,17 @@ UNIT = "TFLOP/s"
 B, T, HQ, HK, D = 1, 8192, 32, 8, 128
 WORKLOAD = "cfg2: B1 Tq=Tk=8192 Hq32 Hk8 D128 bf16 non-causal, fwd+bwd per GPU"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes (read + write) per launch of the backward main kernel at this workload:
-# dram__bytes_read.sum 314,331,392 + dram__bytes_write.sum 222,560,256 from one ncu
-# capture of this bench command (profiles/launches_cfg2_fwd_bwd.md).
+# DRAM bytes (read + write) per launch of the backward main kernel at this workload,
+# dram__bytes_read.sum + dram__bytes_write.sum from one ncu capture of this bench
+# command, and the commit of the kernel code that capture measured.
 NCU_BWD_MAIN_TRAFFIC = 536891648
+NCU_BWD_MAIN_TRAFFIC_CODE = "1114cec"
 L2_FLUSH_BYTES = 256 << 20
+
+
+def median_ms(pairs):
+    """Median elapsed time (ms) of a list of (start, end) CUDA events."""
+    return statistics.median(a.elapsed_time(b) for a, b in pairs)
 
 
 def fwd_flops(b, hq, tq, tk, d, causal):
@@ -173,72 +179,89 @@ def _run_ours(args, _lib):
     stream = torch.cuda.current_stream(dev)
 
     ev = lambda: torch.cuda.Event(enable_timing=True)
-    rec = {"fwd": [], "preprocess": [], "main": [], "dq_convert": [], "step": []}
 
-    def step(timed, events=True):
-        if not events:  # the step as captured into the CUDA graph
-            o, lse = _lib.forward(q, k, v, None, None, scale, _lib.CAUSAL_NONE)
-            _lib.backward(do, q, k, v, o, lse, None, None, scale, _lib.CAUSAL_NONE)
+    def measure(mode):
+        """One causal mode of the workload: per-stage medians of eager launches with
+        events around each stage, then the medians of `steps` graph replays of the
+        whole step (fwd + the backward's launches) and of the forward alone, with L2
+        flushed before each replay (outside its events)."""
+        rec = {"fwd": [], "preprocess": [], "main": [], "dq_convert": [], "step": []}
+
+        def step(timed, events=True):
+            if not events:  # the step as captured into the CUDA graph
+                o, lse = _lib.forward(q, k, v, None, None, scale, mode)
+                _lib.backward(do, q, k, v, o, lse, None, None, scale, mode)
+                return o
+            e0, e1 = ev(), ev()
+            e0.record(stream)
+            o, lse = _lib.forward(q, k, v, None, None, scale, mode)
+            e1.record(stream)
+            marks = []
+
+            def stage(name, launch):
+                a, b = ev(), ev()
+                a.record(stream)
+                launch()
+                b.record(stream)
+                marks.append((name, a, b))
+
+            _lib.backward(do, q, k, v, o, lse, None, None, scale, mode, stages=stage)
+            if timed:
+                rec["fwd"].append((e0, e1))
+                for name, a, b in marks:
+                    rec[name].append((a, b))
+                rec["step"].append((e0, marks[-1][2]))
             return o
-        e0, e1 = ev(), ev()
-        e0.record(stream)
-        o, lse = _lib.forward(q, k, v, None, None, scale, _lib.CAUSAL_NONE)
-        e1.record(stream)
-        marks = []
 
-        def stage(name, launch):
-            a, b = ev(), ev()
-            a.record(stream)
-            launch()
-            b.record(stream)
-            marks.append((name, a, b))
-
-        _lib.backward(do, q, k, v, o, lse, None, None, scale, _lib.CAUSAL_NONE, stages=stage)
-        if timed:
-            rec["fwd"].append((e0, e1))
-            for name, a, b in marks:
-                rec[name].append((a, b))
-            rec["step"].append((e0, marks[-1][2]))
-        return o
+        for _ in range(args.warmup):
+            step(False)
+        torch.cuda.synchronize(dev)
+        for _ in range(min(args.steps, 10)):
+            flush.zero_()
+            step(True)
+        torch.cuda.synchronize(dev)
+        # Graph replays, so host-side launch work cannot leave gaps between the kernels.
+        graph, fgraph = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            o = step(False, events=False)
+        with torch.cuda.graph(fgraph):
+            _lib.forward(q, k, v, None, None, scale, mode)
+        for _ in range(args.warmup):
+            graph.replay()
+            fgraph.replay()
+        torch.cuda.synchronize(dev)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        steps_ev, fwd_ev = [], []
+        for g_, out_ in ((graph, steps_ev), (fgraph, fwd_ev)):
+            for _ in range(args.steps):
+                flush.zero_()  # L2 flush between steps, outside the step's events
+                a, b = ev(), ev()
+                a.record(stream)
+                g_.replay()
+                b.record(stream)
+                out_.append((a, b))
+        torch.cuda.synchronize(dev)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ms = {k2: median_ms(v2) for k2, v2 in rec.items()}
+        ms["step_eager"] = ms.pop("step")
+        ms["step"] = median_ms(steps_ev)
+        ms["fwd_graph"] = median_ms(fwd_ev)
+        del graph, fgraph
+        return ms, o
 
     sampler = ClockSampler(dev) if rank == 0 else None  # started early: nvidia-smi needs ~0.5 s to begin
-    for _ in range(args.warmup):
-        step(False)
-    torch.cuda.synchronize(dev)
-    # Per-kernel times: eager launches with events around each stage.
-    for _ in range(min(args.steps, 10)):
-        flush.zero_()
-        step(True)
-    torch.cuda.synchronize(dev)
-    # The timed steps replay the step (fwd + the 3 backward launches) as one CUDA
-    # graph, so host-side launch work cannot leave gaps between the kernels.
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        o = step(False, events=False)
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize(dev)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    steps_ev = []
-    for _ in range(args.steps):
-        flush.zero_()  # L2 flush between steps, outside the step's events
-        a, b = ev(), ev()
-        a.record(stream)
-        graph.replay()
-        b.record(stream)
-        steps_ev.append((a, b))
-    torch.cuda.synchronize(dev)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
+    ms, o = measure(_lib.CAUSAL_NONE)
+    ms_causal, _ = measure(_lib.CAUSAL_TOP_LEFT)
     clocks = sampler.stop() if sampler else None
 
-    ms = {k2: sum(a.elapsed_time(b) for a, b in v2) / max(1, len(v2)) for k2, v2 in rec.items()}
-    ms["step_eager"] = ms.pop("step")
-    ms["step"] = sum(a.elapsed_time(b) for a, b in steps_ev) / len(steps_ev)
     t_step = shard.max_over_ranks(ms["step"], dist, dev)
+    t_fwd = shard.max_over_ranks(ms["fwd_graph"], dist, dev)
+    t_step_causal = shard.max_over_ranks(ms_causal["step"], dist, dev)
+    t_fwd_causal = shard.max_over_ranks(ms_causal["fwd_graph"], dist, dev)
     if dist:
         # Verification only (outside the timed region): per-rank output checksums.
         chk = o.float().abs().sum().reshape(1)
@@ -260,8 +283,11 @@ def _run_ours(args, _lib):
 
     bwd_main_flops = fwd_bwd_flops(B, HQ, T, T, D, False) - fwd_flops(B, HQ, T, T, D, False)
     main_tflops = bwd_main_flops / (ms["main"] * 1e-3) / 1e12
-    fwd_tflops = fwd_flops(B, HQ, T, T, D, False) / (ms["fwd"] * 1e-3) / 1e12
+    fwd_tflops = fwd_flops(B, HQ, T, T, D, False) / (t_fwd * 1e-3) / 1e12
     peak = peaks["bf16_tflops"]
+    c_fwd = fwd_flops(B, HQ, T, T, D, True) / (t_fwd_causal * 1e-3) / 1e12
+    c_fb = fwd_bwd_flops(B, HQ, T, T, D, True) / (t_step_causal * 1e-3) / 1e12
+    c_main = (fwd_bwd_flops(B, HQ, T, T, D, True) - fwd_flops(B, HQ, T, T, D, True)) / (ms_causal["main"] * 1e-3) / 1e12
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -290,7 +316,18 @@ def _run_ours(args, _lib):
         "fwd_bwd_frac_of_peak": round(value / world / peak, 4),
         "kernel_ms": {k2: round(v2, 4) for k2, v2 in ms.items() if k2 not in ("step", "step_eager")},
         "step_ms_eager_launches": round(ms["step_eager"], 4),
-        "timing": "CUDA events around each timed step, which replays the step as one captured CUDA graph",
+        # The same workload with top-left causal masking, measured the same way (graph
+        # replays, L2 flushed, median of `steps`; FLOPs x0.5 by the convention).
+        "causal": {
+            "fwd_ms": round(t_fwd_causal, 4), "fwd_tflops": round(c_fwd, 2), "fwd_frac_of_peak": round(c_fwd / peak, 4),
+            "fwd_bwd_ms": round(t_step_causal, 4), "fwd_bwd_tflops": round(world * c_fb, 2),
+            "fwd_bwd_frac_of_peak": round(c_fb / peak, 4),
+            "bwd_main_ms": round(ms_causal["main"], 4), "bwd_main_frac_of_peak": round(c_main / peak, 4),
+            "kernel_ms": {k2: round(v2, 4) for k2, v2 in ms_causal.items() if k2 not in ("step", "step_eager")},
+        },
+        "timing": "median over `steps` of CUDA events around graph replays of the whole step (value) and of "
+                  "the forward alone (fwd_tflops), L2 flushed before each replay; per-kernel times are medians "
+                  "of 10 eager steps with events around each stage",
         "roofline": {
             "kernel": "bwd_kernel<128,bf16> (fa4d_bwd_main)",
             "bound": "tensor",
@@ -302,6 +339,8 @@ def _run_ours(args, _lib):
             else "fallback 1590 TFLOP/s",
             "algorithmic": "10*B*Hq*Tq*Tk*D FLOP per launch (bwd share of the 14x convention)",
             "traffic": NCU_BWD_MAIN_TRAFFIC,
+            "traffic_source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum, one capture of this command "
+                              f"on kernel code {NCU_BWD_MAIN_TRAFFIC_CODE}",
         },
         # fwd, preprocess, main, dQ convert, plus the split-slice sum when the
         # backward's group split is on for this workload.
@@ -323,19 +362,29 @@ def _run_ours(args, _lib):
     return line
 
 
-def time_fn(fn, iters, warm=2):
+_FLUSH = {}
+
+
+def time_fn(fn, iters=10, warm=3):
+    """Median ms of `iters` calls of fn after `warm` untimed ones, CUDA events on the
+    current stream, L2 flushed (a 256 MiB write) before each timed call."""
+    dev = torch.cuda.current_device()
+    if dev not in _FLUSH:
+        _FLUSH[dev] = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = _FLUSH[dev]
     for _ in range(warm):
         fn()
     torch.cuda.synchronize()
     evs = []
     for _ in range(iters):
+        flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         fn()
         b.record()
         evs.append((a, b))
     torch.cuda.synchronize()
-    return statistics.median(a.elapsed_time(b) for a, b in evs)
+    return median_ms(evs)
 
 
 def _dev_inputs(dev, b, tq, tk, hq, hk, d, seed):
@@ -386,7 +435,7 @@ def extra_measurements(_lib, dev, peaks):
     out = {}
     peak = peaks["bf16_tflops"]
 
-    def fb(b, tq, tk, hq, hk, d, causal_mode, mask=None, score=None, iters=5, deterministic=False):
+    def fb(b, tq, tk, hq, hk, d, causal_mode, mask=None, score=None, iters=10, deterministic=False):
         """(fwd ms, bwd ms) with the mask prepared once beforehand (block map + packed bits,
         as the op caches it per mask); the preparation itself is timed by map_ms()."""
         q, k, v, do = (x.transpose(1, 2) for x in _dev_inputs(dev, b, tq, tk, hq, hk, d, seed=3))
@@ -398,60 +447,92 @@ def extra_measurements(_lib, dev, peaks):
                                            deterministic=deterministic), iters)
         return tf, tb
 
-    def map_ms(mask):
-        return round(time_fn(lambda: _lib.mask_prepare(mask), 5), 4)
+    hbm = peaks["hbm_gbs"]
 
-    tf, tb = fb(B, T, T, HQ, HK, D, _lib.CAUSAL_TOP_LEFT)
-    ff, fbf = fwd_flops(B, HQ, T, T, D, True), fwd_bwd_flops(B, HQ, T, T, D, True)
-    out["cfg2_causal"] = {"fwd_ms": round(tf, 4), "fwd_tflops": round(ff / tf / 1e9, 1),
-                          "fwd_bwd_ms": round(tf + tb, 4), "fwd_bwd_tflops": round(fbf / (tf + tb) / 1e9, 1),
-                          "fwd_frac": round(ff / tf / 1e9 / peak, 4),
-                          "fwd_bwd_frac": round(fbf / (tf + tb) / 1e9 / peak, 4)}
-    tf, tb = fb(B, T, T, HQ, HK, D, _lib.CAUSAL_NONE, iters=3, deterministic=True)
+    def map_ms(mask):
+        return round(time_fn(lambda: _lib.mask_prepare(mask)), 4)
+
+    def tensor_bytes(b, tq, tk, hq, hk, d):
+        """(fwd, bwd) bytes of the dense tensors: fwd reads Q, K, V and writes O and LSE;
+        bwd reads Q, K, V, O, dO, LSE and writes dQ, dK, dV (2-byte elements)."""
+        qb, kb, lse = 2 * b * tq * hq * d, 2 * b * tk * hk * d, 4 * b * hq * tq
+        return 2 * qb + 2 * kb + lse, 3 * qb + 2 * kb + lse + qb + 2 * kb
+
+    tf, tb = fb(B, T, T, HQ, HK, D, _lib.CAUSAL_NONE, deterministic=True)
     fbf = fwd_bwd_flops(B, HQ, T, T, D, False)
     out["cfg2_deterministic_bwd"] = {"fwd_bwd_ms": round(tf + tb, 4), "bwd_ms": round(tb, 4),
-                                     "fwd_bwd_tflops": round(fbf / (tf + tb) / 1e9, 1)}
+                                     "fwd_bwd_tflops": round(fbf / (tf + tb) / 1e9, 1),
+                                     "fwd_bwd_frac": round(fbf / (tf + tb) / 1e9 / peak, 4)}
     # cfg4: ALiBi-style fp32 score + Bernoulli(0.9) bool mask, MHA, non-causal (HBM-bound)
     b4, t4, h4 = 1, 4096, 16
     score = _alibi_score(dev, b4, h4, t4, t4)
     mask = _bernoulli_mask(dev, b4, h4, t4, t4, 0.9)
-    tf, tb = fb(b4, t4, t4, h4, h4, D, _lib.CAUSAL_NONE, mask=mask, score=score, iters=3)
-    bytes_fwd = score.numel() * 4 + mask.numel() + 4 * b4 * t4 * h4 * D * 2
-    out["cfg4_score_mask"] = {"fwd_ms": round(tf, 4), "fwd_gbs": round(bytes_fwd / tf / 1e6, 1),
-                              "fwd_frac_hbm": round(bytes_fwd / tf / 1e6 / peaks["hbm_gbs"], 4),
-                              "fwd_bwd_ms": round(tf + tb, 4),
-                              "algorithmic_fwd_bytes": bytes_fwd,
-                              "mask_prepare_ms": map_ms(mask)}
+    tf, tb = fb(b4, t4, t4, h4, h4, D, _lib.CAUSAL_NONE, mask=mask, score=score)
+    prep = map_ms(mask)
+    tfw, tbw = tensor_bytes(b4, t4, t4, h4, h4, D)
+    sm = score.numel() * 4 + mask.numel()
+    bits = 2 * mask.numel() // 8  # the prepared row bits (forward) and column bits (backward)
+    bytes_fwd = sm + tfw
+    bytes_fb = 2 * sm + tfw + tbw
+    moved_fwd = score.numel() * 4 + bits // 2 + tfw  # the forward reads the row bits, not the mask bytes
+    out["cfg4_score_mask"] = {
+        "fwd_ms": round(tf, 4), "fwd_bwd_ms": round(tf + tb, 4), "mask_prepare_ms": prep,
+        "algorithmic_fwd_bytes": bytes_fwd, "algorithmic_fwd_bwd_bytes": bytes_fb,
+        "fwd_gbs": round(bytes_fwd / tf / 1e6, 1),
+        "fwd_frac_hbm": round(bytes_fwd / tf / 1e6 / hbm, 4),
+        "fwd_bwd_frac_hbm": round(bytes_fb / (tf + tb) / 1e6 / hbm, 4),
+        # Bytes the forward kernel actually moves (packed bits instead of mask bytes),
+        # and the algorithmic fraction with one mask preparation charged to the call.
+        "fwd_frac_hbm_bytes_moved": round(moved_fwd / tf / 1e6 / hbm, 4),
+        "fwd_frac_hbm_with_prepare": round(bytes_fwd / (tf + prep) / 1e6 / hbm, 4),
+        "fwd_bwd_frac_hbm_with_prepare": round(bytes_fb / (tf + tb + prep) / 1e6 / hbm, 4),
+        "mask_prepare_frac_hbm": round((mask.numel() + bits) / prep / 1e6 / hbm, 4),
+    }
     del score, mask
     # cfg3: packed-document [B,1,T,T] mask
     b3, t3 = 2, 4096
     mask = _packed_doc_mask(dev, b3, t3)
     mview = mask.expand(b3, HQ, t3, t3)
-    tf, tb = fb(b3, t3, t3, HQ, HK, D, _lib.CAUSAL_NONE, mask=mview, iters=3)
+    tf, tb = fb(b3, t3, t3, HQ, HK, D, _lib.CAUSAL_NONE, mask=mview)
+    prep = map_ms(mview)
     ff, fbf = fwd_flops(b3, HQ, t3, t3, D, False), fwd_bwd_flops(b3, HQ, t3, t3, D, False)
     counts = _lib.mask_blocks(mview).counts()
     live = (counts["partial"] + counts["full"]) / sum(counts.values())
+    tfw, tbw = tensor_bytes(b3, t3, t3, HQ, HK, D)
+    mbytes = mask.numel()  # the unexpanded [B, 1, T, T] mask, each element once
     out["cfg3_packed_docs"] = {"fwd_ms": round(tf, 4), "fwd_bwd_ms": round(tf + tb, 4),
                                "fwd_dense_equiv_tflops": round(ff / tf / 1e9, 1),
                                "fwd_bwd_dense_equiv_tflops": round(fbf / (tf + tb) / 1e9, 1),
                                "blocks": counts,
                                "fwd_live_block_tflops": round(live * ff / tf / 1e9, 1),
                                "fwd_bwd_live_block_tflops": round(live * fbf / (tf + tb) / 1e9, 1),
-                               "mask_prepare_ms": map_ms(mview)}
+                               "fwd_live_block_frac_tensor": round(live * ff / tf / 1e9 / peak, 4),
+                               "algorithmic_fwd_bytes": mbytes + tfw,
+                               "algorithmic_fwd_bwd_bytes": 2 * mbytes + tfw + tbw,
+                               "fwd_frac_hbm": round((mbytes + tfw) / tf / 1e6 / hbm, 4),
+                               "fwd_bwd_frac_hbm": round((2 * mbytes + tfw + tbw) / (tf + tb) / 1e6 / hbm, 4),
+                               "mask_prepare_ms": prep,
+                               "mask_prepare_frac_hbm": round((mbytes + 2 * mbytes // 8) / prep / 1e6 / hbm, 4)}
     del mask, mview
     # cfg5: MQA, bshd, bottom-right causal, one GPU's shard of 16 (B=2)
-    tf, tb = fb(2, 1024, 4096, 64, 1, 64, _lib.CAUSAL_BOTTOM_RIGHT, iters=3)
+    tf, tb = fb(2, 1024, 4096, 64, 1, 64, _lib.CAUSAL_BOTTOM_RIGHT)
     ff, fbf = fwd_flops(2, 64, 1024, 4096, 64, True), fwd_bwd_flops(2, 64, 1024, 4096, 64, True)
-    tbd = fb(2, 1024, 4096, 64, 1, 64, _lib.CAUSAL_BOTTOM_RIGHT, iters=3, deterministic=True)[1]
+    tbd = fb(2, 1024, 4096, 64, 1, 64, _lib.CAUSAL_BOTTOM_RIGHT, deterministic=True)[1]
+    # Bottom-right causal with Tq=1024 < Tk=4096 keeps 87.5% of the (q, k) pairs, not the
+    # convention's 50%: the true work is 0.875 / 0.5 of the convention's FLOPs.
+    true_fb = fbf * 0.875 / 0.5
     out["cfg5_mqa_shard_b2"] = {"fwd_ms": round(tf, 4), "fwd_bwd_ms": round(tf + tb, 4),
                                 "fwd_bwd_tflops_convention": round(fbf / (tf + tb) / 1e9, 1),
+                                "fwd_bwd_tflops_true_work": round(true_fb / (tf + tb) / 1e9, 1),
+                                "fwd_bwd_frac_true_work": round(true_fb / (tf + tb) / 1e9 / peak, 4),
                                 "fwd_bwd_ms_use_atomic_backward_false": round(tf + tbd, 4)}
     # Head dim 256 at config 2's shape (its own kernels: one-slot forward, column-split
     # backward and the ordered dQ pass)
-    tf, tb = fb(B, T, T, HQ, HK, 256, _lib.CAUSAL_NONE, iters=3)
+    tf, tb = fb(B, T, T, HQ, HK, 256, _lib.CAUSAL_NONE, iters=5)
     ff, fbf = fwd_flops(B, HQ, T, T, 256, False), fwd_bwd_flops(B, HQ, T, T, 256, False)
     out["cfg2_shape_d256"] = {"fwd_ms": round(tf, 4), "fwd_tflops": round(ff / tf / 1e9, 1),
-                              "fwd_bwd_ms": round(tf + tb, 4), "fwd_bwd_tflops": round(fbf / (tf + tb) / 1e9, 1)}
+                              "fwd_bwd_ms": round(tf + tb, 4), "fwd_bwd_tflops": round(fbf / (tf + tb) / 1e9, 1),
+                              "fwd_bwd_frac": round(fbf / (tf + tb) / 1e9 / peak, 4)}
     return out
 
 
@@ -459,7 +540,7 @@ def library_context(dev, peaks):
     """Context only (not this library's work): the same config-2 shape through torch's
     scaled_dot_product_attention (whatever backend torch picks on this GPU) and, when
     it loads and runs on this GPU, flash_attn 2.x — fwd and fwd+bwd, non-causal and
-    causal, bf16, CUDA events, median of 5 after 2 warm-ups."""
+    causal, bf16, CUDA events, median of 20 after 3 warm-ups, L2 flushed before each."""
     out = {}
     g = torch.Generator(device=dev)
     g.manual_seed(9)
@@ -471,8 +552,8 @@ def library_context(dev, peaks):
         for causal in (False, True):
             c = 0.5 if causal else 1.0
             try:
-                tf = time_fn(lambda: run_fwd(causal, False), 5)
-                tfb = time_fn(lambda: run_fwd(causal, True), 5)
+                tf = time_fn(lambda: run_fwd(causal, False), 20)
+                tfb = time_fn(lambda: run_fwd(causal, True), 20)
             except Exception as exc:  # context only: report and go on
                 res["error"] = f"{type(exc).__name__}: {str(exc)[:160]}"
                 break
@@ -507,6 +588,89 @@ def library_context(dev, peaks):
 
         measure(fa, "flash_attn")
     return out
+
+
+# Runs in a child process whose working directory is baseline/_ref (the reference
+# installed unmodified, `pip install --target baseline/_ref`), so `python.fa2` is the
+# reference's own TileLang op and nothing of this repository is importable there.
+# Timed like the reference's benchmark (benchmark/throughput_check.py:206-256): fwd under
+# no_grad, fwd+bwd as forward + backward with fresh leaves; here the median of 20 CUDA-event
+# timings after 3 warm-ups (which include TileLang's JIT compilation), L2 flushed before each.
+_TILELANG_CONTEXT = r"""
+import json, statistics, sys, torch
+from python.fa2 import flash_attention_with_4d_mask
+B, T, HQ, HK, D = (int(x) for x in sys.argv[1:6])
+dev = torch.device("cuda", 0)
+g = torch.Generator(device=dev)
+g.manual_seed(9)
+mk = lambda h: torch.randn((B, T, h, D), generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
+q, k, v, do = mk(HQ), mk(HK), mk(HK), mk(HQ)
+flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+scale = D ** -0.5
+
+def med(fn, iters=20, warm=3):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(iters):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(); fn(); b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+out = {"tilelang": __import__("tilelang").__version__}
+for causal in (False, True):
+    c = 0.5 if causal else 1.0
+    def fwd():
+        with torch.no_grad():
+            flash_attention_with_4d_mask(q, k, v, None, None, scale, causal, True, True)
+    def fwd_bwd():
+        qq, kk, vv = (x.detach().requires_grad_(True) for x in (q, k, v))
+        flash_attention_with_4d_mask(qq, kk, vv, None, None, scale, causal, True, True).backward(do)
+    tag = "causal" if causal else "noncausal"
+    tf, tfb = med(fwd), med(fwd_bwd)
+    out[tag + "_fwd_ms"] = round(tf, 4)
+    out[tag + "_fwd_tflops"] = round(4.0 * B * HQ * T * T * D * c / tf / 1e9, 1)
+    out[tag + "_fwd_bwd_ms"] = round(tfb, 4)
+    out[tag + "_fwd_bwd_tflops"] = round(14.0 * B * HQ * T * T * D * c / tfb / 1e9, 1)
+print("CONTEXT " + json.dumps(out), flush=True)
+"""
+
+
+def tilelang_context(dev, timeout_s=1500):
+    """The reference's own TileLang kernels on this GPU at config 2 (context only)."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "python" / "fa2.py").exists():
+        return {"error": "baseline/_ref not installed"}
+    env = {k2: v2 for k2, v2 in os.environ.items() if k2 != "PYTHONPATH"}
+    env["CUDA_VISIBLE_DEVICES"] = str(dev.index if dev.index is not None else 0)
+    try:
+        res = subprocess.run([sys.executable, "-c", _TILELANG_CONTEXT, str(B), str(T), str(HQ), str(HK), str(D)],
+                             cwd=str(ref), env=env, capture_output=True, text=True, timeout=timeout_s)
+    except subprocess.TimeoutExpired:
+        return {"error": f"timed out after {timeout_s} s"}
+    for line in res.stdout.splitlines():
+        if line.startswith("CONTEXT "):
+            return json.loads(line[len("CONTEXT "):])
+    tail = (res.stderr or res.stdout).strip().splitlines()[-3:]
+    return {"error": f"exit {res.returncode}: " + " | ".join(tail)[:400]}
+
+
+def run_context(args):
+    """--impl context: library kernels on this GPU at config 2 (torch SDPA, flash_attn and
+    the reference's TileLang kernels), one JSON line; context, not this library's work."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return None
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    peaks, _ = load_peaks()
+    line = {"impl": "context", "config": {"workload": WORKLOAD}, "unit": UNIT}
+    line.update(library_context(dev, peaks))
+    line["reference_tilelang"] = tilelang_context(dev)
+    return line
 
 
 def run_e2e(api, dev, args, dist=None, world=1):
@@ -658,7 +822,7 @@ def main() -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--impl", choices=("ours", "reference", "context"), default="ours")
     # End-to-end steps (default: --steps).  The first step's upload and the last step's
     # download have no neighbour to overlap, so too few steps overstate their cost.
     ap.add_argument("--e2e-steps", type=int, default=None)
@@ -671,6 +835,8 @@ def main() -> int:
         args.e2e_steps = args.steps
     if args.impl == "reference":
         line = run_reference(args)
+    elif args.impl == "context":
+        line = run_context(args)
     else:
         import tilelang_fa2_4d_mask  # noqa: F401  (registers fa2_with_4d_mask_b200)
 

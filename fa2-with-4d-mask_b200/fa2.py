@@ -32,6 +32,7 @@ unchanged.
 
 from __future__ import annotations
 
+import os
 import weakref
 from typing import Optional
 
@@ -40,6 +41,11 @@ import torch
 from . import _lib
 
 _CAUSAL_ALIGN = {"top_left": _lib.CAUSAL_TOP_LEFT, "bottom_right": _lib.CAUSAL_BOTTOM_RIGHT}
+
+# FA4D_CHECK_STATUS=1 makes every backward synchronise and read the device status word
+# (bounded waits that gave up), raising instead of returning garbage gradients.  Off by
+# default: the read costs a host synchronisation per call.
+_CHECK_STATUS = os.environ.get("FA4D_CHECK_STATUS", "0") not in ("", "0")
 
 
 def causal_mode(is_causal: bool, causal_align: str = "top_left") -> int:
@@ -125,6 +131,52 @@ def _fwd_views(Q, K, V, bhsd_input):
     return _lib.as_tma(Q), _lib.as_tma(K), _lib.as_tma(V)
 
 
+def _check_inputs(Q, K, V, Mask, Score, bhsd_input) -> None:
+    """Rejects inputs the kernels would index out of bounds.  The C ABI takes Tq, Tk,
+    Hq and Hk from Q and K and trusts the strides of everything else, so a mask, score
+    or V of another shape must be refused here.  The reference rejects the same cases
+    through its kernels' typed tensor signatures (python/fa2.py:38-44) and its
+    wrapper's checks (python/modeling_attention.py:21-59)."""
+    for name, x in (("Q", Q), ("K", K), ("V", V)):
+        if not isinstance(x, torch.Tensor) or x.dim() != 4:
+            raise ValueError(f"{name} must be a rank-4 tensor")
+    if Q.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"Q must be fp16 or bf16, got {Q.dtype}")
+    if K.dtype != Q.dtype or V.dtype != Q.dtype:
+        raise ValueError("Q, K and V must have the same dtype")
+    if tuple(K.shape) != tuple(V.shape):
+        raise ValueError(f"K and V must have the same shape, got {tuple(K.shape)} and {tuple(V.shape)}")
+    if bhsd_input:
+        B, Hq, Tq, D = Q.shape
+        Bk, Hk, Tk, Dk = K.shape
+    else:
+        B, Tq, Hq, D = Q.shape
+        Bk, Tk, Hk, Dk = K.shape
+    if Bk != B:
+        raise ValueError("Q, K and V must have the same batch size")
+    if Dk != D:
+        raise ValueError("Q, K and V must have the same head dimension")
+    if Hk == 0 or Hq % Hk != 0:
+        raise ValueError(f"query heads ({Hq}) must be divisible by key/value heads ({Hk})")
+    for name, x, is_mask in (("Mask", Mask, True), ("Score", Score, False)):
+        if x is None:
+            continue
+        if not isinstance(x, torch.Tensor) or x.dim() != 4:
+            raise ValueError(f"{name} must have shape [B or 1, Hq or 1, Tq, Tk]")
+        if is_mask and x.dtype not in (torch.bool, torch.uint8):
+            raise ValueError("Mask must be a bool tensor with True for valid entries")
+        if not is_mask and not torch.is_floating_point(x):
+            raise ValueError("Score must be a floating-point tensor")
+        if tuple(x.shape[-2:]) != (Tq, Tk):
+            raise ValueError(f"{name} has trailing shape {tuple(x.shape[-2:])}, expected {(Tq, Tk)}")
+        if x.shape[0] not in (1, B):
+            raise ValueError(f"{name} batch dimension must be 1 or {B}")
+        if x.shape[1] not in (1, Hq):
+            raise ValueError(f"{name} head dimension must be 1 or {Hq}")
+        if x.device != Q.device:
+            raise ValueError(f"{name} must be on {Q.device}, got {x.device}")
+
+
 class _flash_attention_with_4d_mask(torch.autograd.Function):
     @staticmethod
     def forward(
@@ -141,7 +193,7 @@ class _flash_attention_with_4d_mask(torch.autograd.Function):
         causal_align: str = "top_left",
         doc_ids=None,
     ):
-        assert Q.dim() == 4 and K.dim() == 4 and V.dim() == 4
+        _check_inputs(Q, K, V, Mask, Score, bhsd_input)
         if not Q.is_cuda:
             raise RuntimeError("flash_attention_with_4d_mask runs on CUDA (sm_100a) tensors only")
         q, k, v = _fwd_views(Q, K, V, bhsd_input)
@@ -175,6 +227,12 @@ class _flash_attention_with_4d_mask(torch.autograd.Function):
         dO = _lib.as_tma(dO)
         dQ, dK, dV = _lib.backward(dO, q, k, v, O, LSE, mask, score, ctx.scale, ctx.mode, blocks=ctx.blocks,
                                    deterministic=ctx.use_atomic_backward is False)
+        if _CHECK_STATUS:
+            # Opt-in: synchronise and raise if any kernel since the last check gave up a
+            # bounded wait (its outputs are then garbage).
+            bits = _lib.device_status(q.device)
+            if bits:
+                raise RuntimeError(f"an attention kernel gave up a bounded wait (device status {bits:#x})")
         if ctx.bhsd_input:
             dQ, dK, dV = dQ.transpose(1, 2), dK.transpose(1, 2), dV.transpose(1, 2)
         return dQ, dK, dV, None, None, None, None, None, None, None, None

@@ -186,6 +186,12 @@ int fa4d_bwd_dq_convert(const fa4d_bwd_args* args, void* stream);
  * args->workspace / workspace_bytes: the scratch (fp32 dQ accumulator and Delta) is a
  * fixed buffer of FA4D_BWD_NOALLOC_MAX_WORKSPACE bytes inside the library, which every
  * GPU that loads the library keeps until the process exits.  Nothing is allocated.
+ *  - The buffer is device memory of the library's code module.  The CUDA runtime
+ *    reserves it on a device when it loads that module there: at the first call of
+ *    any fa4d entry point on that device under lazy module loading (the CUDA 12
+ *    default), or when the library is loaded with CUDA_MODULE_LOADING=EAGER.  A host
+ *    whose memory pool reserves all device memory should make one fa4d call per
+ *    device before the pool does, or that first call fails with FA4D_ERR_CUDA.
  *  - Problems whose fa4d_bwd_workspace_size() exceeds the buffer are rejected with
  *    FA4D_ERR_WORKSPACE (e.g. B=1, Hq=32, D=128 fits up to Tq = 3968).
  *  - The first call on a device looks up the buffer's device address (no

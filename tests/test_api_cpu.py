@@ -173,3 +173,85 @@ def test_doc_id_parsing():
         impl_fa2._doc_ids((torch.zeros(1, 8, dtype=torch.int64), torch.zeros(1, 7, dtype=torch.int64)), 1, 8, 9, "cpu")
     with pytest.raises(ValueError, match="integer"):
         impl_fa2._doc_ids(torch.zeros(1, 8), 1, 8, 8, "cpu")
+
+
+def _op_inputs(bhsd=True):
+    """Q [1, 4, 16, 64], K/V [1, 2, 24, 64] (BHSD) or their BSHD transposes."""
+    q, k, v = qkv(B=1, Hq=4, Hk=2, Tq=16, Tk=24, D=64)
+    if not bhsd:
+        q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    return q, k, v
+
+
+@pytest.mark.parametrize(
+    "case,msg",
+    [
+        ("v_seq", "K and V must have the same shape"),
+        ("v_heads", "K and V must have the same shape"),
+        ("k_batch", "same batch size"),
+        ("k_dim", "same head dimension"),
+        ("gqa", r"query heads \(3\) must be divisible by key/value heads \(2\)"),
+        ("mask_rank", r"Mask must have shape \[B or 1, Hq or 1, Tq, Tk\]"),
+        ("mask_tq", r"Mask has trailing shape \(15, 24\), expected \(16, 24\)"),
+        ("mask_tk", r"Mask has trailing shape \(16, 23\), expected \(16, 24\)"),
+        ("mask_heads_hk", "Mask head dimension must be 1 or 4"),
+        ("mask_batch", "Mask batch dimension must be 1 or 1"),
+        ("mask_float", "Mask must be a bool tensor"),
+        ("score_tk", r"Score has trailing shape \(16, 25\), expected \(16, 24\)"),
+        ("score_heads", "Score head dimension must be 1 or 4"),
+        ("score_int", "Score must be a floating-point tensor"),
+        ("dtype", "must have the same dtype"),
+        ("fp32", "Q must be fp16 or bf16"),
+    ],
+)
+@pytest.mark.parametrize("bhsd", [True, False])
+def test_op_rejects_shapes_the_kernels_would_read_out_of_bounds(case, msg, bhsd):
+    """The autograd op (not only the wrapper) refuses mask / score / V shapes that do
+    not match Q and K, before anything reaches the C ABI."""
+    q, k, v = _op_inputs(bhsd)
+    mask = score = None
+    seq = 2 if bhsd else 1  # sequence axis of Q/K/V in this layout
+    head = 1 if bhsd else 2
+    if case == "v_seq":
+        v = v.narrow(seq, 0, 20)
+    elif case == "v_heads":
+        v = v.narrow(head, 0, 1)
+    elif case == "k_batch":
+        k, v = torch.cat([k, k]), torch.cat([v, v])
+    elif case == "k_dim":
+        k, v = k[..., :32], v[..., :32]
+    elif case == "gqa":
+        q = q.narrow(head, 0, 3)
+    elif case == "mask_rank":
+        mask = torch.ones(16, 24, dtype=torch.bool)
+    elif case == "mask_tq":
+        mask = torch.ones(1, 1, 15, 24, dtype=torch.bool)
+    elif case == "mask_tk":
+        mask = torch.ones(1, 1, 16, 23, dtype=torch.bool)
+    elif case == "mask_heads_hk":
+        mask = torch.ones(1, 2, 16, 24, dtype=torch.bool)
+    elif case == "mask_batch":
+        mask = torch.ones(2, 1, 16, 24, dtype=torch.bool)
+    elif case == "mask_float":
+        mask = torch.ones(1, 1, 16, 24)
+    elif case == "score_tk":
+        score = torch.zeros(1, 4, 16, 25)
+    elif case == "score_heads":
+        score = torch.zeros(1, 2, 16, 24)
+    elif case == "score_int":
+        score = torch.zeros(1, 4, 16, 24, dtype=torch.int32)
+    elif case == "dtype":
+        v = v.half()
+    elif case == "fp32":
+        q, k, v = q.float(), k.float(), v.float()
+    with pytest.raises(ValueError, match=msg):
+        api.flash_attention_with_4d_mask(q, k, v, mask, score, None, False, True, bhsd)
+
+
+def test_op_accepts_broadcast_mask_and_score_then_needs_cuda():
+    """Well-formed inputs pass the checks and reach the (absent) device path."""
+    q, k, v = _op_inputs()
+    mask = torch.ones(1, 1, 16, 24, dtype=torch.bool)
+    score = torch.zeros(1, 4, 16, 24)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        api.flash_attention_with_4d_mask(q, k, v, mask, score, None, False, True, True)

@@ -42,3 +42,7 @@ def test_bench_line_contract():
     # when the group split is on.
     assert line["gpu_launches"] in (4 * 3, 5 * 3)
     assert "sm_mhz" in line["clocks"] or "error" in line["clocks"]
+    # The causal leg is measured like the headline and reports its own fractions.
+    c = line["causal"]
+    assert c["fwd_ms"] > 0 and c["fwd_bwd_ms"] > c["fwd_ms"]
+    assert 0 < c["fwd_frac_of_peak"] < 2 and 0 < c["fwd_bwd_frac_of_peak"] < 2

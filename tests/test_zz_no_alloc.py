@@ -25,7 +25,7 @@ G_REL = 3e-2  # same gradient tolerance as the parity tests
 I3 = ctypes.c_int64 * 3
 
 
-def _args(q, k, v, o, lse, do, dq, dk, dv, mask, scale, causal):
+def _args(q, k, v, o, lse, do, dq, dk, dv, mask, scale, causal, deterministic):
     a = _lib.BwdArgs()
     a.q, a.k, a.v, a.o, a.dout, a.lse = (t.data_ptr() for t in (q, k, v, o, do, lse))
     a.dq, a.dk, a.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
@@ -38,14 +38,15 @@ def _args(q, k, v, o, lse, do, dq, dk, dv, mask, scale, causal):
                            mask.stride(2))
     B, Tq, Hq, D = q.shape
     a.B, a.Tq, a.Tk, a.Hq, a.Hk, a.D = B, Tq, k.shape[1], Hq, k.shape[2], D
-    a.dtype, a.causal, a.scale = _lib.FA4D_BF16, causal, scale
+    a.dtype = _lib.FA4D_BF16 if q.dtype == torch.bfloat16 else _lib.FA4D_F16
+    a.causal, a.scale, a.deterministic = causal, scale, deterministic
     return a
 
 
-def _grads(entry, q, k, v, o, lse, do, mask, scale, causal):
+def _grads(entry, q, k, v, o, lse, do, mask, scale, causal, deterministic):
     lib = _lib.load_library()
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    a = _args(q, k, v, o, lse, do, dq, dk, dv, mask, scale, causal)
+    a = _args(q, k, v, o, lse, do, dq, dk, dv, mask, scale, causal, deterministic)
     ws = None
     if entry == "fa4d_bwd":
         B, Tq, Hq, D = q.shape
@@ -59,28 +60,43 @@ def _grads(entry, q, k, v, o, lse, do, mask, scale, causal):
 
 
 PROBLEMS = [
-    # (B, Tq, Tk, Hq, Hk, D, causal mode, with mask)
-    (1, 1024, 1024, 8, 2, 128, _lib.CAUSAL_TOP_LEFT, False),
-    (2, 300, 520, 4, 4, 64, _lib.CAUSAL_NONE, True),
+    # (B, Tq, Tk, Hq, Hk, D, causal mode, with mask, deterministic, dtype)
+    (1, 1024, 1024, 8, 2, 128, _lib.CAUSAL_TOP_LEFT, False, 0, torch.bfloat16),
+    (2, 300, 520, 4, 4, 64, _lib.CAUSAL_NONE, True, 0, torch.bfloat16),
+    # The bit-reproducible backward: dQ from the ordered pass, which shares only the
+    # Delta region of the buffer (no accumulator to clear).
+    (1, 700, 900, 8, 2, 128, _lib.CAUSAL_BOTTOM_RIGHT, False, 1, torch.bfloat16),
+    # Head dim 256: the scratch is Delta only, in both backward modes.
+    (1, 384, 384, 4, 2, 256, _lib.CAUSAL_TOP_LEFT, False, 0, torch.bfloat16),
+    (1, 256, 320, 2, 1, 256, _lib.CAUSAL_NONE, True, 1, torch.bfloat16),
+    (2, 513, 513, 4, 1, 128, _lib.CAUSAL_TOP_LEFT, True, 0, torch.float16),
+    # The first problem again, after every other one has left its contents behind.
+    (1, 1024, 1024, 8, 2, 128, _lib.CAUSAL_TOP_LEFT, False, 0, torch.bfloat16),
 ]
 
 
 @pytest.mark.gpu
 def test_noalloc_matches_workspace_backward_on_two_calls_in_a_row():
+    """Each problem is run through fa4d_bwd (caller workspace) and then fa4d_bwd_noalloc;
+    consecutive noalloc calls reuse the one built-in buffer.  dK/dV never use atomics and
+    must match bit for bit; so must dQ where it comes from the ordered pass
+    (deterministic mode, or head dim 256 in either mode)."""
     dev = torch.device("cuda", 0)
-    for i, (B, Tq, Tk, Hq, Hk, D, causal, with_mask) in enumerate(PROBLEMS):
-        q, k, v, do = (x.to(dev).transpose(1, 2).contiguous() for x in I.qkv(B, Tq, Tk, Hq, Hk, D, seed=40 + i))
+    for i, (B, Tq, Tk, Hq, Hk, D, causal, with_mask, det, dtype) in enumerate(PROBLEMS):
+        q, k, v, do = (x.to(dev).transpose(1, 2).contiguous()
+                       for x in I.qkv(B, Tq, Tk, Hq, Hk, D, seed=40 + i, dtype=dtype))
         mask = I.random_mask(1, 1, Tq, Tk, 0.8, seed=9).to(dev) if with_mask else None
         scale = D ** -0.5
         o, lse = _lib.forward(q, k, v, mask, None, scale, causal)
-        ref = _grads("fa4d_bwd", q, k, v, o, lse, do, mask, scale, causal)
-        got = _grads("fa4d_bwd_noalloc", q, k, v, o, lse, do, mask, scale, causal)
+        ref = _grads("fa4d_bwd", q, k, v, o, lse, do, mask, scale, causal, det)
+        got = _grads("fa4d_bwd_noalloc", q, k, v, o, lse, do, mask, scale, causal, det)
         for name, g, r in zip(("dQ", "dK", "dV"), got, ref):
             assert torch.isfinite(g.float()).all(), f"call {i}: {name} not finite"
             e = rel_err(g, r)
             assert e <= G_REL, f"call {i}: {name} rel={e:.3e}"
-        # dK/dV have no atomics: the two entry points must agree bit for bit.
-        assert torch.equal(got[1], ref[1]) and torch.equal(got[2], ref[2])
+        assert torch.equal(got[1], ref[1]) and torch.equal(got[2], ref[2]), f"call {i}: dK/dV differ"
+        if det or D == 256:
+            assert torch.equal(got[0], ref[0]), f"call {i}: ordered-pass dQ differs"
     assert _lib.device_status(dev) == 0
 
 
