@@ -96,14 +96,46 @@ __device__ __forceinline__ uint32_t keep_word(const uint4& a, const uint4& b) {
 //     (bit j of word w = key 128*kt + 32*w + j), read by the forward;
 //   column bits [Bm*Hm][nqt][Tk][2] words: 64 queries of query tile qt for key k
 //     (bit j of word w = query 64*qt + 32*w + j), read by the backward.
-// Keys / queries past Tk / Tq read as 0.  Grid: (ceil(Tk / 512), ceil(Tq / 128),
-// Bm * Hm), 128 threads; warp w owns query rows 32w..32w+31 of the block row
-// (lane = row) and walks 16 chunks of 32 keys; column words come from one ballot per key.
-// Source of the keep flags: mask bytes (kVec: 16-byte loads) or per-token document
-// ids (kDocs: keep iff the query's and the key's ids are equal and not negative).
-template <bool kVec, bool kDocs>
+// Keys / queries past Tk / Tq read as 0.
+//
+// One CTA walks kPrepTiles consecutive 128 x 128 blocks of one 128-row block row
+// (grid (ceil(nkb / kPrepTiles), nqb, Bm * Hm), 128 threads); per block:
+//   1. the block's keep flags as bytes into shared memory: thread t covers the 16-key
+//      chunk t % 8 of rows t / 8 + 16 i (i < 8), so each group of 8 threads reads 128
+//      contiguous bytes of one row (kSrc 0: 16-byte loads, issued for the next block
+//      before the current one is packed, so loads stay in flight); or byte loads (kSrc
+//      1: unaligned rows or Tk % 16 != 0); or flags computed from document ids (kSrc 2:
+//      keep iff the query's and key's ids are equal and not negative);
+//   2. thread r packs row r's 128 flags into 4 words and stores them as one 16-byte
+//      vector (the CTA's 128 rows are one contiguous 2 KB run of the row bits);
+//   3. warp w (rows 32w..32w+31, lane = row) transposes each 32 x 32 bit block of its
+//      words with five shuffle steps, so lane i holds the column word of key 32 j + i;
+//      the words go through shared memory and thread t writes key t's two words of each
+//      64-row query tile as one 8-byte vector (contiguous over the CTA's keys).
+// Rows are padded to 144 bytes in shared memory, so both the chunk stores of step 1 and
+// the row reads of step 2 are free of bank conflicts.
+constexpr int kPrepTiles = 4;
+
+// 32 x 32 bit transpose across a warp: lane i holds row i (bit j = column j) and gets
+// column i (bit j = row j).  Each step swaps the off-diagonal s x s sub-blocks of every
+// 2s x 2s block (s = 16, 8, 4, 2, 1), which composes to the full transpose.
+__device__ __forceinline__ uint32_t transpose32(uint32_t x, int lane) {
+  constexpr uint32_t kMask[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    const int sh = 16 >> i;
+    const uint32_t m = kMask[i];
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, x, sh);
+    x = (lane & sh) ? ((x & ~m) | ((y & ~m) >> sh)) : ((x & m) | ((y & m) << sh));
+  }
+  return x;
+}
+
+template <int kSrc>
 __global__ void __launch_bounds__(128) mask_prepare_kernel(const MaskPrepParams p) {
-  __shared__ uint32_t s_any[4], s_all[4];
+  constexpr int kPitch = 144;
+  __shared__ __align__(16) uint8_t tile[128 * kPitch];
+  __shared__ uint32_t cols[4][128];  // [32-row quarter][key]: column word of that quarter
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -111,94 +143,114 @@ __global__ void __launch_bounds__(128) mask_prepare_kernel(const MaskPrepParams 
   const int b = bh / p.Hm;
   const int h = bh - b * p.Hm;
   const int qb = blockIdx.y;
-  const int q0w = qb * 128 + 32 * warp;  // first row of this warp
-  const int row = q0w + lane;
-  const bool row_ok = row < p.Tq;
-  if (tid < 4) {
-    s_any[tid] = 0u;
-    s_all[tid] = 1u;
-  }
-  __syncthreads();
-  const uint8_t* src = kDocs ? nullptr
-                             : p.mask + b * p.stride[0] + h * p.stride[1] +
-                                   static_cast<int64_t>(row_ok ? row : 0) * p.stride[2];
-  const int32_t doc_row = (kDocs && row_ok) ? __ldg(p.doc_q + b * p.doc_q_stride + row) : -1;
-  uint32_t* row_bits = p.row_bits + static_cast<int64_t>(bh) * p.nkb * p.Tq * 4;
-  // This warp's 32 rows are half (q0w / 32) % 2 of query tile q0w / 64.
-  const int qt = q0w >> 6;
-  const bool col_ok = qt < p.nqt;
-  uint32_t* col_bits = p.col_bits + (static_cast<int64_t>(bh) * p.nqt + qt) * p.Tk * 2 + ((q0w >> 5) & 1);
-  bool any_blk = false, all_blk = true;
-#pragma unroll 1
-  for (int it = 0; it < 16; ++it) {
-    const int kc = blockIdx.x * 512 + 32 * it;
-    // Keys of this chunk inside Tk (as bits).
-    const int nin = min(max(p.Tk - kc, 0), 32);
-    const uint32_t inb = nin >= 32 ? 0xffffffffu : ((1u << nin) - 1u);
-    uint32_t rw = 0u;
-    if (kDocs) {
-      // Lane j holds key kc+j's document; each row compares against all 32.
-      const int32_t doc_key = (kc + lane < p.Tk) ? __ldg(p.doc_k + b * p.doc_k_stride + kc + lane) : -2;
+  const int q0 = qb * 128;
+  const int kt0 = blockIdx.x * kPrepTiles;
+  const int c = tid & 7, r0 = tid >> 3;
+  const uint8_t* mask_base = kSrc == 2 ? nullptr : p.mask + b * p.stride[0] + h * p.stride[1];
+
+  // kSrc 0: one block's 16-byte chunks, loaded into registers ahead of their use.
+  auto load_block = [&](int kt, uint4 (&v)[8]) {
+    const int kk = kt * 128 + 16 * c;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int32_t dk = __shfl_sync(0xffffffffu, doc_key, j);
-        if (doc_row >= 0 && dk == doc_row) rw |= 1u << j;
-      }
-    } else if (row_ok && nin > 0) {
-      if (kVec) {
-        // Tk % 16 == 0: each 16-byte half is entirely in or out of bounds.
-        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-        const uint4 a = __ldg(reinterpret_cast<const uint4*>(src + kc));
-        const uint4 c = nin > 16 ? __ldg(reinterpret_cast<const uint4*>(src + kc + 16)) : z;
-        rw = keep_word(a, c);
-      } else {
-#pragma unroll 4
-        for (int j = 0; j < 32; ++j)
-          if (j < nin && __ldg(src + kc + j) != 0) rw |= 1u << j;
-      }
+    for (int i = 0; i < 8; ++i) {
+      const int q = q0 + r0 + 16 * i;
+      // Tk % 16 == 0: a 16-key chunk is entirely inside or outside Tk.
+      v[i] = (q < p.Tq && kk < p.Tk)
+                 ? __ldg(reinterpret_cast<const uint4*>(mask_base + static_cast<int64_t>(q) * p.stride[2] + kk))
+                 : make_uint4(0u, 0u, 0u, 0u);
     }
-    rw &= inb;
-    const int kt = kc >> 7;
-    if (row_ok && kt < p.nkb) row_bits[(static_cast<int64_t>(kt) * p.Tq + row) * 4 + ((kc >> 5) & 3)] = rw;
-    // Column words: bit `lane` of the ballot for key kc+j is row q0w+lane's flag.
-    uint32_t mine = 0u;
+  };
+  uint4 v[8];
+  if constexpr (kSrc == 0) load_block(kt0, v);
+
+  for (int u = 0; u < kPrepTiles; ++u) {
+    const int kt = kt0 + u;
+    if (kt >= p.nkb) break;
+    const int k0 = kt * 128;
+    __syncthreads();  // the previous block's shared-memory reads are done
+    // ---- 1. keep flags as bytes
+    if constexpr (kSrc == 0) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const uint32_t bal = __ballot_sync(0xffffffffu, (rw >> j) & 1u);
-      if (lane == j) mine = bal;
-    }
-    if (kc + lane < p.Tk && col_ok) col_bits[static_cast<int64_t>(kc + lane) * 2] = mine;
-    any_blk = any_blk || __any_sync(0xffffffffu, rw != 0u);
-    all_blk = all_blk && __all_sync(0xffffffffu, !row_ok || rw == inb);
-    if ((it & 3) == 3) {
-      if (lane == 0) {
-        if (any_blk) atomicOr(&s_any[it >> 2], 1u);
-        if (!all_blk) atomicAnd(&s_all[it >> 2], 0u);
+      for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(tile + (r0 + 16 * i) * kPitch + 16 * c) = v[i];
+      if (u + 1 < kPrepTiles && kt + 1 < p.nkb) load_block(kt + 1, v);
+    } else if constexpr (kSrc == 1) {
+      const int kk = k0 + 16 * c;
+      for (int i = 0; i < 8; ++i) {
+        const int q = q0 + r0 + 16 * i;
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        if (q < p.Tq) {
+          const uint8_t* row = mask_base + static_cast<int64_t>(q) * p.stride[2];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (kk + e < p.Tk && __ldg(row + kk + e) != 0) w[e >> 2] |= 1u << (8 * (e & 3));
+        }
+        *reinterpret_cast<uint4*>(tile + (r0 + 16 * i) * kPitch + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      any_blk = false;
-      all_blk = true;
+    } else {
+      const int kk = k0 + 16 * c;
+      int32_t dk[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) dk[e] = kk + e < p.Tk ? __ldg(p.doc_k + b * p.doc_k_stride + kk + e) : -2;
+      for (int i = 0; i < 8; ++i) {
+        const int q = q0 + r0 + 16 * i;
+        const int32_t dq = q < p.Tq ? __ldg(p.doc_q + b * p.doc_q_stride + q) : -1;
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (dq >= 0 && dk[e] == dq) w[e >> 2] |= 1u << (8 * (e & 3));
+        *reinterpret_cast<uint4*>(tile + (r0 + 16 * i) * kPitch + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
     }
-  }
-  __syncthreads();
-  if (tid < 4) {
-    const int kb = blockIdx.x * 4 + tid;
-    if (kb < p.nkb) {
-      const uint8_t state = s_any[tid] ? (s_all[tid] ? 2 : 1) : 0;
-      p.blocks[(static_cast<int64_t>(bh) * p.nqb + qb) * p.nkb + kb] = state;
+    __syncthreads();
+
+    // ---- 2. row bits (thread = row)
+    const int row = q0 + tid;
+    const bool row_ok = row < p.Tq;
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 x = *reinterpret_cast<const uint4*>(tile + tid * kPitch + 32 * j);
+      const uint4 y = *reinterpret_cast<const uint4*>(tile + tid * kPitch + 32 * j + 16);
+      w[j] = keep_word(x, y);
     }
+    if (row_ok)
+      *reinterpret_cast<uint4*>(p.row_bits + ((static_cast<int64_t>(bh) * p.nkb + kt) * p.Tq + row) * 4) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    // Block state over the in-bounds elements only.
+    bool full = true;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) full = full && (w[j] == low_bits(p.Tk - k0 - 32 * j));
+    const int any = __syncthreads_or(row_ok && (w[0] | w[1] | w[2] | w[3]) != 0u);
+    const int all = __syncthreads_and(!row_ok || full);
+
+    // ---- 3. column bits: bit transpose of the warp's 32 rows (lane = row)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) cols[warp][32 * j + lane] = transpose32(w[j], lane);
+    __syncthreads();
+    const int k = k0 + tid;
+    if (k < p.Tk) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int qt = 2 * qb + t;
+        if (qt < p.nqt)
+          *reinterpret_cast<uint2*>(p.col_bits + ((static_cast<int64_t>(bh) * p.nqt + qt) * p.Tk + k) * 2) =
+              make_uint2(cols[2 * t][tid], cols[2 * t + 1][tid]);
+      }
+    }
+    if (tid == 0) p.blocks[(static_cast<int64_t>(bh) * p.nqb + qb) * p.nkb + kt] = any ? (all ? 2 : 1) : 0;
   }
 }
 
 }  // namespace
 
 cudaError_t launch_mask_prepare(const MaskPrepParams& p, cudaStream_t s) {
-  dim3 grid((p.Tk + 511) / 512, p.nqb, p.Bm * p.Hm);
+  dim3 grid((p.nkb + kPrepTiles - 1) / kPrepTiles, p.nqb, p.Bm * p.Hm);
   if (p.doc_q)
-    mask_prepare_kernel<false, true><<<grid, 128, 0, s>>>(p);
+    mask_prepare_kernel<2><<<grid, 128, 0, s>>>(p);
   else if (p.vec)
-    mask_prepare_kernel<true, false><<<grid, 128, 0, s>>>(p);
+    mask_prepare_kernel<0><<<grid, 128, 0, s>>>(p);
   else
-    mask_prepare_kernel<false, false><<<grid, 128, 0, s>>>(p);
+    mask_prepare_kernel<1><<<grid, 128, 0, s>>>(p);
   return cudaGetLastError();
 }
 
