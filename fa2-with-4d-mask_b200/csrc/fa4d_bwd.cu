@@ -9,17 +9,18 @@
 // every query head of its GQA group, so dK/dV are summed in tensor memory and
 // stored once in the input dtype (the reference sums the group with fp32 atomics,
 // python/fa2.py:299-302, or with a bf16 host-side sum, python/fa2.py:548-549).
-// Each 64-query dQ tile is staged in shared memory and added to an fp32
-// accumulator with one bulk reduction (cp.reduce.async.bulk ... add.f32).
+// Each 64-query dQ tile is added to an fp32 accumulator straight from registers
+// (red.global.add.f32, one contiguous run of D columns per warp and query).
 //
 // CTA = 128 keys x one (batch, KV head); 512 threads:
 //   warp 0       TMA producer (K/V once; Q, dO, LSE, Delta per 64-row query tile,
 //                3-stage ring)
-//   warp 1       tcgen05.mma issuer, two query tiles ahead of the P/dS warpgroups
+//   warps 1, 3   tcgen05.mma issuers, two query tiles ahead of the P/dS warpgroups:
+//                warp 1 issues S^T and dV, warp 3 issues dP^T, dK and dQ^T
 //   warp 2       TMEM allocator
 //   warps 4-7    P / dS of the even query tiles (one thread per key row), then dV out
 //   warps 8-11   P / dS of the odd query tiles, then dK out
-//   warps 12-15  dQ drain: TMEM -> shared staging -> bulk reduce-add into global
+//   warps 12-15  dQ drain: TMEM -> registers -> reduce-add into the global accumulator
 // The two P/dS warpgroups ping-pong, so the hand-off latency of one tile (MMA
 // completion -> P -> MMA -> dS -> MMA) overlaps the other tile's work.
 // TMEM (512 columns): S^T x2 [0,128), X x2 [128,256) (a tile's dP^T, later its
@@ -52,17 +53,15 @@ struct BwdLayout {
   static constexpr int kKV = 128 * D * 2;   // K or V tile (128 keys)
   static constexpr int kQT = 64 * D * 2;    // Q or dO tile (64 queries)
   static constexpr int kDS = 128 * 64 * 2;  // dS^T tile (128 keys x 64 queries, 16-bit)
-  static constexpr int kDQS = 64 * D * 4;   // dQ staging tile (64 queries x D, fp32)
   static constexpr int kK = 0;
   static constexpr int kV = kK + kKV;
   static constexpr int kQ = kV + kKV;                 // kQStages stages
   static constexpr int kDO = kQ + kQStages * kQT;     // kQStages stages
   static constexpr int kDSb = kDO + kQStages * kQT;   // 2 buffers
-  static constexpr int kDQs = kDSb + 2 * kDS;
-  static constexpr int kLSE = kDQs + kDQS;               // kQStages x 64 floats
+  static constexpr int kLSE = kDSb + 2 * kDS;            // kQStages x 64 floats
   static constexpr int kDelta = kLSE + kQStages * 256;   // kQStages x 64 floats
   static constexpr int kBar = kDelta + kQStages * 256;
-  static constexpr int kNumBars = 25;
+  static constexpr int kNumBars = 24;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -119,20 +118,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* kv_full = bars + 0;
-  uint64_t* dkv_full = bars + 1;
-  uint64_t* mma_drain = bars + 2;
-  uint64_t* stage_free = bars + 3;
-  uint64_t* stage_full = bars + 4;
+  uint64_t* dkv_full = bars + 1;   // dV and dK complete (one arrival per MMA issuer)
+  uint64_t* mma_drain = bars + 2;  // MMAs of issuer warp 1 complete
+  uint64_t* mma_drain_b = bars + 3;  // MMAs of issuer warp 3 complete
   // Per tile parity (tile it uses buffer it & 1; each is owned by one P/dS warpgroup).
-  uint64_t* s_full = bars + 5;     // [2] S^T of the tile is in TMEM
-  uint64_t* p_full = bars + 7;     // [2] P^T written to TMEM (128 arrivals)
-  uint64_t* dp_full = bars + 9;    // [2] dP^T of the tile is in TMEM
-  uint64_t* ds_full = bars + 11;   // [2] dS^T written to smem (128 arrivals)
-  uint64_t* ds_empty = bars + 13;  // [2] dS^T smem buffer free again
-  uint64_t* dq_full = bars + 15;   // [2] dQ^T of the tile is in TMEM
-  uint64_t* dq_empty = bars + 17;  // [2] drain has read dQ^T (128 arrivals)
-  uint64_t* q_full = bars + 19;    // [kQStages]
-  uint64_t* q_empty = bars + 22;   // [kQStages]
+  uint64_t* s_full = bars + 4;     // [2] S^T of the tile is in TMEM
+  uint64_t* p_full = bars + 6;     // [2] P^T written to TMEM (128 arrivals)
+  uint64_t* dp_full = bars + 8;    // [2] dP^T of the tile is in TMEM
+  uint64_t* ds_full = bars + 10;   // [2] dS^T written to smem (128 arrivals)
+  uint64_t* ds_empty = bars + 12;  // [2] dS^T smem buffer free again
+  uint64_t* dq_full = bars + 14;   // [2] dQ^T of the tile is in TMEM
+  uint64_t* dq_empty = bars + 16;  // [2] drain has read dQ^T (128 arrivals)
+  uint64_t* q_full = bars + 18;    // [kQStages]
+  uint64_t* q_empty = bars + 21;   // [kQStages] (2 arrivals: the last dV and the last dK reading the stage)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -175,10 +173,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(dkv_full, 1);
+    mbar_init(dkv_full, 2);
     mbar_init(mma_drain, 1);
-    mbar_init(stage_free, 1);
-    mbar_init(stage_full, 128);
+    mbar_init(mma_drain_b, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
@@ -190,7 +187,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     }
     for (int i = 0; i < kQStages; ++i) {
       mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
+      mbar_init(&q_empty[i], 2);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -256,12 +253,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       }
     }
     __syncwarp();
-    } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    // Runs two tiles ahead: S and dP of tile it+2 are issued while the P/dS
-    // warpgroups work on tiles it and it+1.  The whole warp runs the loop (waits
-    // included); each group of MMAs and its commits is issued by one elected lane.
+    } else if (warp == 1 || warp == 3) {
+    // ------------------------------------------------------------ MMA issuers
+    // One tcgen05.mma issue occupies the issuing thread for about 45 SM clocks, longer
+    // than an N = 64 product runs, so one issuing thread cannot keep the tensor pipe
+    // busy with this tile's 32 instructions; two threads can.  Warp 1 issues S^T and dV
+    // (it alone writes the S^T buffers and the dV accumulator), warp 3 issues dP^T, dK
+    // and dQ^T (the X buffers, the dK accumulator, the dS^T shared buffers), so every
+    // TMEM region is written and later reused by one issuer, whose own issue order
+    // keeps its reads before its overwrites.  Each runs two tiles ahead of the P/dS
+    // warpgroups; the whole warp runs the loop (waits included) and one elected lane
+    // issues each group of MMAs and its commits.
     if (any_work) {
+      const bool is_a = warp == 1;
       const uint32_t sK = smem_u32(smem + L::kK);
       const uint32_t sV = smem_u32(smem + L::kV);
       const uint32_t sQ = smem_u32(smem + L::kQ);
@@ -272,7 +276,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       };
       bool ok = wait(kv_full, 0);
       // `ahead` walks the pair list two entries in front of `it`; n_known counts the
-      // pairs whose S and dP have been issued.
+      // pairs whose first product (S^T, or dP^T) has been issued.
       QTiles<kMask> ahead = first;
       int n_known = 0;
       for (int j = 0; ok && j < 2 && ahead.valid(); ++j, ahead.advance(), ++n_known) {
@@ -280,10 +284,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         if (!ok) break;
         tc_fence_after();
         if (elect_one()) {
-          issue_kt<D, kBF16>(tmem + kColS + 64 * j, sK, sQ + j * L::kQT);
-          tc_commit(&s_full[j]);
-          issue_kt<D, kBF16>(tmem + kColX + 64 * j, sV, sDO + j * L::kQT);
-          tc_commit(&dp_full[j]);
+          if (is_a) {
+            issue_kt<D, kBF16>(tmem + kColS + 64 * j, sK, sQ + j * L::kQT);
+            tc_commit(&s_full[j]);
+          } else {
+            issue_kt<D, kBF16>(tmem + kColX + 64 * j, sV, sDO + j * L::kQT);
+            tc_commit(&dp_full[j]);
+          }
         }
         __syncwarp();
       }
@@ -291,56 +298,63 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         const int st = it & 1;
         const uint32_t par = (it >> 1) & 1;
         const int qs = it % kQStages;
-        ok = wait(&p_full[st], par);
-        if (!ok) break;
-        tc_fence_after();
-        if (elect_one()) issue_dv<D, kBF16>(tmem + kColDV, tmem + kColS + 64 * st, sDO + qs * L::kQT, it > 0);
-        __syncwarp();
-        ok = wait(&ds_full[st], par);
-        if (!ok) break;
-        tc_fence_after();
-        if (elect_one()) {
-          issue_dk<D, kBF16>(tmem + kColDK, tmem + kColX + 64 * st, sQ + qs * L::kQT, it > 0);
-          tc_commit(&q_empty[qs]);
-          if (!p.skip_dq) {
-            // dQ^T overwrites this tile's dP^T (read before ds_full).
-            issue_dq<D, kBF16>(tmem + kColX + 64 * st, sK, sDS + st * L::kDS);
-            tc_commit(&dq_full[st]);
+        if (is_a) {
+          ok = wait(&p_full[st], par);
+          if (!ok) break;
+          tc_fence_after();
+          if (elect_one()) {
+            issue_dv<D, kBF16>(tmem + kColDV, tmem + kColS + 64 * st, sDO + qs * L::kQT, it > 0);
+            tc_commit(&q_empty[qs]);
           }
-          tc_commit(&ds_empty[st]);
+          __syncwarp();
+        } else {
+          ok = wait(&ds_full[st], par);
+          if (!ok) break;
+          tc_fence_after();
+          if (elect_one()) {
+            issue_dk<D, kBF16>(tmem + kColDK, tmem + kColX + 64 * st, sQ + qs * L::kQT, it > 0);
+            tc_commit(&q_empty[qs]);
+            if (!p.skip_dq) {
+              // dQ^T overwrites this tile's dP^T (read before ds_full).
+              issue_dq<D, kBF16>(tmem + kColX + 64 * st, sK, sDS + st * L::kDS);
+              tc_commit(&dq_full[st]);
+            }
+            tc_commit(&ds_empty[st]);
+          }
+          __syncwarp();
         }
-        __syncwarp();
-        const int jn = it + 2;
         if (ahead.valid()) {
+          const int jn = it + 2;
           ahead.advance();
           ++n_known;
           const int qn = jn % kQStages;
           ok = wait(&q_full[qn], (jn / kQStages) & 1);
           if (!ok) break;
-          tc_fence_after();
-          if (elect_one()) {
-            issue_kt<D, kBF16>(tmem + kColS + 64 * st, sK, sQ + qn * L::kQT);
-            tc_commit(&s_full[st]);
-          }
-          __syncwarp();
-          // dP of tile it+2 reuses X[st] once the drain has read dQ^T of tile it (at
-          // once when dQ is left to the deterministic kernel: ds_full ended the reads).
-          if (!p.skip_dq) ok = wait(&dq_empty[st], par);
+          // Warp 3: dP^T of tile it+2 reuses X[st] once the drain has read dQ^T of tile
+          // it (at once when dQ is left to the deterministic kernel: ds_full ended the
+          // reads).  Warp 1: S^T of tile it+2 reuses S[st], whose P^T the dV above read.
+          if (!is_a && !p.skip_dq) ok = wait(&dq_empty[st], par);
           if (!ok) break;
           tc_fence_after();
           if (elect_one()) {
-            issue_kt<D, kBF16>(tmem + kColX + 64 * st, sV, sDO + qn * L::kQT);
-            tc_commit(&dp_full[st]);
+            if (is_a) {
+              issue_kt<D, kBF16>(tmem + kColS + 64 * st, sK, sQ + qn * L::kQT);
+              tc_commit(&s_full[st]);
+            } else {
+              issue_kt<D, kBF16>(tmem + kColX + 64 * st, sV, sDO + qn * L::kQT);
+              tc_commit(&dp_full[st]);
+            }
           }
           __syncwarp();
         }
       }
+      uint64_t* drain_bar = is_a ? mma_drain : mma_drain_b;
       if (elect_one()) {
         if (ok) tc_commit(dkv_full);
-        tc_commit(mma_drain);
+        tc_commit(drain_bar);
       }
       __syncwarp();
-      wait(mma_drain, 0);
+      wait(drain_bar, 0);
     }
     }
   } else if (warp < 12) {
@@ -571,8 +585,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     // 16*wq .. 16*wq+15 in lanes 0-15 of each 32-lane quadrant.
     const int d = (D == 128) ? (wq * 32 + lane) : (wq * 16 + lane);
     const bool d_valid = (D == 128) || (lane < 16);
-    const bool leader = (warp == 12 && lane == 0);
-    float* stage = reinterpret_cast<float*>(smem + L::kDQs);  // [64 queries][D]
     QTiles<kMask> cur = first;
     for (int it = 0; !p.skip_dq && cur.valid(); ++it, cur.advance()) {
       const int st = it & 1;
@@ -588,27 +600,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&dq_empty[st]);
-      // The previous tile's bulk reduction must have finished reading the staging tile.
-      if (leader) {
-        bulk_wait_read_all();
-        mbar_arrive(stage_free);
-      }
-      if (!__all_sync(0xffffffffu, mbar_wait(stage_free, it & 1, abort_flag))) break;
+      // Rows q0..q0+63 of head h are contiguous in the [B, Hq, Tq_pad, D] accumulator
+      // (rows past Tq land in the padding and are never read); for each query the warp's
+      // lanes add one contiguous run of D columns.
       if (d_valid) {
+        float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + q0) * D + d;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) stage[c * D + d] = __uint_as_float(v[c]);
-      }
-      fence_async_smem();
-      mbar_arrive(stage_full);
-      if (leader && mbar_wait(stage_full, it & 1, abort_flag)) {
-        // Rows q0..q0+63 of head h are contiguous in the [B, Hq, Tq_pad, D] accumulator
-        // (rows past Tq land in the padding and are never read).
-        float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + q0) * D;
-        bulk_reduce_add_f32(dst, stage, 64 * D * 4);
-        bulk_commit();
+        for (int c = 0; c < 64; ++c) red_add_f32(dst + c * D, __uint_as_float(v[c]));
       }
     }
-    if (leader) bulk_wait_all();
     tc_fence_before();
   }
 
