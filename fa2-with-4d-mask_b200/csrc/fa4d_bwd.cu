@@ -38,9 +38,15 @@ namespace fa4d {
 namespace {
 
 constexpr int kBwdThreads = 512;
-// Depth of the Q / dO / LSE / Delta ring: the load for query tile it+2 is issued
-// while tile it is still being consumed, which hides its L2/HBM latency.
-constexpr int kQStages = 3;
+// Depth of the Q / dO / LSE / Delta ring: the load for query tile it+Q-1 is issued
+// while tile it is still being consumed, which hides its L2/HBM latency.  The variants
+// without a mask or score take 4 stages (the Sᵀ issuer waited on the third stage's load
+// for ~1200 clocks per tile; config 2 backward main -5%, causal -3%), the others 3 (4
+// measured 2-3% slower there).  At 4 stages with D = 128 the layout leaves no room for
+// the 1 KB alignment slack: the kernel then relies on the dynamic shared memory base
+// being 1024-byte aligned (as it is on this hardware) and checks it.
+template <bool kMask, bool kScore>
+constexpr int kQStagesFor = (kMask || kScore) ? 3 : 4;
 // Register split (launch: 512 threads x 128 = 65536): producer/MMA warpgroup 88,
 // P/dS warpgroups 160, dQ drain 96 -> 128*88 + 256*160 + 128*96 = 64512 (no variant
 // spills; 152 / 112 left the P/dS code 16-32 bytes of spills).
@@ -48,7 +54,7 @@ constexpr uint32_t kRegsLaunch = 128, kRegsCtl = 88, kRegsSoftmax = 160, kRegsDr
 static_assert(128 * kRegsCtl + 256 * kRegsSoftmax + 128 * kRegsDrain <= kBwdThreads * kRegsLaunch,
               "register split exceeds the launch allocation");
 
-template <int D>
+template <int D, int kQStages>
 struct BwdLayout {
   static constexpr int kKV = 128 * D * 2;   // K or V tile (128 keys)
   static constexpr int kQT = 64 * D * 2;    // Q or dO tile (64 queries)
@@ -61,10 +67,12 @@ struct BwdLayout {
   static constexpr int kLSE = kDSb + 2 * kDS;            // kQStages x 64 floats
   static constexpr int kDelta = kLSE + kQStages * 256;   // kQStages x 64 floats
   static constexpr int kBar = kDelta + kQStages * 256;
-  static constexpr int kNumBars = 24;
+  static constexpr int kNumBars = 18 + 2 * kQStages;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
-  static constexpr int kAlloc = kBytes + 1024;
+  // Slack to align the base to 1024 B when it fits; without it the base must already be.
+  static constexpr int kSlack = kBytes + 1024 <= 232448 ? 1024 : 0;
+  static constexpr int kAlloc = kBytes + kSlack;
   static_assert(kAlloc <= 232448, "shared memory beyond the 227 KB per-block limit");
 };
 
@@ -111,8 +119,14 @@ __device__ __forceinline__ void issue_dq(uint32_t tD, uint32_t sK, uint32_t sDS)
 
 template <int D, bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_constant__ BwdParams p) {
-  using L = BwdLayout<D>;
+  constexpr int kQStages = kQStagesFor<kMask, kScore>;
+  using L = BwdLayout<D, kQStages>;
   extern __shared__ uint8_t smem_raw[];
+  if (L::kSlack == 0 && (smem_u32(smem_raw) & 1023u) != 0u) {
+    // No room to realign: report and leave before touching anything (uniform exit).
+    if (threadIdx.x == 0) atomicOr(p.status, FA4D_DEV_SMEM_ALIGN);
+    return;
+  }
   // 1024-B aligned base, derived by pointer arithmetic on the shared array so the
   // compiler keeps the shared address space (LDS/STS rather than generic loads/stores).
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -130,7 +144,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   uint64_t* dq_full = bars + 14;   // [2] dQ^T of the tile is in TMEM
   uint64_t* dq_empty = bars + 16;  // [2] drain has read dQ^T (128 arrivals)
   uint64_t* q_full = bars + 18;    // [kQStages]
-  uint64_t* q_empty = bars + 21;   // [kQStages] (2 arrivals: the last dV and the last dK reading the stage)
+  uint64_t* q_empty = bars + 18 + kQStages;  // [kQStages] (2 arrivals: the last dV and the last dK reading the stage)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -719,7 +733,7 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const ConvertParams p) 
 
 template <int D, bool kBF16, bool kMask, bool kScore>
 cudaError_t launch_bwd_t(const BwdParams& p, cudaStream_t s) {
-  using L = BwdLayout<D>;
+  using L = BwdLayout<D, kQStagesFor<kMask, kScore>>;
   auto kern = bwd_kernel<D, kBF16, kMask, kScore>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return e;

@@ -125,3 +125,84 @@ def max_over_ranks(value: float, dist=None, device: Optional[torch.device] = Non
     t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def max_units(B: int, Hk: int, world: int) -> int:
+    """The most units any rank holds (ranks pad to this for an equal-size gather)."""
+    return -(-(B * Hk) // world)
+
+
+def _unit_views(tensors: Sequence[torch.Tensor], kv_heads: Sequence[bool], G: int, b: int, hk: int, hd: int):
+    for t, kv in zip(tensors, kv_heads):
+        h0, h1 = (hk, hk + 1) if kv else (hk * G, (hk + 1) * G)
+        yield _slice(t, b, h0, h1, hd)
+
+
+def pack_units(
+    tensors: Sequence[torch.Tensor],
+    kv_heads: Sequence[bool],
+    B: int,
+    Hq: int,
+    Hk: int,
+    rank: int,
+    world: int,
+    layout: str = "bhsd",
+) -> torch.Tensor:
+    """One flat buffer holding, unit by unit, the rank's pieces of full-size result
+    tensors (each tensor's query heads of the unit, or its KV head where `kv_heads`),
+    padded with zeros to max_units units so that every rank sends the same number of
+    elements to an all-gather."""
+    G = Hq // Hk
+    hd = _head_dim(layout)
+    start, stop = unit_range(B, Hk, rank, world)
+    pieces = []
+    for u in range(start, stop):
+        b, hk = divmod(u, Hk)
+        pieces.extend(v.reshape(-1) for v in _unit_views(tensors, kv_heads, G, b, hk, hd))
+    per_unit = sum(t[0:1].numel() // t.shape[hd] * (1 if kv else G) for t, kv in zip(tensors, kv_heads))
+    pad = (max_units(B, Hk, world) - (stop - start)) * per_unit
+    ref = tensors[0]
+    if pad:
+        pieces.append(torch.zeros(pad, dtype=ref.dtype, device=ref.device))
+    return torch.cat(pieces) if pieces else torch.zeros(0, dtype=ref.dtype, device=ref.device)
+
+
+def unpack_units(
+    gathered: torch.Tensor,
+    tensors: Sequence[torch.Tensor],
+    kv_heads: Sequence[bool],
+    B: int,
+    Hq: int,
+    Hk: int,
+    world: int,
+    layout: str = "bhsd",
+) -> None:
+    """Inverse of pack_units over all ranks: `gathered` is the concatenation of every
+    rank's buffer (rank order); each unit's pieces are written into `tensors`."""
+    G = Hq // Hk
+    hd = _head_dim(layout)
+    per_rank = gathered.numel() // world
+    for r in range(world):
+        off = r * per_rank
+        start, stop = unit_range(B, Hk, r, world)
+        for u in range(start, stop):
+            b, hk = divmod(u, Hk)
+            for v in _unit_views(tensors, kv_heads, G, b, hk, hd):
+                n = v.numel()
+                v.copy_(gathered[off : off + n].view(v.shape))
+                off += n
+
+
+def gather_units(dist, tensors, kv_heads, B: int, Hq: int, Hk: int, layout: str = "bhsd") -> None:
+    """All ranks exchange their units of `tensors` (full-size on every rank, each rank
+    having filled its own units) so that every rank ends with all of them."""
+    world, rank = dist.get_world_size(), dist.get_rank()
+    mine = pack_units(tensors, kv_heads, B, Hq, Hk, rank, world, layout)
+    if hasattr(dist, "all_gather_into_tensor") and mine.is_cuda:
+        out = torch.empty(world * mine.numel(), dtype=mine.dtype, device=mine.device)
+        dist.all_gather_into_tensor(out, mine)
+    else:
+        chunks = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(chunks, mine)
+        out = torch.cat(chunks)
+    unpack_units(out, tensors, kv_heads, B, Hq, Hk, world, layout)

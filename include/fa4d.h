@@ -259,6 +259,9 @@ const char* fa4d_last_error(void);
 #define FA4D_DEV_TIMEOUT_FWD 1
 #define FA4D_DEV_TIMEOUT_BWD 2
 #define FA4D_DEV_TIMEOUT_CHECK 4
+/* A kernel whose shared-memory layout leaves no alignment slack found its dynamic shared
+ * memory base not 1024-byte aligned and returned without computing (not seen on B200). */
+#define FA4D_DEV_SMEM_ALIGN 8
 int fa4d_device_status(int device, void* stream, int clear);
 
 /* Diagnostic (no counterpart in the reference): runs the kernels' bounded mbarrier

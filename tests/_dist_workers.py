@@ -61,3 +61,27 @@ def rank_dies(rank, world, port, out_q):
         out_q.put(("no error", None))
     except Exception as e:
         out_q.put(("error", type(e).__name__))
+
+
+def gathered_units(rank, world, port, shape, out_q):
+    """Each rank fills only its own units of full-size result tensors (the others stay
+    NaN), then gather_units exchanges them; rank 0 reports what it ends with."""
+    try:
+        _init(rank, world, port, 60)
+        B, T, Hq, Hk, D = shape
+        g = torch.Generator().manual_seed(80)
+        ref = [torch.randn(B, T, Hq, D, generator=g), torch.randn(B, T, Hk, D, generator=g)]
+        kv = [False, True]
+        local = [torch.full_like(t, float("nan")) for t in ref]
+        G = Hq // Hk
+        for seg in shard.segments(B, Hk, rank, world):
+            for dst, src, is_kv in zip(local, ref, kv):
+                h0, h1 = (seg.hk0, seg.hk1) if is_kv else (seg.hk0 * G, seg.hk1 * G)
+                dst[seg.b : seg.b + 1, :, h0:h1].copy_(src[seg.b : seg.b + 1, :, h0:h1])
+        shard.gather_units(dist, local, kv, B, Hq, Hk, layout="bshd")
+        if rank == 0:
+            out_q.put(("ok", all(torch.equal(a, b) for a, b in zip(local, ref)), None))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        out_q.put(("error", f"rank {rank}: {type(e).__name__}: {e}", None))

@@ -90,3 +90,24 @@ def test_a_dead_rank_makes_the_next_collective_fail_not_hang():
     res = _run(W.rank_dies, 2, timeout=90)
     assert res, "the surviving rank reported nothing"
     assert res[0][0] == "error", res
+
+
+@pytest.mark.parametrize("shape,world", [((1, 6, 8, 4, 3), 2), ((3, 5, 6, 1, 2), 2), ((2, 4, 6, 3, 2), 3)])
+def test_units_gathered_over_ranks_rebuild_the_full_results(shape, world):
+    """The verification gather of the strong-scaling benchmark: each rank packs its
+    units (uneven counts are padded), all ranks all-gather, every unit lands back."""
+    res = _run(W.gathered_units, world, shape)
+    assert res and res[0][0] == "ok", res
+    assert res[0][1] is True
+
+
+@pytest.mark.parametrize("B,Hq,Hk,world", [(1, 32, 8, 8), (16, 64, 1, 8), (3, 6, 3, 4), (2, 4, 1, 3)])
+def test_unit_packing_round_trip(B, Hq, Hk, world):
+    T, D = 3, 4
+    full = [torch.randn(B, T, Hq, D), torch.randn(B, T, Hq, D), torch.randn(B, T, Hk, D)]
+    kv = [False, False, True]
+    bufs = [shard.pack_units(full, kv, B, Hq, Hk, r, world, "bshd") for r in range(world)]
+    assert len({b.numel() for b in bufs}) == 1
+    out = [torch.zeros_like(t) for t in full]
+    shard.unpack_units(torch.cat(bufs), out, kv, B, Hq, Hk, world, "bshd")
+    assert all(torch.equal(a, b) for a, b in zip(out, full))
