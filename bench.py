@@ -136,6 +136,33 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+# --------------------------------------------------------------------------- NUMA placement
+def numa_bind(device: torch.device) -> dict:
+    """Runs this process on the CPUs of the GPU's NUMA node, so that its pinned host
+    buffers (allocated afterwards, first touch) sit next to the GPU's PCIe root."""
+    props = torch.cuda.get_device_properties(device)
+    bus = getattr(props, "pci_bus_id", None)
+    dom = getattr(props, "pci_domain_id", 0) or 0
+    dev_id = getattr(props, "pci_device_id", 0) or 0
+    if bus is None:
+        return {"applied": False, "why": "no PCI id"}
+    try:
+        node = int(Path(f"/sys/bus/pci/devices/{dom:04x}:{bus:02x}:{dev_id:02x}.0/numa_node").read_text())
+        if node < 0:
+            return {"applied": False, "why": "no NUMA node reported"}
+        cpus = set()
+        for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip().split(","):
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return {"applied": False, "node": node, "why": "no allowed CPU on the node"}
+        os.sched_setaffinity(0, cpus)
+        return {"applied": True, "node": node, "cpus": len(cpus)}
+    except (OSError, ValueError) as e:
+        return {"applied": False, "why": f"{type(e).__name__}"}
+
+
 # --------------------------------------------------------------------------- our arm
 def run_ours(args):
     from fa2_with_4d_mask_b200 import _lib  # noqa: E402  (registered by the import below)
@@ -153,6 +180,7 @@ def _run_ours(args, _lib):
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    numa = numa_bind(dev)
     dist = None
     if world > 1:
         import torch.distributed as dist
@@ -274,6 +302,8 @@ def _run_ours(args, _lib):
     status = _lib.device_status(dev)
     # End-to-end leg on every rank (each rank its own host batch element), max over ranks.
     e2e = run_e2e(api, dev, args, dist, world) if args.e2e_steps > 0 else None
+    copies = copy_leg(dev, dist, world) if args.e2e_steps > 0 else None
+    strong = strong_leg(_lib, dev, dist, world, rank, min(args.steps, 20), args.warmup) if args.strong else None
 
     if rank != 0:
         if dist:
@@ -354,6 +384,11 @@ def _run_ours(args, _lib):
         line["extra"]["library_context_cfg2"] = library_context(dev, peaks)
     if e2e is not None:
         line["e2e"] = e2e
+    if copies is not None:
+        line["host_copies"] = copies
+    line["numa"] = numa
+    if strong is not None:
+        line["strong_scaling"] = strong
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args)
     if dist:
@@ -673,6 +708,156 @@ def run_context(args):
     return line
 
 
+# Global problems of the strong-scaling leg: (name, B, Tq, Tk, Hq, Hk, D, causal mode).
+STRONG = (
+    ("cfg2", 1, 8192, 8192, 32, 8, 128, "none"),
+    ("cfg5", 16, 1024, 4096, 64, 1, 64, "bottom_right"),
+)
+
+
+def _launch_slices(segs, Hk):
+    """The rank's segments as launches: consecutive whole batch elements (every KV
+    head) merge into one batch range; a partial element is its own launch.
+    Returns (b0, b1, hk0, hk1) tuples."""
+    out = []
+    for s in segs:
+        whole = s.hk0 == 0 and s.hk1 == Hk
+        if whole and out and out[-1][2] == 0 and out[-1][3] == Hk and out[-1][1] == s.b:
+            out[-1] = (out[-1][0], s.b + 1, 0, Hk)
+        else:
+            out.append((s.b, s.b + 1, s.hk0, s.hk1))
+    return out
+
+
+def strong_leg(_lib, dev, dist, world, rank, steps, warmup):
+    """Fixed global problems split over the ranks by (batch, KV head) units, no exchange
+    on the data path.  Each rank times its share (graph replays of fwd + bwd over its
+    launches, L2 flushed, median), the step is the max over ranks; rank 0 also times the
+    whole problem alone.  Outside the timed region every rank's O, dQ, dK, dV units are
+    all-gathered and compared on rank 0 with its single-GPU result."""
+    from fa2_with_4d_mask_b200 import shard
+
+    modes = {"none": _lib.CAUSAL_NONE, "bottom_right": _lib.CAUSAL_BOTTOM_RIGHT}
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+    for name, B_, Tq, Tk, Hq, Hk, D_, cm in STRONG:
+        mode = modes[cm]
+        G = Hq // Hk
+        g = torch.Generator(device=dev)
+        g.manual_seed(4242)
+        mk = lambda t, h: torch.randn((B_, t, h, D_), generator=g, device=dev).to(torch.bfloat16)
+        q, k, v, do = mk(Tq, Hq), mk(Tk, Hk), mk(Tk, Hk), mk(Tq, Hq)  # [B, T, H, D] storage
+        sc = D_ ** -0.5
+
+        def views_of(slices):
+            return [(b0, hk0, hk1, q[b0:b1, :, hk0 * G:hk1 * G], k[b0:b1, :, hk0:hk1], v[b0:b1, :, hk0:hk1],
+                     do[b0:b1, :, hk0 * G:hk1 * G]) for b0, b1, hk0, hk1 in slices]
+
+        def step(views):
+            outs = []
+            for _, _, _, qs, ks, vs, ds in views:
+                o, lse = _lib.forward(qs, ks, vs, None, None, sc, mode)
+                outs.append((o, *_lib.backward(ds, qs, ks, vs, o, lse, None, None, sc, mode)))
+            return outs
+
+        def timed(views):
+            for _ in range(warmup):
+                step(views)
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step(views)
+            for _ in range(warmup):
+                graph.replay()
+            torch.cuda.synchronize(dev)
+            evs = []
+            for _ in range(steps):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                graph.replay()
+                b.record(stream)
+                evs.append((a, b))
+            torch.cuda.synchronize(dev)
+            del graph
+            return median_ms(evs)
+
+        mine = views_of(_launch_slices(shard.segments(B_, Hk, rank, world), Hk))
+        if dist:
+            dist.barrier()
+        t_n = shard.max_over_ranks(timed(mine), dist, dev)
+        # Verification, outside the timed region.
+        nan = float("nan")
+        full = [torch.full((B_, Tq, Hq, D_), nan, dtype=torch.bfloat16, device=dev),
+                torch.full((B_, Tq, Hq, D_), nan, dtype=torch.bfloat16, device=dev),
+                torch.full((B_, Tk, Hk, D_), nan, dtype=torch.bfloat16, device=dev),
+                torch.full((B_, Tk, Hk, D_), nan, dtype=torch.bfloat16, device=dev)]
+        for (b0, hk0, hk1, *_), outs in zip(mine, step(mine)):
+            for dst, src, kv in zip(full, outs, (False, False, True, True)):
+                h0, h1 = (hk0, hk1) if kv else (hk0 * G, hk1 * G)
+                dst[b0:b0 + src.shape[0], :, h0:h1].copy_(src)
+        if dist:
+            shard.gather_units(dist, full, (False, False, True, True), B_, Hq, Hk, layout="bshd")
+        entry = None
+        if rank == 0:
+            whole = views_of([(0, B_, 0, Hk)])
+            t_1 = timed(whole)
+            ref = step(whole)[0]
+            rel = lambda a, r: float((a.float() - r.float()).norm() / r.float().norm())
+            flops = fwd_bwd_flops(B_, Hq, Tq, Tk, D_, cm != "none")
+            entry = {
+                "global": f"B{B_} Tq{Tq} Tk{Tk} Hq{Hq} Hk{Hk} D{D_} bf16 causal={cm}",
+                "units": B_ * Hk, "ranks": world, "ms": round(t_n, 4), "ms_1gpu": round(t_1, 4),
+                "tflops": round(flops / t_n / 1e9, 1), "tflops_1gpu": round(flops / t_1 / 1e9, 1),
+                "speedup": round(t_1 / t_n, 3), "efficiency": round(t_1 / (world * t_n), 4),
+                "verified": {
+                    "all_finite": bool(all(torch.isfinite(t.float()).all() for t in full)),
+                    "o_bitwise_equal": bool(torch.equal(full[0], ref[0])),
+                    "dq_rel": rel(full[1], ref[1]), "dk_rel": rel(full[2], ref[2]), "dv_rel": rel(full[3], ref[3]),
+                    "how": "NCCL all_gather_into_tensor of every rank's O, dQ, dK, dV units, compared with the "
+                           "whole problem run on rank 0",
+                },
+            }
+            entry["verified"]["ok"] = (entry["verified"]["all_finite"] and entry["verified"]["o_bitwise_equal"]
+                                       and max(entry["verified"][k2] for k2 in ("dq_rel", "dk_rel", "dv_rel")) < 1e-2)
+        if dist:
+            dist.barrier()
+        del q, k, v, do, full
+        if entry is not None:
+            res[name] = entry
+    return res if rank == 0 else None
+
+
+def copy_leg(dev, dist, world, reps=5):
+    """Host<->device bandwidth alone: each rank copies one e2e step's inputs (q, k, v,
+    dO) from pinned host memory and its outputs (O, dQ, dK, dV) back, all ranks at
+    once, timed with CUDA events (median of `reps`, max over ranks)."""
+    from fa2_with_4d_mask_b200 import shard
+
+    n_in = 2 * B * T * D * (2 * HQ + 2 * HK)
+    h = torch.empty(n_in, dtype=torch.uint8).pin_memory()
+    d = torch.empty(n_in, dtype=torch.uint8, device=dev)
+    out = {}
+    for name, dst, src in (("h2d", d, h), ("d2h", h, d)):
+        dst.copy_(src, non_blocking=True)
+        torch.cuda.synchronize(dev)
+        evs = []
+        for _ in range(reps):
+            if dist:
+                dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            dst.copy_(src, non_blocking=True)
+            b.record()
+            torch.cuda.synchronize(dev)
+            evs.append((a, b))
+        ms = shard.max_over_ranks(median_ms(evs), dist, dev)
+        out[name] = {"bytes_per_rank": n_in, "ms": round(ms, 4), "gbs_per_rank": round(n_in / ms / 1e6, 1),
+                     "gbs_all_ranks": round(world * n_in / ms / 1e6, 1)}
+    return out
+
+
 def run_e2e(api, dev, args, dist=None, world=1):
     """Same metric through the public API with pinned host buffers, as a training input
     pipeline runs it: every step uploads its q/k/v/dO host->device, runs forward +
@@ -828,6 +1013,8 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-extra", dest="extra", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-strong", dest="strong", action="store_false",
+                    help="skip the strong-scaling leg (fixed global problems split over the ranks)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

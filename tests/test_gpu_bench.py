@@ -42,6 +42,12 @@ def test_bench_line_contract():
     # when the group split is on.
     assert line["gpu_launches"] in (4 * 3, 5 * 3)
     assert "sm_mhz" in line["clocks"] or "error" in line["clocks"]
+    # Strong scaling on one GPU: the sharded run is the whole problem; the gathered
+    # results match the single-GPU run.
+    for name in ("cfg2", "cfg5"):
+        st = line["strong_scaling"][name]
+        assert st["ranks"] == 1 and st["ms"] > 0 and st["verified"]["ok"], st
+    assert line["host_copies"]["h2d"]["gbs_per_rank"] > 0 and line["host_copies"]["d2h"]["gbs_per_rank"] > 0
     # The causal leg is measured like the headline and reports its own fractions.
     c = line["causal"]
     assert c["fwd_ms"] > 0 and c["fwd_bwd_ms"] > c["fwd_ms"]
