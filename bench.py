@@ -46,8 +46,8 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) per launch of the backward main kernel at this workload,
 # dram__bytes_read.sum + dram__bytes_write.sum from one ncu capture of this bench
 # command, and the commit of the kernel code that capture measured.
-NCU_BWD_MAIN_TRAFFIC = 536891648
-NCU_BWD_MAIN_TRAFFIC_CODE = "1114cec"
+NCU_BWD_MAIN_TRAFFIC = 545651712
+NCU_BWD_MAIN_TRAFFIC_CODE = "369d887"
 L2_FLUSH_BYTES = 256 << 20
 
 
