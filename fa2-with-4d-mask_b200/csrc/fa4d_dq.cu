@@ -9,11 +9,16 @@
 // input dtype.  The result is bit-reproducible.  The main kernel then skips its dQ
 // products (BwdParams::skip_dq).
 //
-// CTA = 128 query rows, 256 threads: warp 0 TMA (Q, dO, LSE, Delta once; K/V rings),
-// warp 1 MMA issue, warp 2 TMEM allocation, warps 4-7 one thread per query row.
-// TMEM: S [0,128) (dS^T... dS as 16-bit overwrites its first 64 columns), dP
-// [128,256), dQ [256,256+D).  Per key tile: S, dP (N = 128 keys), then dQ += dS K
-// (A = dS from TMEM, B = K, MN-major).
+// CTA = 128 query rows, 384 threads: warp 0 TMA (Q, dO, LSE, Delta once; K/V rings),
+// warp 1 MMA issue, warp 2 TMEM allocation, warps 4-7 and 8-11 two warpgroups that
+// share each key tile: one thread per query row, warpgroup w on keys [64w, 64w + 64)
+// (P and dS are elementwise once LSE is known, so the halves need no exchange).
+// TMEM: S x2 [0,256) (a tile's dS as 16-bit overwrites columns [0,32) and [64,96) of
+// its S buffer), dP [256,384), dQ [384,384+D).  Per key tile u the MMA warp waits for
+// dS(u), then issues dP(u+1) (the dP buffer is free once dS(u) is formed), dQ += dS(u)
+// K(u) (A = dS from TMEM, B = K, MN-major) and S(u+2) into the S buffer dQ(u) has just
+// read; S(u+1) was issued a tile earlier, so the warpgroups start P(u+1) at once and
+// dQ(u) runs under the next dS.
 #include <cfloat>
 
 #include "fa4d.h"
@@ -25,7 +30,7 @@ namespace fa4d {
 
 namespace {
 
-constexpr int kDqThreads = 256;
+constexpr int kDqThreads = 384;
 
 template <int D>
 struct DqLayout {
@@ -37,7 +42,7 @@ struct DqLayout {
   static constexpr int kLSE = kV + 2 * kTile;
   static constexpr int kDelta = kLSE + 512;
   static constexpr int kBar = kDelta + 512;
-  static constexpr int kNumBars = 12;
+  static constexpr int kNumBars = 14;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -55,13 +60,15 @@ __device__ __forceinline__ void issue_abt(uint32_t tD, uint32_t sA, uint32_t sB)
   }
 }
 
-// dQ (+)= dS K : M=128 queries, N=D, K=128 keys; dS from TMEM, K MN-major.
+// dQ (+)= dS K : M=128 queries, N=D, K=128 keys; dS from TMEM (keys 0-63 at columns
+// [0,32) of the S buffer, keys 64-127 at [64,96)), K MN-major.
 template <int D, bool kBF16>
 __device__ __forceinline__ void issue_dsk(uint32_t tDQ, uint32_t tDS, uint32_t sK, bool accumulate) {
   constexpr uint32_t idesc = make_idesc(128, D, kBF16, false, true);
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
-    mma_ts(tDQ, tDS + kk * 8, sw128_desc(sK + kk * 2048, 16384, 1024), idesc, (accumulate || kk > 0) ? 1u : 0u);
+    mma_ts(tDQ, tDS + (kk >> 2) * 64 + (kk & 3) * 8, sw128_desc(sK + kk * 2048, 16384, 1024), idesc,
+           (accumulate || kk > 0) ? 1u : 0u);
 }
 
 template <int D, bool kBF16, bool kMask, bool kScore>
@@ -75,9 +82,10 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
   uint64_t* k_empty = bars + 3;  // [2]
   uint64_t* v_full = bars + 5;   // [2]
   uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // S and dP of the current tile are in TMEM
-  uint64_t* ds_full = bars + 10; // dS written to TMEM (128 arrivals)
-  uint64_t* mma_drain = bars + 11;
+  uint64_t* s_full = bars + 9;   // [2] S of a tile is in S buffer u & 1
+  uint64_t* dp_full = bars + 11; // dP of the current tile is in TMEM
+  uint64_t* ds_full = bars + 12; // dS written to TMEM, dP read (256 arrivals)
+  uint64_t* mma_drain = bars + 13;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -106,8 +114,10 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(ds_full, 128);
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(dp_full, 1);
+    mbar_init(ds_full, 256);
     mbar_init(mma_drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -120,7 +130,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256;
+  constexpr uint32_t kColS = 0, kColDP = 256, kColDQ = 384;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -169,8 +179,6 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Per tile u: dQ of tile u-1 (it reads dS from the S columns, so it goes before
-    // this tile's S), then S and dP of tile u.
     if (any_work) {
       const uint32_t sQ = smem_u32(smem + L::kQ);
       const uint32_t sDO = smem_u32(smem + L::kDO);
@@ -179,37 +187,63 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
       auto wait = [&](uint64_t* bar, uint32_t parity) {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
       };
-      bool ok = wait(q_full, 0);
+      // Tiles u = 0, 1, ... are the visited key tiles in order (K/V stage u & 1).
+      const int k1 = tl.next(kt_first + 1);
+      bool ok = wait(q_full, 0) && wait(&k_full[0], 0) && wait(&v_full[0], 0);
+      if (ok) {
+        tc_fence_after();
+        if (elect_one()) {
+          issue_abt<D, kBF16>(tmem + kColS, sQ, sK);
+          tc_commit(&s_full[0]);
+          issue_abt<D, kBF16>(tmem + kColDP, sDO, sV);
+          tc_commit(dp_full);
+          tc_commit(&v_empty[0]);
+        }
+        __syncwarp();
+      }
+      if (ok && k1 < tl.n) {
+        ok = wait(&k_full[1], 0);
+        if (ok) {
+          tc_fence_after();
+          if (elect_one()) {
+            issue_abt<D, kBF16>(tmem + kColS + 128, sQ, sK + L::kTile);
+            tc_commit(&s_full[1]);
+          }
+          __syncwarp();
+        }
+      }
       int u = 0;
-      for (int kt = kt_first; ok && kt < tl.n; kt = tl.next(kt + 1), ++u) {
+      int kt_a = k1;                  // tile u + 1
+      int kt_b = k1 < tl.n ? tl.next(k1 + 1) : tl.n;  // tile u + 2
+      for (int kt = kt_first; ok && kt < tl.n; kt = kt_a, kt_a = kt_b, kt_b = kt_b < tl.n ? tl.next(kt_b + 1) : tl.n, ++u) {
         const int s = u & 1;
-        const uint32_t par = (u >> 1) & 1;
-        ok = wait(&k_full[s], par) && wait(&v_full[s], par);
+        ok = wait(ds_full, u & 1);
         if (!ok) break;
-        if (u > 0) {
-          ok = wait(ds_full, (u - 1) & 1);
+        const bool has1 = kt_a < tl.n, has2 = kt_b < tl.n;
+        if (has1) {
+          ok = wait(&v_full[s ^ 1], ((u + 1) >> 1) & 1);
           if (!ok) break;
         }
         tc_fence_after();
         if (elect_one()) {
-          if (u > 0) {
-            issue_dsk<D, kBF16>(tmem + kColDQ, tmem + kColS, sK + (s ^ 1) * L::kTile, u > 1);
-            tc_commit(&k_empty[s ^ 1]);
+          if (has1) {
+            // dP of tile u+1: the warpgroups have read dP(u) (ds_full).
+            issue_abt<D, kBF16>(tmem + kColDP, sDO, sV + (s ^ 1) * L::kTile);
+            tc_commit(dp_full);
+            tc_commit(&v_empty[s ^ 1]);
           }
-          issue_abt<D, kBF16>(tmem + kColS, sQ, sK + s * L::kTile);
-          issue_abt<D, kBF16>(tmem + kColDP, sDO, sV + s * L::kTile);
-          tc_commit(&v_empty[s]);
-          tc_commit(s_full);
+          issue_dsk<D, kBF16>(tmem + kColDQ, tmem + kColS + 128 * s, sK + s * L::kTile, u > 0);
+          tc_commit(&k_empty[s]);
         }
         __syncwarp();
-      }
-      if (ok && u > 0) {
-        ok = wait(ds_full, (u - 1) & 1);
-        if (ok) {
+        if (has2) {
+          // S of tile u+2 into the buffer whose dS the dQ above read (issued in order).
+          ok = wait(&k_full[s], ((u + 2) >> 1) & 1);
+          if (!ok) break;
           tc_fence_after();
           if (elect_one()) {
-            issue_dsk<D, kBF16>(tmem + kColDQ, tmem + kColS, sK + ((u - 1) & 1) * L::kTile, u > 1);
-            tc_commit(&k_empty[(u - 1) & 1]);
+            issue_abt<D, kBF16>(tmem + kColS + 128 * s, sQ, sK + s * L::kTile);
+            tc_commit(&s_full[s]);
           }
           __syncwarp();
         }
@@ -221,13 +255,14 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ dS and epilogue
-    const int row = (warp - 4) * 32 + lane;
+    const int wg = (warp - 4) >> 2;  // keys [64 wg, 64 wg + 64) of every tile
+    const int row = (warp & 3) * 32 + lane;
     const int q = q0 + row;
     const bool q_valid = q < p.Tq;
     const int64_t qc = min(q, p.Tq - 1);
-    const uint32_t lane_base = static_cast<uint32_t>((warp - 4) * 32) << 16;
-    const uint32_t tS = tmem + lane_base + kColS;
-    const uint32_t tDP = tmem + lane_base + kColDP;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS0 = tmem + lane_base + kColS + 64 * wg;
+    const uint32_t tDP = tmem + lane_base + kColDP + 64 * wg;
     const float* score_row = nullptr;
     const uint8_t* mask_row = nullptr;
     const uint4* bits_row = nullptr;
@@ -261,14 +296,17 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
 #pragma unroll
         for (int c = 0; c < 4; ++c) mw[c] &= low_bits(key_lim - (kbase + 32 * c));
       }
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full, u & 1, abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[u & 1], (u >> 1) & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
+      const uint32_t tS = tS0 + 128 * (u & 1);
+      // P for this warpgroup's 64 keys (kept in registers), then dS once dP is in.
+      float pr[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dpv[32];
-        tmem_ld32(tS + 32 * c, sv);
-        tmem_ld32(tDP + 32 * c, dpv);
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * wg + cc;
+        uint32_t sv[32];
+        tmem_ld32(tS + 32 * cc, sv);
         tmem_wait_ld();
         const int kc = kbase + 32 * c;
         float add[32];
@@ -287,24 +325,31 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
             for (int e = 0; e < 32; ++e) add[e] = (kc + e < p.Tk) ? __ldg(score_row + kc + e) : 0.f;
           }
         }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = __uint_as_float(sv[i]);
+          if constexpr (kScore) x += add[i];
+          const float e = ex2(fmaf(x, p.scale_log2, -lse));
+          pr[32 * cc + i] = ((mw[c] >> i) & 1u) ? e : 0.f;
+        }
+      }
+      ok = __all_sync(0xffffffffu, mbar_wait(dp_full, u & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t dpv[32];
+        tmem_ld32(tDP + 32 * cc, dpv);
+        tmem_wait_ld();
         uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float ds2[2];
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int i = 2 * e + j;
-            float x = __uint_as_float(sv[i]);
-            if constexpr (kScore) x += add[i];
-            const float pr = ex2(fmaf(x, p.scale_log2, -lse));
-            // dS without the softmax scale (applied to dQ at the end).
-            ds2[j] = ((mw[c] >> i) & 1u) ? pr * (__uint_as_float(dpv[i]) - delta) : 0.f;
-          }
-          pk[e] = pack2<kBF16>(ds2[0], ds2[1]);
-        }
-        // dS (16-bit) for keys 32c..32c+31 goes to columns 16c..16c+15, which hold S
-        // values already read.
-        tmem_st16(tS + 16 * c, pk);
+        for (int e = 0; e < 16; ++e)
+          // dS without the softmax scale (applied to dQ at the end).
+          pk[e] = pack2<kBF16>(pr[32 * cc + 2 * e] * (__uint_as_float(dpv[2 * e]) - delta),
+                               pr[32 * cc + 2 * e + 1] * (__uint_as_float(dpv[2 * e + 1]) - delta));
+        // dS (16-bit) for this warpgroup's keys 32cc..32cc+31 goes to columns
+        // 16cc..16cc+15 of its half of the S buffer, which hold S values already read.
+        tmem_st16(tS + 16 * cc, pk);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -318,7 +363,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
       ok = __all_sync(0xffffffffu, mbar_wait(mma_drain, 0, abort_flag));
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = wg * (D / 64); c < (wg + 1) * (D / 64); ++c) {
         uint32_t v[32];
         tmem_ld32(tmem + lane_base + kColDQ + 32 * c, v);
         tmem_wait_ld();
@@ -334,7 +379,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_kernel(const __grid_constant
       }
     } else if (q_valid) {
 #pragma unroll
-      for (int w = 0; w < D / 8; ++w)
+      for (int w = wg * (D / 16); w < (wg + 1) * (D / 16); ++w)
         if (8 * w < p.d_out) reinterpret_cast<uint4*>(dst)[w] = make_uint4(0u, 0u, 0u, 0u);
     }
     tc_fence_before();
