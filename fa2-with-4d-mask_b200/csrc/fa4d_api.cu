@@ -274,7 +274,7 @@ KeyTileWork key_tile_work(int Tq, int Tk, int causal) {
 int group_split(int B, int Tq, int Tk, int Hq, int Hk, int D, int causal) {
   const int G = Hq / Hk;
   const int nkb = (Tk + 127) / 128;
-  // At D = 256 a CTA pair shares each key tile (one per half of the output columns).
+  // At D = 256 a cluster of two CTAs shares each key tile (one per half of the products).
   const double base = static_cast<double>(nkb) * Hk * B * (D == 256 ? 2 : 1);
   const double sms = sm_count();
   const double tile_us = D == 256 ? 2.0 : (D > 64 ? 1.5 : 0.9);

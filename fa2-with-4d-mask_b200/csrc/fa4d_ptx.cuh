@@ -82,6 +82,84 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* a
   }
 }
 
+// ------------------------------------------------------------------ 2-CTA clusters
+// The D = 256 backward runs each key tile on a cluster of two CTAs: one stores rows
+// into the other's shared memory with st.async (completion counted in bytes on the
+// receiver's mbarrier), the receiver hands the buffer back with a remote arrival.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The same shared-memory offset in CTA `rank` of this cluster (a shared::cluster address).
+__device__ __forceinline__ uint32_t peer_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+// Every thread of every CTA of the cluster: release this thread's earlier memory
+// accesses at cluster scope, wait for all the others, acquire theirs.  The barrier is
+// a warp-aligned instruction, so the warp is reconverged first.
+__device__ __forceinline__ void cluster_sync() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 16 bytes into shared memory of a CTA of this cluster; the bytes are counted on that
+// CTA's mbarrier `bar` (both shared::cluster addresses) when they have landed.
+__device__ __forceinline__ void st_async_v4(uint32_t addr, uint4 v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   addr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(bar)
+               : "memory");
+}
+// `bytes` of this CTA's shared memory (16-B aligned, multiple of 16) into shared memory
+// of a CTA of this cluster, counted on that CTA's mbarrier `bar` (dst and bar are
+// shared::cluster addresses) when they have landed.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+// Arrival without data on an mbarrier of a CTA of this cluster (a pure signal).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+// try_wait with cluster-scope acquire, for phases completed from the peer CTA.
+__device__ __forceinline__ uint32_t mbar_try_wait_cl(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done;
+}
+// mbar_wait (below) for phases completed from the peer CTA: same bound and abort flag.
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity, int* abort_flag) {
+  if (mbar_try_wait_cl(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait_cl(bar, parity)) return true;
+    if ((n & 15u) == 0u) {
+      if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
+      if (clock64() - t0 > kWaitLimitCycles) {
+        *reinterpret_cast<volatile int*>(abort_flag) = 1;
+        return false;
+      }
+    }
+  }
+}
+// Abort-path wait with cluster-scope acquire: gives up after a short bound.
+__device__ __forceinline__ void mbar_wait_short_cl(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait_cl(bar, parity)) {
+    if (clock64() - t0 > kWaitLimitCycles / 8) return;
+  }
+}
+
 // Abort-path wait for copies still in flight: gives up after a short bound.
 __device__ __forceinline__ void mbar_wait_short(uint64_t* bar, uint32_t parity) {
   const long long t0 = clock64();

@@ -7,10 +7,11 @@ document ids, the split-group and deterministic backward, fp16, BSHD with bottom
 causal), plus a direct check that nothing is written past column 96 of each output row.
 
 D = 256 runs its own kernels: the forward with one 128-row query slot per CTA, the
-backward with a CTA pair per key tile, each CTA owning half of the dK / dV / dQ
-columns, and the deterministic dQ pass walking each key tile in two 64-key halves.
-The same variants are covered; the deterministic backward is also checked to repeat
-bit for bit.
+backward with a cluster of two CTAs per key tile (one computing S^T, P and dV, the
+other dP^T, dS and dK, P crossing through distributed shared memory), and the dQ pass
+(used in both backward modes at this head dim) walking each key tile in two 64-key
+halves.  The same variants are covered; the deterministic backward is also checked to
+repeat bit for bit.
 """
 
 from __future__ import annotations
