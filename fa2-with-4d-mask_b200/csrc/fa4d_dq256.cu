@@ -9,11 +9,15 @@
 // tile is walked as two 64-key halves: K in a 2-stage ring of 32 KB halves, V in one
 // 32 KB stage (free again as soon as dP of its half is done).
 //
-// CTA = 128 query rows, 256 threads: warp 0 TMA, warp 1 MMA issue, warp 2 TMEM
-// allocation, warps 4-7 one thread per query row.
-// TMEM: S [0,64) (dS as 16-bit overwrites its first 32 columns), dP [64,128),
-// dQ [128,384).  Per 64-key half: dQ += dS K of the previous half (A = dS from TMEM,
-// B = K MN-major, N = 256), then S and dP (N = 64, K = 256) of this half.
+// CTA = 128 query rows, 384 threads: warp 0 TMA (Q, dO, LSE, Delta, K halves), warp 1
+// MMA issue, warp 2 TMEM allocation, warp 3 TMA (V halves), warps 4-7 and 8-11 one
+// thread per query row, warpgroup wg taking keys 32 wg .. 32 wg + 31 of every half
+// and dQ columns 128 wg .. 128 wg + 127 in the epilogue.
+// TMEM: S x2 [0,128) (dS as 16-bit overwrites the first 16 of each warpgroup's 32 S
+// columns), dP x2 [128,256), dQ [256,512).  Per 64-key half u the MMAs go S(u),
+// dQ += dS K of half u-1 (A = dS from TMEM, B = K MN-major, N = 256), dP(u): S and dP
+// of half u run while the row threads form dS of half u-1, and the K half of u-1 is
+// released (for the load of u+1) before dP(u) runs.
 #include <cfloat>
 
 #include "fa4d.h"
@@ -25,7 +29,7 @@ namespace fa4d {
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
 
 struct Layout {
   static constexpr int kQT = 128 * 256 * 2;  // Q or dO tile (128 rows x 256)
@@ -37,14 +41,14 @@ struct Layout {
   static constexpr int kLSE = kV + kKT;
   static constexpr int kDelta = kLSE + 512;
   static constexpr int kBar = kDelta + 512;
-  static constexpr int kNumBars = 10;
+  static constexpr int kNumBars = 12;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
   static_assert(kAlloc <= 232448, "shared memory beyond the 227 KB per-block limit");
 };
 
-constexpr uint32_t kColS = 0, kColDP = 64, kColDQ = 128;
+constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256;  // S, dP: 2 buffers of 64 columns
 
 // D[128 x 64] = A[128 rows x 256] B[64 rows x 256]^T, both K-major (S = Q K^T, dP = dO V^T).
 template <bool kBF16>
@@ -58,13 +62,15 @@ __device__ __forceinline__ void issue_abt(uint32_t tD, uint32_t sA, uint32_t sB)
   }
 }
 
-// dQ (+)= dS K : M=128 queries, N=256, K=64 keys; dS from TMEM, K MN-major (4 chunks).
+// dQ (+)= dS K : M=128 queries, N=256, K=64 keys; dS from TMEM (keys 0-31 in columns
+// [0,16), keys 32-63 in [32,48) of the S buffer), K MN-major (4 chunks).
 template <bool kBF16>
 __device__ __forceinline__ void issue_dsk(uint32_t tDQ, uint32_t tDS, uint32_t sK, bool accumulate) {
   constexpr uint32_t idesc = make_idesc(128, 256, kBF16, false, true);
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk)
-    mma_ts(tDQ, tDS + kk * 8, sw128_desc(sK + kk * 2048, 8192, 1024), idesc, (accumulate || kk > 0) ? 1u : 0u);
+    mma_ts(tDQ, tDS + (kk >> 1) * 32 + (kk & 1) * 8, sw128_desc(sK + kk * 2048, 8192, 1024), idesc,
+           (accumulate || kk > 0) ? 1u : 0u);
 }
 
 // Number of 64-key halves of key tile kt that hold keys below kv_end (1 or 2).
@@ -81,9 +87,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
   uint64_t* k_empty = bars + 3;  // [2]
   uint64_t* v_full = bars + 5;
   uint64_t* v_empty = bars + 6;
-  uint64_t* s_full = bars + 7;   // S and dP of the current half are in TMEM
-  uint64_t* ds_full = bars + 8;  // dS written to TMEM (128 arrivals)
-  uint64_t* mma_drain = bars + 9;
+  uint64_t* s_full = bars + 7;    // [2] S and dP of the half are in TMEM
+  uint64_t* ds_full = bars + 9;   // [2] dS written to TMEM (256 arrivals)
+  uint64_t* mma_drain = bars + 11;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -117,8 +123,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
     }
     mbar_init(v_full, 1);
     mbar_init(v_empty, 1);
-    mbar_init(s_full, 1);
-    mbar_init(ds_full, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&ds_full[i], 256);
+    }
     mbar_init(mma_drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -132,13 +140,16 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && any_work) {
+  if ((warp == 0 || warp == 3) && lane == 0 && any_work) {
+    // ------------------------------------------------------------ TMA producers
+    // Warp 0: Q, dO, LSE, Delta once, then the K half of every half u (2-stage ring,
+    // a stage freed by dQ of its half); warp 3: the V half of every half (one stage,
+    // freed by dP of its half).
+    const bool is_k = warp == 0;
+    if (is_k) {
       prefetch_tmap(&p.tm_q);
       prefetch_tmap(&p.tm_do);
       prefetch_tmap(&p.tm_k);
-      prefetch_tmap(&p.tm_v);
       mbar_arrive_expect_tx(q_full, 2 * L::kQT + 1024);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -148,13 +159,17 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
       const int64_t row = (static_cast<int64_t>(b) * p.Hq + h) * p.lse_ld + q0;
       bulk_load(smem + L::kLSE, p.lse + row, 512, q_full);
       bulk_load(smem + L::kDelta, p.delta + row, 512, q_full);
-      int u = 0;  // halves whose K and V loads were both issued
-      bool stop = false;
-      for (int kt = kt_first; kt < tl.n && !stop; kt = tl.next(kt + 1)) {
-        const int nh = halves(kt, kv_end);
-        for (int j = 0; j < nh; ++j) {
+    } else {
+      prefetch_tmap(&p.tm_v);
+    }
+    int u = 0;  // halves whose load was issued
+    bool stop = false;
+    for (int kt = kt_first; kt < tl.n && !stop; kt = tl.next(kt + 1)) {
+      const int nh = halves(kt, kv_end);
+      for (int j = 0; j < nh; ++j) {
+        const int key0 = kt * 128 + 64 * j;
+        if (is_k) {
           const int s = u & 1;
-          const int key0 = kt * 128 + 64 * j;
           if (!mbar_wait(&k_empty[s], ((u >> 1) & 1) ^ 1, abort_flag)) {
             stop = true;
             break;
@@ -163,9 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             tma_load_4d(smem + L::kK + s * L::kKT + c * 8192, &p.tm_k, &k_full[s], c * 64, key0, hk, b);
+        } else {
           if (!mbar_wait(v_empty, (u & 1) ^ 1, abort_flag)) {
-            // K of this half is in flight, V is not: wait (bounded) for K here.
-            mbar_wait_short(&k_full[s], (u >> 1) & 1);
             stop = true;
             break;
           }
@@ -173,21 +187,25 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             tma_load_4d(smem + L::kV + c * 8192, &p.tm_v, v_full, c * 64, key0, hk, b);
-          ++u;
         }
-      }
-      if (*reinterpret_cast<volatile int*>(abort_flag)) {
-        // Wait (bounded) for the copies of the u issued halves still in flight.
-        mbar_wait_short(q_full, 0);
-        for (int jj = max(0, u - 2); jj < u; ++jj) mbar_wait_short(&k_full[jj & 1], (jj >> 1) & 1);
-        if (u > 0) mbar_wait_short(v_full, (u - 1) & 1);
+        ++u;
       }
     }
-    __syncwarp();
+    if (*reinterpret_cast<volatile int*>(abort_flag)) {
+      // Wait (bounded) for this producer's copies still in flight.
+      if (is_k) {
+        mbar_wait_short(q_full, 0);
+        for (int jj = max(0, u - 2); jj < u; ++jj) mbar_wait_short(&k_full[jj & 1], (jj >> 1) & 1);
+      } else if (u > 0) {
+        mbar_wait_short(v_full, (u - 1) & 1);
+      }
+    }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Per half u: dQ of half u-1 (it reads dS from the S columns, so it goes before
-    // this half's S), then S and dP of half u.
+    // Per half u: S(u) into buffer u & 1, then dQ += dS K of half u-1 (its dS sits in
+    // the other buffer; issuing it here frees that K stage before dP(u) runs), then
+    // dP(u).  S(u) overwrites the dS of half u-2, which dQ read one half earlier (MMAs
+    // run in issue order).
     if (any_work) {
       const uint32_t sQ = smem_u32(smem + L::kQ);
       const uint32_t sDO = smem_u32(smem + L::kDO);
@@ -196,43 +214,44 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
       auto wait = [&](uint64_t* bar, uint32_t parity) {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
       };
+      // dQ += dS K of half w (dS in S buffer w & 1, K in stage w & 1).
+      auto issue_dq = [&](int w) {
+        if (!wait(&ds_full[w & 1], (w >> 1) & 1)) return false;
+        tc_fence_after();
+        if (elect_one()) {
+          issue_dsk<kBF16>(tmem + kColDQ, tmem + kColS + 64 * (w & 1), sK + (w & 1) * L::kKT, w > 0);
+          tc_commit(&k_empty[w & 1]);
+        }
+        __syncwarp();
+        return true;
+      };
       bool ok = wait(q_full, 0);
       int u = 0;
       for (int kt = kt_first; ok && kt < tl.n; kt = tl.next(kt + 1)) {
         const int nh = halves(kt, kv_end);
         for (int j = 0; ok && j < nh; ++j, ++u) {
           const int s = u & 1;
-          ok = wait(&k_full[s], (u >> 1) & 1) && wait(v_full, u & 1);
+          ok = wait(&k_full[s], (u >> 1) & 1);
           if (!ok) break;
+          tc_fence_after();
+          if (elect_one()) issue_abt<kBF16>(tmem + kColS + 64 * s, sQ, sK + s * L::kKT);
+          __syncwarp();
           if (u > 0) {
-            ok = wait(ds_full, (u - 1) & 1);
+            ok = issue_dq(u - 1);
             if (!ok) break;
           }
+          ok = wait(v_full, u & 1);
+          if (!ok) break;
           tc_fence_after();
           if (elect_one()) {
-            if (u > 0) {
-              issue_dsk<kBF16>(tmem + kColDQ, tmem + kColS, sK + (s ^ 1) * L::kKT, u > 1);
-              tc_commit(&k_empty[s ^ 1]);
-            }
-            issue_abt<kBF16>(tmem + kColS, sQ, sK + s * L::kKT);
-            issue_abt<kBF16>(tmem + kColDP, sDO, sV);
+            issue_abt<kBF16>(tmem + kColDP + 64 * s, sDO, sV);
             tc_commit(v_empty);
-            tc_commit(s_full);
+            tc_commit(&s_full[s]);
           }
           __syncwarp();
         }
       }
-      if (ok && u > 0) {
-        ok = wait(ds_full, (u - 1) & 1);
-        if (ok) {
-          tc_fence_after();
-          if (elect_one()) {
-            issue_dsk<kBF16>(tmem + kColDQ, tmem + kColS, sK + ((u - 1) & 1) * L::kKT, u > 1);
-            tc_commit(&k_empty[(u - 1) & 1]);
-          }
-          __syncwarp();
-        }
-      }
+      if (ok && u > 0) ok = issue_dq(u - 1);
       if (elect_one()) tc_commit(mma_drain);
       __syncwarp();
       wait(mma_drain, 0);
@@ -240,13 +259,12 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ dS and epilogue
-    const int row = (warp - 4) * 32 + lane;
+    const int wg = (warp - 4) >> 2;  // keys 32 wg .. 32 wg + 31 of every half
+    const int row = (warp & 3) * 32 + lane;
     const int q = q0 + row;
     const bool q_valid = q < p.Tq;
     const int64_t qc = min(q, p.Tq - 1);
-    const uint32_t lane_base = static_cast<uint32_t>((warp - 4) * 32) << 16;
-    const uint32_t tS = tmem + lane_base + kColS;
-    const uint32_t tDP = tmem + lane_base + kColDP;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const float* score_row = nullptr;
     const uint8_t* mask_row = nullptr;
     const uint4* bits_row = nullptr;
@@ -283,11 +301,14 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
 #pragma unroll
           for (int c = 0; c < 2; ++c) w2[c] &= low_bits(key_lim - (kbase + 32 * c));
         }
-        ok = __all_sync(0xffffffffu, mbar_wait(s_full, u & 1, abort_flag));
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[u & 1], (u >> 1) & 1, abort_flag));
         if (!ok) break;
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        const uint32_t tS = tmem + lane_base + kColS + 64 * (u & 1);
+        const uint32_t tDP = tmem + lane_base + kColDP + 64 * (u & 1);
+        {
+          const int c = wg;
+          const uint32_t keep = wg ? w2[1] : w2[0];
           uint32_t sv[32], dpv[32];
           tmem_ld32(tS + 32 * c, sv);
           tmem_ld32(tDP + 32 * c, dpv);
@@ -320,17 +341,17 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
               if constexpr (kScore) x += add[i];
               const float pr = ex2(fmaf(x, p.scale_log2, -lse));
               // dS without the softmax scale (applied to dQ at the end).
-              ds2[jj] = ((w2[c] >> i) & 1u) ? pr * (__uint_as_float(dpv[i]) - delta) : 0.f;
+              ds2[jj] = ((keep >> i) & 1u) ? pr * (__uint_as_float(dpv[i]) - delta) : 0.f;
             }
             pk[e] = pack2<kBF16>(ds2[0], ds2[1]);
           }
-          // dS (16-bit) for keys 32c..32c+31 goes to columns 16c..16c+15, which hold S
-          // values already read.
-          tmem_st16(tS + 16 * c, pk);
+          // dS (16-bit) for keys 32c..32c+31 goes to columns 32c..32c+15: S values this
+          // warpgroup has already read (the other warpgroup reads only its own 32).
+          tmem_st16(tS + 32 * c, pk);
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(ds_full);
+        mbar_arrive(&ds_full[u & 1]);
       }
     }
     // Epilogue: dQ = scale * accumulated dS K, in the input dtype.
@@ -341,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
       ok = __all_sync(0xffffffffu, mbar_wait(mma_drain, 0, abort_flag));
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 4 * wg; c < 4 * wg + 4; ++c) {
         uint32_t v[32];
         tmem_ld32(tmem + lane_base + kColDQ + 32 * c, v);
         tmem_wait_ld();
@@ -357,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
       }
     } else if (q_valid) {
 #pragma unroll
-      for (int w = 0; w < 32; ++w) reinterpret_cast<uint4*>(dst)[w] = make_uint4(0u, 0u, 0u, 0u);
+      for (int w = 16 * wg; w < 16 * wg + 16; ++w) reinterpret_cast<uint4*>(dst)[w] = make_uint4(0u, 0u, 0u, 0u);
     }
     tc_fence_before();
   }
