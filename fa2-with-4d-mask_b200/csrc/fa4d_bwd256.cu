@@ -635,9 +635,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
           }
         }
-        // Every lane of the warp has used its P^T values: the peer may refill buffer jp.
-        __syncwarp();
-        if (lane == 0) mbar_arrive_remote(peer_out_free + 8u * jp);
         // dS^T row r into buffer s (A operand of dK) once the last dK has read it.
         ok = __all_sync(0xffffffffu, mbar_wait(&ds_empty[s], par ^ 1, abort_flag));
         if (!ok) break;
@@ -649,6 +646,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 make_uint4(dsk[4 * cc], dsk[4 * cc + 1], dsk[4 * cc + 2], dsk[4 * cc + 3]);
         }
         fence_async_smem();
+        // The peer may refill P^T buffer jp.  The hand-back is a relaxed arrival, which
+        // does not wait for this thread's earlier loads; it comes after the dS^T stores,
+        // which cannot issue before the P^T loads they depend on have returned (handing
+        // the buffer back straight after the loads let the next copy overwrite the first
+        // rows of a tile before they were read).
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(peer_out_free + 8u * jp);
         mbar_arrive(&ds_full[s]);
         cur = nxt;
       }
