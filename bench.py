@@ -866,6 +866,31 @@ def copy_leg(dev, dist, world, reps=5):
         ms = shard.max_over_ranks(median_ms(evs), dist, dev)
         out[name] = {"bytes_per_rank": n_in, "ms": round(ms, 4), "gbs_per_rank": round(n_in / ms / 1e6, 1),
                      "gbs_all_ranks": round(world * n_in / ms / 1e6, 1)}
+    # Both directions at once, as the end-to-end step runs them (one step's inputs up and
+    # the previous step's outputs down on two copy streams): the copy bound of that step.
+    h2 = torch.empty(n_in, dtype=torch.uint8).pin_memory()
+    d2 = torch.empty(n_in, dtype=torch.uint8, device=dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    evs = []
+    for _ in range(reps):
+        if dist:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        up.wait_event(a)
+        down.wait_event(a)
+        with torch.cuda.stream(up):
+            d.copy_(h, non_blocking=True)
+        with torch.cuda.stream(down):
+            h2.copy_(d2, non_blocking=True)
+        torch.cuda.current_stream(dev).wait_stream(up)
+        torch.cuda.current_stream(dev).wait_stream(down)
+        b.record()
+        torch.cuda.synchronize(dev)
+        evs.append((a, b))
+    ms = shard.max_over_ranks(median_ms(evs), dist, dev)
+    out["both"] = {"bytes_per_rank_each_way": n_in, "ms": round(ms, 4),
+                   "gbs_per_rank_each_way": round(n_in / ms / 1e6, 1)}
     return out
 
 

@@ -63,6 +63,13 @@ constexpr float kRescaleThreshold = 8.0f;
 #define FA4D_POLY_EVERY 3
 #endif
 constexpr int kPolyEvery = FA4D_POLY_EVERY;
+// At D = 64 the softmax warps signal P of keys 0-63 on their own barrier and the MMA
+// warp issues that half of PV at once, so only the second half of PV sits between the
+// end of the softmax and the slot's next S.  Measured (interleaved A/B, medians of 8
+// blocks of 10): D = 64 forward at config 2's shape -2.9%, config 5 forward -1.2%; at
+// D = 128 the same split made the forward 2% slower, so it is kept to D = 64.
+template <int D>
+constexpr bool kSplitPVFor = D == 64;
 // One staged score chunk (128 rows x 32 keys, fp32): 128 B per row, 128-B swizzled.
 constexpr int kRingEntry = 16384;
 
@@ -83,7 +90,7 @@ struct FwdLayout {
   static constexpr int kRingFit = kRingRoom / (kSlots * kRingEntry);
   static constexpr int kRingDepth = kScore ? (kRingFit < 4 ? kRingFit : 4) : 0;
   static constexpr int kBar = kRing + kSlots * kRingDepth * kRingEntry;
-  static constexpr int kNumBars = 16 + 4 * kRingDepth;
+  static constexpr int kNumBars = 18 + 4 * kRingDepth;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
@@ -102,12 +109,14 @@ __device__ __forceinline__ void issue_qk(uint32_t tS, uint32_t sQ, uint32_t sK) 
   }
 }
 
-// O[slot] (+)= P[slot] V : M=128, N=D, K=128; P from TMEM, V MN-major.
+// O[slot] (+)= P[slot] V : M=128, N=D, K=128; P from TMEM, V MN-major.  Covers keys
+// [64 * first_half, 64 * last_half + 64) of the tile (K-steps of 16 keys).
 template <int D, bool kBF16>
-__device__ __forceinline__ void issue_pv(uint32_t tO, uint32_t tP, uint32_t sV, bool accumulate) {
+__device__ __forceinline__ void issue_pv(uint32_t tO, uint32_t tP, uint32_t sV, bool accumulate, int first_half = 0,
+                                         int last_half = 1) {
   constexpr uint32_t idesc = make_idesc(128, D, kBF16, false, true);
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
+  for (int kk = 4 * first_half; kk < 4 * last_half + 4; ++kk) {
     mma_ts(tO, tP + kk * 8, sw128_desc(sV + kk * 2048, 16384, 1024), idesc,
            (accumulate || kk > 0) ? 1u : 0u);
   }
@@ -123,6 +132,7 @@ __device__ __forceinline__ int next_union(const SlotTiles<kMask>& s0, const Slot
 template <int D, bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_constant__ FwdParams p) {
   using L = FwdLayout<D, kMask, kScore>;
+  constexpr bool kSplitPV = kSplitPVFor<D>;
   constexpr int R = L::kRingDepth > 0 ? L::kRingDepth : 1;  // ring index modulus (ring unused if 0 deep)
   constexpr int KVS = L::kKVStages;
   extern __shared__ uint8_t smem_raw[];
@@ -141,6 +151,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
   uint64_t* mma_drain = bars + 15;
   uint64_t* ring_full = bars + 16;                         // [2 slots][kRingDepth]
   uint64_t* ring_empty = bars + 16 + 2 * L::kRingDepth;   // [2 slots][kRingDepth], 128 arrivals
+  uint64_t* p_half = bars + 16 + 4 * L::kRingDepth;       // [2] per slot: P of keys 0-63 written (D = 64)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -176,6 +187,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
+      mbar_init(&p_half[i], 128);
       mbar_init(&o_full[i], 1);
     }
     mbar_init(mma_drain, 1);
@@ -293,12 +305,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
           const bool cur = tl.state(kt) != 0;
           const bool nxt = has_next && tl.state(ktn) != 0;
           if (cur) {
+            if constexpr (kSplitPV) {
+              // The first half of PV goes out once the softmax warps have written P of
+              // keys 0-63, while they still work on the rest of the row.
+              ok = wait(&p_half[t], cnt & 1);
+              if (!ok) break;
+              tc_fence_after();
+              if (elect_one()) issue_pv<D, kBF16>(tmem + 256 + D * t, tmem + 128 * t, sV + sv * L::kTile, cnt > 0, 0, 0);
+              __syncwarp();
+            }
             ok = wait(&p_full[t], cnt & 1);
             if (!ok) break;
             tc_fence_after();
           }
           if (elect_one()) {
-            if (cur) issue_pv<D, kBF16>(tmem + 256 + D * t, tmem + 128 * t, sV + sv * L::kTile, cnt > 0);
+            if (cur) {
+              if constexpr (kSplitPV)
+                issue_pv<D, kBF16>(tmem + 256 + D * t, tmem + 128 * t, sV + sv * L::kTile, true, 1, 1);
+              else
+                issue_pv<D, kBF16>(tmem + 256 + D * t, tmem + 128 * t, sV + sv * L::kTile, cnt > 0);
+            }
             if (nxt) {
               // S of the slot's next tile; the PV above (or an earlier one) has
               // consumed the P that shares these TMEM columns.
@@ -460,7 +486,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         tmem_wait_ld();
         float m4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
 #pragma unroll
-        for (int k = 0; k < 128; ++k) m4[k & 3] = fmaxf(m4[k & 3], __uint_as_float(sr[k]));
+        for (int k = 0; k < 128; k += 2)
+          m4[(k >> 1) & 3] = fmax3(m4[(k >> 1) & 3], __uint_as_float(sr[k]), __uint_as_float(sr[k + 1]));
         const float m_use = online_update(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2);
         // exp2(s * scale * log2(e) - m) on pairs of packed fp32; every kPolyEvery-th
         // pair on the FMA pipe (ex2_poly2) so the MUFU unit is not the limit.
@@ -479,6 +506,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             pk[k] = pack2<kBF16>(pr.x, pr.y);
           }
           tmem_st16(tS + 16 * c, pk);
+          if (kSplitPV && c == 1) {
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&p_half[t]);
+          }
         }
         const float2 rs = f2_split(rs2);
         rowsum = rs.x + rs.y;
@@ -504,10 +536,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         tmem_wait_ld();
         float m4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
 #pragma unroll
-        for (int k = 0; k < 128; ++k) {
-          const float x = ((mw[k >> 5] >> (k & 31)) & 1u) ? __uint_as_float(xr[k]) * p.scale_log2 : kNegInf;
-          xr[k] = __float_as_uint(x);
-          m4[k & 3] = fmaxf(m4[k & 3], x);
+        for (int k = 0; k < 128; k += 2) {
+          const float x0 = ((mw[k >> 5] >> (k & 31)) & 1u) ? __uint_as_float(xr[k]) * p.scale_log2 : kNegInf;
+          const float x1 = ((mw[k >> 5] >> ((k + 1) & 31)) & 1u) ? __uint_as_float(xr[k + 1]) * p.scale_log2 : kNegInf;
+          xr[k] = __float_as_uint(x0);
+          xr[k + 1] = __float_as_uint(x1);
+          m4[(k >> 1) & 3] = fmax3(m4[(k >> 1) & 3], x0, x1);
         }
         const float m_use = online_update(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
         const uint64_t nm2 = f2(m_use, m_use);
@@ -523,6 +557,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             pk[k] = pack2<kBF16>(p0, p1);
           }
           tmem_st16(tS + 16 * c, pk);
+          if (kSplitPV && c == 1) {
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&p_half[t]);
+          }
         }
         const float2 rs = f2_split(rs2);
         rowsum = rs.x + rs.y;
@@ -631,6 +670,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
               pk[k] = pack2<kBF16>(p0, p1);
             }
             tmem_st16(tS + 32 * hh + 16 * c, pk);
+          }
+          if (kSplitPV && hh == 0) {
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&p_half[t]);
           }
         }
         const float2 rs = f2_split(rs2);

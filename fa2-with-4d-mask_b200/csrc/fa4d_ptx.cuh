@@ -389,6 +389,13 @@ __device__ __forceinline__ float ex2_poly(float x) {
 // ------------------------------------------------------------------ packed fp32 pairs
 // sm_100 executes add/sub/fma on two fp32 values held in one 64-bit register pair as
 // one instruction (same rounding as the scalar forms).
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ uint64_t f2(float a, float b) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
@@ -431,9 +438,10 @@ __device__ __forceinline__ float2 ex2_poly2(float x0, float x1) {
   p = ffma2(p, f, f2(0.69326097f, 0.69326097f));
   p = ffma2(p, f, f2(0.99992806f, 0.99992806f));
   const float2 tv = f2_split(t), pv = f2_split(p);
-  const int n0 = __float_as_int(tv.x) - 0x4B400000, n1 = __float_as_int(tv.y) - 0x4B400000;
-  return make_float2(__int_as_float(__float_as_int(pv.x) + (n0 << 23)),
-                     __int_as_float(__float_as_int(pv.y) + (n1 << 23)));
+  // n << 23 with n = bits(t) - 0x4B400000: every set bit of that constant sits at bit 22
+  // or above, so shifting bits(t) alone gives the same word.
+  return make_float2(__int_as_float(__float_as_int(pv.x) + (__float_as_int(tv.x) << 23)),
+                     __int_as_float(__float_as_int(pv.y) + (__float_as_int(tv.y) << 23)));
 }
 
 template <bool kBF16>
