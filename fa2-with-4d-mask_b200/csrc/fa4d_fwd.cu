@@ -22,8 +22,9 @@
 // Mask tiles (PARTIAL blocks only) and score chunks reach shared memory by TMA
 // through a per-slot ring, so the softmax threads read them with 16-B shared loads
 // instead of waiting on global memory.
-// At D=256 the CTA has one slot (S0 and O0 [256,512) fill TMEM's 512 columns) and
-// warps 8-11 stay idle.
+// At D=256 the CTA has one slot whose S has two buffers, [0,128) and [128,256), with
+// O0 [256,512): the next key tile's S is computed while the softmax works on the
+// current one.  Warp 2 then loads V (warp 0 Q and K) and warps 8-11 stay idle.
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
 // P (16-bit) overwrites the first 64 columns of S and feeds the PV MMA from TMEM.
 #include <cfloat>
@@ -76,9 +77,9 @@ constexpr int kRingEntry = 16384;
 template <int D, bool kMask, bool kScore>
 struct FwdLayout {
   static constexpr int kTile = 128 * D * 2;  // one 128-row tile of 16-bit elements
-  // Query slots per CTA.  At D=256 one slot's S (128 columns) and O (256) take 384 of
-  // the 512 TMEM columns and its Q, K and V tiles 192 KB of shared memory, so the CTA
-  // has one slot and single-stage K/V (the second slot's warps stay idle).
+  // Query slots per CTA.  At D=256 one slot's O takes 256 of the 512 TMEM columns and
+  // its Q, K and V tiles 192 KB of shared memory, so the CTA has one slot (with two S
+  // buffers) and single-stage K/V (the second slot's warps stay idle).
   static constexpr int kSlots = D == 256 ? 1 : 2;
   // With a score at D=128 the score staging rings take the room of one K/V stage.
   static constexpr int kKVStages = (D == 256 || (kScore && D == 128)) ? 1 : 2;
@@ -90,7 +91,7 @@ struct FwdLayout {
   static constexpr int kRingFit = kRingRoom / (kSlots * kRingEntry);
   static constexpr int kRingDepth = kScore ? (kRingFit < 4 ? kRingFit : 4) : 0;
   static constexpr int kBar = kRing + kSlots * kRingDepth * kRingEntry;
-  static constexpr int kNumBars = 18 + 4 * kRingDepth;
+  static constexpr int kNumBars = 19 + 4 * kRingDepth;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
@@ -133,6 +134,10 @@ template <int D, bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_constant__ FwdParams p) {
   using L = FwdLayout<D, kMask, kScore>;
   constexpr bool kSplitPV = kSplitPVFor<D>;
+  // One query slot per CTA (D = 256): the slot's S has two TMEM buffers, [0,128) and
+  // [128,256) (O takes [256,512)), so the S of the next key tile is computed while the
+  // softmax works on the current one; V comes from its own producer warp (warp 2).
+  constexpr bool kDoubleS = L::kSlots == 1;
   constexpr int R = L::kRingDepth > 0 ? L::kRingDepth : 1;  // ring index modulus (ring unused if 0 deep)
   constexpr int KVS = L::kKVStages;
   extern __shared__ uint8_t smem_raw[];
@@ -152,6 +157,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
   uint64_t* ring_full = bars + 16;                         // [2 slots][kRingDepth]
   uint64_t* ring_empty = bars + 16 + 2 * L::kRingDepth;   // [2 slots][kRingDepth], 128 arrivals
   uint64_t* p_half = bars + 16 + 4 * L::kRingDepth;       // [2] per slot: P of keys 0-63 written (D = 64)
+  uint64_t* pv_done = bars + 18 + 4 * L::kRingDepth;      // one slot (D = 256): PV of a tile completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -191,6 +197,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       mbar_init(&o_full[i], 1);
     }
     mbar_init(mma_drain, 1);
+    mbar_init(pv_done, 1);
     for (int i = 0; i < 2 * L::kRingDepth; ++i) {
       mbar_init(&ring_full[i], 1);
       mbar_init(&ring_empty[i], 128);
@@ -236,21 +243,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
           tma_load_4d(sK + s * L::kTile + c * 16384, &p.tm_k, &k_full[s], c * 64, kt * 128, hk, b);
-        if (!mbar_wait(&v_empty[s], par, abort_flag)) {
-          k_pending = true;
-          break;
-        }
-        mbar_arrive_expect_tx(&v_full[s], L::kTile);
+        if constexpr (!kDoubleS) {
+          if (!mbar_wait(&v_empty[s], par, abort_flag)) {
+            k_pending = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&v_full[s], L::kTile);
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(sV + s * L::kTile + c * 16384, &p.tm_v, &v_full[s], c * 64, kt * 128, hk, b);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_4d(sV + s * L::kTile + c * 16384, &p.tm_v, &v_full[s], c * 64, kt * 128, hk, b);
+        }
       }
       // Abort path only: make sure no copy is still writing shared memory.
       if (*reinterpret_cast<volatile int*>(abort_flag)) {
         mbar_wait_short(q_full, 0);
         for (int j = max(0, u - KVS); j < u; ++j) {
           mbar_wait_short(&k_full[j % KVS], (j / KVS) & 1);
-          mbar_wait_short(&v_full[j % KVS], (j / KVS) & 1);
+          if (!kDoubleS) mbar_wait_short(&v_full[j % KVS], (j / KVS) & 1);
         }
         if (k_pending) mbar_wait_short(&k_full[u % KVS], (u / KVS) & 1);
       }
@@ -267,6 +276,53 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       auto wait = [&](uint64_t* bar, uint32_t parity) {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
       };
+      if constexpr (kDoubleS) {
+        // Tile u's S sits in buffer u & 1.  S of tile u+1 goes out as soon as its K has
+        // landed, ahead of PV of tile u; its buffer last held P of tile u-1, whose PV
+        // was issued in the previous iteration (the tensor pipe runs them in order).
+        bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
+        if (ok) {
+          tc_fence_after();
+          if (elect_one()) {
+            issue_qk<D, kBF16>(tmem, sQ, sK);
+            tc_commit(&s_full[0]);
+            tc_commit(&k_empty[0]);
+          }
+          __syncwarp();
+        }
+        int u = 0;
+        for (int kt = kt_first; ok && kt < n_max; ++u) {
+          const int ktn = next_union(tiles0, tiles1, kt + 1, n_max);
+          const bool has_next = ktn < n_max;
+          if (has_next) {
+            const int sk = (u + 1) % KVS;
+            ok = wait(&k_full[sk], ((u + 1) / KVS) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            if (elect_one()) {
+              issue_qk<D, kBF16>(tmem + 128 * ((u + 1) & 1), sQ, sK + sk * L::kTile);
+              tc_commit(&s_full[(u + 1) & 1]);
+              tc_commit(&k_empty[sk]);
+            }
+            __syncwarp();
+          }
+          const int sv = u % KVS;
+          ok = wait(&v_full[sv], (u / KVS) & 1) && wait(&p_full[u & 1], (u >> 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          if (elect_one()) {
+            issue_pv<D, kBF16>(tmem + 256, tmem + 128 * (u & 1), sV + sv * L::kTile, u > 0);
+            tc_commit(pv_done);
+            tc_commit(&v_empty[sv]);
+            if (!has_next) tc_commit(&o_full[0]);
+          }
+          __syncwarp();
+          kt = ktn;
+        }
+        if (elect_one()) tc_commit(mma_drain);
+        __syncwarp();
+        wait(mma_drain, 0);
+      } else {
       const int last0 = tiles0.last(), last1 = tiles1.last();
       bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
       if (ok) {
@@ -349,6 +405,27 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       if (elect_one()) tc_commit(mma_drain);
       __syncwarp();
       wait(mma_drain, 0);
+      }
+    }
+    __syncwarp();
+    } else if (kDoubleS && warp == 2) {
+    // ------------------------------------------------------------ V producer (one slot)
+    // V of tile u is loaded once PV of tile u-1 has freed the stage; K (warp 0) does not
+    // wait behind it.
+    if (lane == 0 && any_work) {
+      uint8_t* sV = smem + L::kV;
+      int u = 0;
+      for (int kt = kt_first; kt < n_max; kt = next_union(tiles0, tiles1, kt + 1, n_max), ++u) {
+        const int s = u % KVS;
+        if (!mbar_wait(&v_empty[s], ((u / KVS) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&v_full[s], L::kTile);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(sV + s * L::kTile + c * 16384, &p.tm_v, &v_full[s], c * 64, kt * 128, hk, b);
+      }
+      if (*reinterpret_cast<volatile int*>(abort_flag)) {
+        for (int j = max(0, u - KVS); j < u; ++j) mbar_wait_short(&v_full[j % KVS], (j / KVS) & 1);
+      }
     }
     __syncwarp();
     } else if (kScore) {
@@ -394,7 +471,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     const int q = qs + row;
     const bool q_valid = q < p.Tq;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_base + 128 * t;
+    const uint32_t tS_slot = tmem + lane_base + 128 * t;
     const uint32_t tO = tmem + lane_base + 256 + D * t;
     const SlotTiles<kMask> tl = t ? tiles1 : tiles0;
 
@@ -444,7 +521,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         bits_next = __ldg(bits_row + static_cast<int64_t>(kt_next) * p.Tq);
 
       // Warp-uniform outcome: the tcgen05.ld below is warp-collective.
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], i & 1, abort_flag));
+      // S buffer of this tile (one-slot CTAs alternate two) and its completion phase.
+      const int sb = kDoubleS ? (i & 1) : t;
+      const uint32_t tS = kDoubleS ? tmem + lane_base + 128 * sb : tS_slot;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[sb], kDoubleS ? (i >> 1) & 1 : i & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
 
@@ -465,7 +545,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
           m_run = m_new;
         }
         if (i > 0 && __any_sync(0xffffffffu, need)) {
-          // The slot's previous PV has completed (this tile's S was issued after it).
+          // The slot's previous PV has completed (this tile's S was issued after it), or,
+          // with two S buffers, is waited for here: PV of tile i cannot have completed
+          // (it needs this tile's P) and PV of tile i-2 ran before this tile's S, so
+          // pv_done is in the phase of PV i-1 or the one after it.
+          if (kDoubleS) mbar_wait(pv_done, (i - 1) & 1, abort_flag);
 #pragma unroll
           for (int c = 0; c < D / 16; ++c) {
             uint32_t o[16];
@@ -683,7 +767,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
       l_run += rowsum;
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[t]);
+      mbar_arrive(&p_full[sb]);
       kt = kt_next;
     }
 
