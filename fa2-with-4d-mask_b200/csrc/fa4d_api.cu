@@ -610,12 +610,14 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
   p.dk = a->dk;
   p.dv = a->dv;
   p.v = a->v;
+  p.k = a->k;
   p.mask = a->mask;
   p.score = a->score;
   for (int i = 0; i < 3; ++i) {
     p.dk_stride[i] = a->dk_stride[i];
     p.dv_stride[i] = a->dv_stride[i];
     p.v_stride[i] = a->v_stride[i];
+    p.k_stride[i] = a->k_stride[i];
     p.mask_stride[i] = a->mask_stride[i];
     p.score_stride[i] = a->score_stride[i];
   }

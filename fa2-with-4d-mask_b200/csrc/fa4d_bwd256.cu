@@ -22,22 +22,27 @@
 // B1 T8192 Hq32, more than the whole ordered pass costs.)
 //
 // CTA = 128 keys x one (batch, KV head) x one rank; 384 threads:
-//   warp 0       TMA producer of the operand this rank needs first (rank 0: K, then Q
-//                per 64-row query tile; rank 1: dO), 2-stage ring
+//   warp 0       TMA producer of the operand this rank needs first (rank 0: Q per
+//                64-row query tile; rank 1: dO), 2-stage ring
 //   warp 1       tcgen05.mma issuer
 //   warp 2       TMEM allocator; then rank 0: copies each staged P^T tile to rank 1;
 //                rank 1: counts each tile's bytes in and reports its landing
 //   warp 3       TMA producer of the operand needed last, with the row statistic
 //                (rank 0: dO and LSE; rank 1: Q and Delta), 2-stage ring, so each
 //                stage is released by its last reader and neither ring waits on the other
-//   warps 4-7    queries 0-31 of every tile (one thread per key row), then columns
-//                0-127 of dV (rank 0) or dK (rank 1); rank 1: V columns 0-127 into TMEM
-//   warps 8-11   queries 32-63, then columns 128-255; rank 1: V columns 128-255
+//   warps 4-7    first K (rank 0) or V (rank 1) columns 0-127 of their key into TMEM,
+//                then queries 0-31 of every tile (one thread per key row), then
+//                columns 0-127 of dV (rank 0) or dK (rank 1)
+//   warps 8-11   the same for columns 128-255 and queries 32-63
 // TMEM (512 columns): rank 0  S^T x2 [0,128) (P^T over the first 16 columns of each
-//                             warpgroup's 32), dV [256,512)
+//                             warpgroup's 32), K [128,256) (16-bit pairs, the A
+//                             operand of S^T: only Q is read from shared memory, which
+//                             took 6.3% off the kernel against S^T from shared memory),
+//                             dV [256,512)
 //                     rank 1  dP^T [0,64), V [64,192) (16-bit pairs, the A operand of
 //                             dP^T), dK [256,512)
-// Shared memory: rank 0  K 64 KB, Q x2, dO x2 (32 KB each), P^T staged x2 (16 KB each), LSE
+// Shared memory: rank 0  Q x2, dO x2 (32 KB each), P^T staged x2 (16 KB each), LSE (its
+//                        first 64 KB unused)
 //                rank 1  P^T received x4 (16 KB each), Q x2, dO x2, dS^T x2, Delta
 #include <algorithm>
 
@@ -58,10 +63,9 @@ static_assert(128 * kRegsCtl + 256 * kRegsRows <= kThreads * kRegsLaunch,
               "register split exceeds the launch allocation");
 
 struct Layout {
-  static constexpr int kKT = 128 * 256 * 2;  // K tile (128 keys x 256)
+  static constexpr int kKT = 128 * 256 * 2;  // one 128-key tile x 256 (rank 1's received P^T ring)
   static constexpr int kQT = 64 * 256 * 2;   // Q or dO tile (64 queries x 256)
   static constexpr int kXT = 128 * 64 * 2;   // P^T or dS^T tile (128 keys x 64 queries, 16-bit)
-  static constexpr int kK = 0;               // rank 0: K
   static constexpr int kPin = 0;             // rank 1: P^T received, kPinBufs buffers
   static constexpr int kPinBufs = 4;
   static constexpr int kQ = kKT;             // 2 stages
@@ -81,6 +85,7 @@ struct Layout {
 constexpr uint32_t kColS = 0;      // rank 0: S^T, 2 buffers of 64 columns
 constexpr uint32_t kColDP = 0;     // rank 1: dP^T
 constexpr uint32_t kColV = 64;     // rank 1: V, 128 columns
+constexpr uint32_t kColK = 128;    // rank 0: K, 128 columns (the A operand of S^T)
 constexpr uint32_t kColAcc = 256;  // rank 0 dV, rank 1 dK: 256 columns
 constexpr uint32_t kPBytes = 128 * 64 * 2;  // bytes of one P^T tile sent to rank 1
 
@@ -145,8 +150,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // a shared-memory offset names the same buffer in either.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  uint64_t* k_full = bars + 0;     // rank 0: K in shared memory
-  uint64_t* v_full = bars + 1;     // rank 1: V in TMEM (256 arrivals)
+  uint64_t* v_full = bars + 1;     // rank 1: V in TMEM; rank 0: K in TMEM (256 arrivals)
   uint64_t* dkv_full = bars + 2;   // every dV / dK product done
   uint64_t* mma_drain = bars + 3;
   uint64_t* q_full = bars + 4;     // [2]
@@ -203,7 +207,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const bool any_work = first.valid();
 
   if (threadIdx.x == 0) {
-    mbar_init(k_full, 1);
     mbar_init(v_full, 256);
     mbar_init(dkv_full, 1);
     mbar_init(mma_drain, 1);
@@ -258,12 +261,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint64_t* empty = is_q ? q_empty : do_empty;
       uint8_t* ring = smem + (is_q ? L::kQ : L::kDO);
       prefetch_tmap(tm);
-      if (rank == 0 && !late) {
-        prefetch_tmap(&p.tm_k);
-        mbar_arrive_expect_tx(k_full, L::kKT);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tma_load_4d(smem + L::kK + c * 16384, &p.tm_k, k_full, c * 64, k0, hk, b);
-      }
       if (kScore && p.score_pf && rank == 0 && late) prefetch_tmap(&p.tm_score);
       int issued = 0;
       QTiles<kMask> cur = first;
@@ -288,7 +285,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       if (*reinterpret_cast<volatile int*>(abort_flag)) {
         // Let the copies in flight land before the CTA leaves.
-        if (rank == 0 && !late) mbar_wait_short(k_full, 0);
         for (int it = max(0, issued - 2); it < issued; ++it) mbar_wait_short(&full[it & 1], (it >> 1) & 1);
       }
     } else if (warp == 2 && rank == 0 && any_work) {
@@ -347,13 +343,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (rank == 0) {
         // Per tile: dV after its P^T, then S^T of the tile two ahead into the same
         // buffer (MMAs run in issue order, so it overwrites P^T only after dV read it).
-        const uint32_t sK = smem_u32(smem + L::kK);
+        // S^T = K Q^T with K from TMEM (TS form, as dP^T on rank 1): only Q is read from
+        // shared memory.
+        const uint32_t tK = tmem + kColK;
         const uint32_t tS = tmem + kColS;
-        ok = wait(k_full, 0) && wait(&q_full[0], 0);
+        ok = wait(v_full, 0) && wait(&q_full[0], 0);
         if (ok) {
           tc_fence_after();
           if (elect_one()) {
-            issue_s<kBF16>(tS, sK, sQ);
+            issue_dp<kBF16>(tS, tK, sQ);
             tc_commit(&s_full[0]);
             tc_commit(&q_empty[0]);
           }
@@ -365,7 +363,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (ok) {
               tc_fence_after();
               if (elect_one()) {
-                issue_s<kBF16>(tS + 64, sK, sQ + L::kQT);
+                issue_dp<kBF16>(tS + 64, tK, sQ + L::kQT);
                 tc_commit(&s_full[1]);
                 tc_commit(&q_empty[1]);
               }
@@ -394,7 +392,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (!ok) break;
             tc_fence_after();
             if (elect_one()) {
-              issue_s<kBF16>(tS + 64 * s, sK, sQ + s * L::kQT);
+              issue_dp<kBF16>(tS + 64 * s, tK, sQ + s * L::kQT);
               tc_commit(&s_full[s]);
               tc_commit(&q_empty[s]);
             }
@@ -466,6 +464,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bool ok = true;
 
     if (rank == 0) {
+      if (any_work) {
+        // K columns [128 wg, 128 wg + 128) of this key into TMEM (zeros past Tk).
+        const uint4* krow = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.k) +
+                                                           b * p.k_stride[0] + static_cast<int64_t>(kc) * p.k_stride[1] +
+                                                           hk * p.k_stride[2] + 128 * wg);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t w[16];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint4 x = k_valid ? __ldg(krow + 4 * j + u) : make_uint4(0u, 0u, 0u, 0u);
+            w[4 * u] = x.x;
+            w[4 * u + 1] = x.y;
+            w[4 * u + 2] = x.z;
+            w[4 * u + 3] = x.w;
+          }
+          tmem_st16(tmem + lane_base + kColK + 64 * wg + 16 * j, w);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(v_full);
+      }
       QTiles<kMask> cur = first;
       auto load_bits = [&](const QTiles<kMask>& c) {
         const int hh = h_first + c.g();

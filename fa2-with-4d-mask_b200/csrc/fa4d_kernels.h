@@ -111,6 +111,8 @@ struct BwdParams {
   // kernel copies each key's V row into tensor memory with plain loads.
   const void* v;
   int64_t v_stride[3];
+  const void* k;        // D = 256: rank 0 copies its K tile into TMEM (A operand of S^T)
+  int64_t k_stride[3];
 };
 
 // Deterministic dQ: one CTA per 128-row query tile of one (batch, head) walks its key
