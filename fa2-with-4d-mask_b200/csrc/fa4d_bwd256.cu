@@ -40,10 +40,10 @@
 //                             took 6.3% off the kernel against S^T from shared memory),
 //                             dV [256,512)
 //                     rank 1  dP^T [0,64), V [64,192) (16-bit pairs, the A operand of
-//                             dP^T), dK [256,512)
+//                             dP^T), dS^T x2 [192,256) (the A operand of dK), dK [256,512)
 // Shared memory: rank 0  Q x2, dO x2 (32 KB each), P^T staged x2 (16 KB each), LSE (its
 //                        first 64 KB unused)
-//                rank 1  P^T received x4 (16 KB each), Q x2, dO x2, dS^T x2, Delta
+//                rank 1  P^T received x4 (16 KB each), Q x2, dO x2, Delta
 #include <algorithm>
 
 #include "fa4d.h"
@@ -70,7 +70,7 @@ struct Layout {
   static constexpr int kPinBufs = 4;
   static constexpr int kQ = kKT;             // 2 stages
   static constexpr int kDO = kQ + 2 * kQT;   // 2 stages
-  static constexpr int kDS = kDO + 2 * kQT;  // rank 1: dS^T, 2 buffers
+  static constexpr int kDS = kDO + 2 * kQT;  // rank 0: P^T staging (rank 1: unused)
   static constexpr int kStage = kDS;         // rank 0: P^T (fp16) staged for the peer, 2 buffers
   static constexpr int kStat = kDS + 2 * kXT;  // 2 stages x 64 floats: rank 0 LSE, rank 1 Delta
   static constexpr int kBar = kStat + 2 * 256;
@@ -86,26 +86,15 @@ constexpr uint32_t kColS = 0;      // rank 0: S^T, 2 buffers of 64 columns
 constexpr uint32_t kColDP = 0;     // rank 1: dP^T
 constexpr uint32_t kColV = 64;     // rank 1: V, 128 columns
 constexpr uint32_t kColK = 128;    // rank 0: K, 128 columns (the A operand of S^T)
+constexpr uint32_t kColDS = 192;   // rank 1: dS^T, 2 buffers of 32 columns (the A operand of dK)
 constexpr uint32_t kColAcc = 256;  // rank 0 dV, rank 1 dK: 256 columns
 constexpr uint32_t kPBytes = 128 * 64 * 2;  // bytes of one P^T tile sent to rank 1
 
 // Byte offset of 16-byte chunk cc of row r in a tile of 128-byte rows, 128-B swizzled
-// (chunk ^ (row % 8)): the layout the tensor cores read dS^T in, also used for P^T so
-// that a warp's 32 rows spread over all banks.
+// (chunk ^ (row % 8)): the layout of the P^T tiles, so that a warp's 32 rows spread over
+// all banks.
 __device__ __forceinline__ uint32_t sw_chunk(int r, int cc) {
   return static_cast<uint32_t>(r * 128 + ((cc ^ (r & 7)) << 4));
-}
-
-// S^T = K Q^T: M=128 keys, N=64 queries, K=256; both K-major (4 chunks of 64 columns).
-template <bool kBF16>
-__device__ __forceinline__ void issue_s(uint32_t tD, uint32_t sK, uint32_t sQ) {
-  constexpr uint32_t idesc = make_idesc(128, 64, kBF16, false, false);
-#pragma unroll
-  for (int kk = 0; kk < 16; ++kk) {
-    const uint32_t offa = static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 32);
-    const uint32_t offb = static_cast<uint32_t>((kk >> 2) * 8192 + (kk & 3) * 32);
-    mma_ss(tD, sw128_desc(sK + offa, 16, 1024), sw128_desc(sQ + offb, 16, 1024), idesc, kk > 0 ? 1u : 0u);
-  }
 }
 
 // dP^T = V dO^T: M=128 keys, N=64 queries, K=256; V from TMEM (columns kk*8 hold the
@@ -131,14 +120,14 @@ __device__ __forceinline__ void issue_dv(uint32_t tD, uint32_t tS, uint32_t sDO,
            (acc || kk > 0) ? 1u : 0u);
 }
 
-// dK += dS^T Q: M=128 keys, N=256, K=64 queries; dS^T K-major, Q MN-major.
+// dK += dS^T Q: M=128 keys, N=256, K=64 queries; dS^T from TMEM (queries 0-31 in
+// columns [0,16), 32-63 in [16,32)), Q MN-major.
 template <bool kBF16>
-__device__ __forceinline__ void issue_dk(uint32_t tD, uint32_t sDS, uint32_t sQ, bool acc) {
+__device__ __forceinline__ void issue_dk(uint32_t tD, uint32_t tDS, uint32_t sQ, bool acc) {
   constexpr uint32_t idesc = make_idesc(128, 256, kBF16, false, true);
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk)
-    mma_ss(tD, sw128_desc(sDS + kk * 32, 16, 1024), sw128_desc(sQ + kk * 2048, 8192, 1024), idesc,
-           (acc || kk > 0) ? 1u : 0u);
+    mma_ts(tD, tDS + kk * 8, sw128_desc(sQ + kk * 2048, 8192, 1024), idesc, (acc || kk > 0) ? 1u : 0u);
 }
 
 template <bool kBF16, bool kMask, bool kScore>
@@ -403,7 +392,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       } else {
         // Per tile: dP^T of the next tile as soon as this tile's dP^T has been read out
         // (one buffer), then dK of this tile after its dS^T.
-        const uint32_t sDS = smem_u32(smem + L::kDS);
         const uint32_t tDP = tmem + kColDP, tV = tmem + kColV;
         ok = wait(v_full, 0) && wait(&do_full[0], 0);
         if (ok) {
@@ -436,7 +424,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (!ok) break;
           tc_fence_after();
           if (elect_one()) {
-            issue_dk<kBF16>(tAcc, sDS + s * L::kXT, sQ + s * L::kQT, it > 0);
+            issue_dk<kBF16>(tAcc, tmem + kColDS + 32 * s, sQ + s * L::kQT, it > 0);
             tc_commit(&q_empty[s]);
             tc_commit(&ds_empty[s]);
           }
@@ -655,24 +643,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
           }
         }
-        // dS^T row r into buffer s (A operand of dK) once the last dK has read it.
+        // dS^T row r into TMEM buffer s (A operand of dK) once the last dK has read it.
         ok = __all_sync(0xffffffffu, mbar_wait(&ds_empty[s], par ^ 1, abort_flag));
         if (!ok) break;
-        {
-          uint8_t* row = smem + L::kDS + s * L::kXT;
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
-            *reinterpret_cast<uint4*>(row + sw_chunk(r, 4 * wg + cc)) =
-                make_uint4(dsk[4 * cc], dsk[4 * cc + 1], dsk[4 * cc + 2], dsk[4 * cc + 3]);
-        }
-        fence_async_smem();
+        tc_fence_after();
+        tmem_st16(tmem + lane_base + kColDS + 32 * s + 16 * wg, dsk);
+        tmem_wait_st();
         // The peer may refill P^T buffer jp.  The hand-back is a relaxed arrival, which
-        // does not wait for this thread's earlier loads; it comes after the dS^T stores,
-        // which cannot issue before the P^T loads they depend on have returned (handing
-        // the buffer back straight after the loads let the next copy overwrite the first
-        // rows of a tile before they were read).
+        // does not wait for this thread's earlier loads; it comes after the dS^T stores
+        // have completed, which cannot happen before the P^T loads they depend on have
+        // returned (handing the buffer back straight after the loads let the next copy
+        // overwrite the first rows of a tile before they were read).
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(peer_out_free + 8u * jp);
+        tc_fence_before();
         mbar_arrive(&ds_full[s]);
         cur = nxt;
       }
