@@ -41,7 +41,7 @@ struct Layout {
   static constexpr int kLSE = kV + kKT;
   static constexpr int kDelta = kLSE + 512;
   static constexpr int kBar = kDelta + 512;
-  static constexpr int kNumBars = 12;
+  static constexpr int kNumBars = 13;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -78,6 +78,11 @@ __device__ __forceinline__ int halves(int kt, int kv_end) { return kt * 128 + 64
 
 template <bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constant__ DqParams p) {
+  // With a mask or score the row threads take longer per half, and a single issuing
+  // thread, which issues dP(u) only after dQ of half u-1 (and so after its dS), stalls
+  // behind them: those variants give dP to warp 2 (dQ pass with mask + score at B1 T4096
+  // H16: 0.984 -> 0.660 ms).  The dense variants keep one issuer (1% faster there).
+  constexpr bool kTwoIssuers = kMask || kScore;
   using L = Layout;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -87,9 +92,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
   uint64_t* k_empty = bars + 3;  // [2]
   uint64_t* v_full = bars + 5;
   uint64_t* v_empty = bars + 6;
-  uint64_t* s_full = bars + 7;    // [2] S and dP of the half are in TMEM
+  uint64_t* s_full = bars + 7;    // [2] S and dP of the half are in TMEM (one commit per issuer)
   uint64_t* ds_full = bars + 9;   // [2] dS written to TMEM (256 arrivals)
   uint64_t* mma_drain = bars + 11;
+  uint64_t* mma_drain_dp = bars + 12;  // the dP issuer's MMAs complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + L::kMisc + 4);
 
@@ -124,10 +130,11 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
     mbar_init(v_full, 1);
     mbar_init(v_empty, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
+      mbar_init(&s_full[i], kTwoIssuers ? 2 : 1);
       mbar_init(&ds_full[i], 256);
     }
     mbar_init(mma_drain, 1);
+    mbar_init(mma_drain_dp, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -201,11 +208,12 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ MMA issuer (S, dQ, dP)
     // Per half u: S(u) into buffer u & 1, then dQ += dS K of half u-1 (its dS sits in
-    // the other buffer; issuing it here frees that K stage before dP(u) runs), then
-    // dP(u).  S(u) overwrites the dS of half u-2, which dQ read one half earlier (MMAs
-    // run in issue order).
+    // the other buffer; issuing it frees that K stage), then dP(u) (from warp 2 in the
+    // mask / score variants).  S(u) overwrites the dS of half u-2, which dQ read one half
+    // earlier (MMAs of one thread run in issue order).  s_full of a half completes with
+    // the commit after dP, or with two issuers with one commit after each of S and dP.
     if (any_work) {
       const uint32_t sQ = smem_u32(smem + L::kQ);
       const uint32_t sDO = smem_u32(smem + L::kDO);
@@ -234,10 +242,52 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
           ok = wait(&k_full[s], (u >> 1) & 1);
           if (!ok) break;
           tc_fence_after();
-          if (elect_one()) issue_abt<kBF16>(tmem + kColS + 64 * s, sQ, sK + s * L::kKT);
+          if (elect_one()) {
+            issue_abt<kBF16>(tmem + kColS + 64 * s, sQ, sK + s * L::kKT);
+            if (kTwoIssuers) tc_commit(&s_full[s]);
+          }
           __syncwarp();
           if (u > 0) {
             ok = issue_dq(u - 1);
+            if (!ok) break;
+          }
+          if constexpr (!kTwoIssuers) {
+            ok = wait(v_full, u & 1);
+            if (!ok) break;
+            tc_fence_after();
+            if (elect_one()) {
+              issue_abt<kBF16>(tmem + kColDP + 64 * s, sDO, sV);
+              tc_commit(v_empty);
+              tc_commit(&s_full[s]);
+            }
+            __syncwarp();
+          }
+        }
+      }
+      if (ok && u > 0) ok = issue_dq(u - 1);
+      if (elect_one()) tc_commit(mma_drain);
+      __syncwarp();
+      wait(mma_drain, 0);
+    }
+    __syncwarp();
+  } else if (kTwoIssuers && warp == 2) {
+    // ------------------------------------------------------------ MMA issuer (dP)
+    // dP(u) into buffer u & 1 once V(u) has landed and the row threads have read dP of
+    // half u-2 out of that buffer (they arrive on ds_full after reading it).
+    if (any_work) {
+      const uint32_t sDO = smem_u32(smem + L::kDO);
+      const uint32_t sV = smem_u32(smem + L::kV);
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+      };
+      bool ok = wait(q_full, 0);
+      int u = 0;
+      for (int kt = kt_first; ok && kt < tl.n; kt = tl.next(kt + 1)) {
+        const int nh = halves(kt, kv_end);
+        for (int j = 0; ok && j < nh; ++j, ++u) {
+          const int s = u & 1;
+          if (u >= 2) {
+            ok = wait(&ds_full[s], ((u - 2) >> 1) & 1);
             if (!ok) break;
           }
           ok = wait(v_full, u & 1);
@@ -251,10 +301,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq256_kernel(const __grid_constan
           __syncwarp();
         }
       }
-      if (ok && u > 0) ok = issue_dq(u - 1);
-      if (elect_one()) tc_commit(mma_drain);
+      if (elect_one()) tc_commit(mma_drain_dp);
       __syncwarp();
-      wait(mma_drain, 0);
+      wait(mma_drain_dp, 0);
     }
     __syncwarp();
   } else if (warp >= 4) {
