@@ -262,3 +262,17 @@ def test_d256_backward_repeats_bitwise_at_size(T, H, causal):
         for name, a, b in zip(("dQ", "dK", "dV"), got, ref):
             assert torch.equal(a, b), f"repeat {rep}: {name} differs"
     assert _lib.device_status(DEV) == 0
+
+
+@pytest.mark.parametrize("d", [64, 128, 256])
+@pytest.mark.parametrize("causal", [False, True])
+def test_rescale_when_the_row_max_grows(d, causal):
+    """Keys of key tile j scaled by 1 + 3j, so each row's maximum logit grows by far more
+    than the forward's lazy-rescale threshold (2^8 in the exp2 domain) from one key tile
+    to the next: the running O is rescaled at every tile.  At D = 256 the next tile's S
+    is computed before the previous PV, and the rescale first waits for that PV."""
+    q, k, v, do = I.qkv(1, 512, 512, 4, 1, d, seed=93)
+    factor = (1.0 + 3.0 * (torch.arange(512) // 128).float()).view(1, 1, 512, 1)
+    k.mul_(factor.to(k.dtype))  # k is a [B, H, T, D] view; scale its key rows in place
+    check(run_api(q, k, v, do, is_causal=causal), oracle(q, k, v, do, causal=causal, device="cpu"),
+          f"growing max D{d} c={causal}")
