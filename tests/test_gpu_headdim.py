@@ -12,6 +12,9 @@ other dP^T, dS and dK, P crossing through distributed shared memory), and the dQ
 (used in both backward modes at this head dim) walking each key tile in two 64-key
 halves.  The same variants are covered; the deterministic backward is also checked to
 repeat bit for bit.
+
+The last test runs head dims 64, 128 and 256 on inputs whose row maxima grow past the
+forward's lazy-rescale threshold at every key tile.
 """
 
 from __future__ import annotations
