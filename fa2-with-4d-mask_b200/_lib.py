@@ -341,6 +341,14 @@ class PreparedMask:
         col = row + a(bh * self.nkb * self.Tq * 16)
         return row, col, nqt
 
+    def kb_order(self) -> torch.Tensor:
+        """Key-tile order view [Bm, Hm, nkb] (int32): key tiles by decreasing number of
+        non-EMPTY query blocks, the order the backward launches them in."""
+        _, col, nqt = self._offsets()
+        off = col + -(-(self.Bm * self.Hm * nqt * self.Tk * 8) // 256) * 256
+        n = self.Bm * self.Hm * self.nkb * 4
+        return self.buffer[off : off + n].view(torch.int32).view(self.Bm, self.Hm, self.nkb)
+
     def blocks(self) -> torch.Tensor:
         """Block map view [Bm, Hm, nqb, nkb] (uint8)."""
         n = self.Bm * self.Hm * self.nqb * self.nkb

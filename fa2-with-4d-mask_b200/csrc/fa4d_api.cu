@@ -152,7 +152,7 @@ size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 // Byte offsets inside a prepared-mask buffer: [block map][row bits][column bits].
 struct PrepLayout {
-  size_t blocks, row_bits, col_bits, total;
+  size_t blocks, row_bits, col_bits, kb_order, total;
   int nqb, nkb, nqt;
 };
 PrepLayout prep_layout(int Bm, int Hm, int Tq, int Tk) {
@@ -164,7 +164,8 @@ PrepLayout prep_layout(int Bm, int Hm, int Tq, int Tk) {
   L.blocks = 0;
   L.row_bits = align256(bh * L.nqb * L.nkb);
   L.col_bits = L.row_bits + align256(bh * L.nkb * static_cast<size_t>(Tq) * 16);
-  L.total = L.col_bits + align256(bh * L.nqt * static_cast<size_t>(Tk) * 8);
+  L.kb_order = L.col_bits + align256(bh * L.nqt * static_cast<size_t>(Tk) * 8);
+  L.total = L.kb_order + align256(bh * L.nkb * sizeof(int32_t));
   return L;
 }
 
@@ -377,6 +378,7 @@ int fa4d_mask_prepare(const uint8_t* mask, const int64_t mask_stride[3], int32_t
   p.blocks = reinterpret_cast<uint8_t*>(base + L.blocks);
   p.row_bits = reinterpret_cast<uint32_t*>(base + L.row_bits);
   p.col_bits = reinterpret_cast<uint32_t*>(base + L.col_bits);
+  p.kb_order = reinterpret_cast<int32_t*>(base + L.kb_order);
   cudaError_t e = fa4d::launch_mask_prepare(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "mask prepare launch failed: %s", cudaGetErrorString(e));
   return ok();
@@ -410,6 +412,7 @@ int fa4d_mask_prepare_docs(const int32_t* doc_q, const int32_t* doc_k, const int
   p.blocks = reinterpret_cast<uint8_t*>(base + L.blocks);
   p.row_bits = reinterpret_cast<uint32_t*>(base + L.row_bits);
   p.col_bits = reinterpret_cast<uint32_t*>(base + L.col_bits);
+  p.kb_order = reinterpret_cast<int32_t*>(base + L.kb_order);
   cudaError_t e = fa4d::launch_mask_prepare(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(FA4D_ERR_CUDA, "document mask prepare launch failed: %s", cudaGetErrorString(e));
   return ok();
@@ -641,6 +644,12 @@ int plan_bwd(const fa4d_bwd_args* a, BwdPlan* plan) {
     const int64_t per_head = static_cast<int64_t>(L.nqt) * a->Tk * 2;
     p.mbt_stride[0] = Bm > 1 ? per_head * Hm : 0;
     p.mbt_stride[1] = Hm > 1 ? per_head : 0;
+    // Key tiles in the prepared order, longest first (D = 256 runs its own grid).
+    if (compute_dim(a->D) != 256 && static_cast<int64_t>(L.nkb) * a->B <= 65535) {
+      p.kb_order = reinterpret_cast<const int32_t*>(static_cast<const char*>(a->mask_prepared) + L.kb_order);
+      p.ko_stride[0] = Bm > 1 ? static_cast<int64_t>(Hm) * L.nkb : 0;
+      p.ko_stride[1] = Hm > 1 ? L.nkb : 0;
+    }
   } else if (a->mask && a->mask_blocks) {
     p.mask_blocks = a->mask_blocks;
     p.mb_stride[0] = a->mask_blocks_stride[0];

@@ -154,15 +154,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   // tile go out together, and under a causal mask the first key tiles (which see the
   // most queries) go first.  KV head x split: the CTA takes query heads
   // [h_first, h_first + G) of its KV head's group (G = Hq / Hk / g_split).
-  // With p.kb_fastest the grid is (key tiles, KV head x split, B) instead.
-  const int kb = p.kb_fastest ? blockIdx.x : blockIdx.y;
+  // With p.kb_fastest the grid is (key tiles, KV head x split, B) instead; with
+  // p.kb_order (a prepared block map) it is (KV head x split, key-tile rank x B), the
+  // batch fastest in y and the key tile of each rank taken from the prepared order,
+  // which lists the key tiles with the most live query blocks first.
   const int hx = p.kb_fastest ? blockIdx.y : blockIdx.x;
-  const int k0 = kb * 128;
   const int hk = hx / p.g_split;
   const int split = hx - hk * p.g_split;
-  const int b = blockIdx.z;
+  const int b = p.kb_order ? static_cast<int>(blockIdx.y) % p.B : static_cast<int>(blockIdx.z);
   const int G = p.Hq / p.Hk / p.g_split;
   const int h_first = hk * (p.Hq / p.Hk) + split * G;
+  const int kb = p.kb_order ? __ldg(p.kb_order + b * p.ko_stride[0] + static_cast<int64_t>(h_first) * p.ko_stride[1] +
+                                    static_cast<int>(blockIdx.y) / p.B)
+                            : (p.kb_fastest ? blockIdx.x : blockIdx.y);
+  const int k0 = kb * 128;
 
   // Query tiles this key tile interacts with.
   int first_qt = 0;
@@ -738,7 +743,7 @@ cudaError_t launch_bwd_t(const BwdParams& p, cudaStream_t s) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return e;
   const unsigned nkb = (p.Tk + 127) / 128, nh = p.Hk * p.g_split;
-  const dim3 grid = p.kb_fastest ? dim3(nkb, nh, p.B) : dim3(nh, nkb, p.B);
+  const dim3 grid = p.kb_order ? dim3(nh, nkb * p.B, 1) : (p.kb_fastest ? dim3(nkb, nh, p.B) : dim3(nh, nkb, p.B));
   kern<<<grid, kBwdThreads, L::kAlloc, s>>>(p);
   return cudaGetLastError();
 }

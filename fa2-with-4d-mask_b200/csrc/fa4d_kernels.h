@@ -113,6 +113,12 @@ struct BwdParams {
   int64_t v_stride[3];
   const void* k;        // D = 256: rank 0 copies its K tile into TMEM (A operand of S^T)
   int64_t k_stride[3];
+  // Block-sparse grids with a prepared mask: the key tile of grid row rank comes from
+  // kb_order (mask batch / head strides ko_stride, 0 where the mask broadcasts), longest
+  // first, and the grid is (KV head x split, key-tile rank x B) with the batch fastest
+  // in y, so the longest CTAs of every batch element start first.  Null: grid as above.
+  const int32_t* kb_order;
+  int64_t ko_stride[2];
 };
 
 // Deterministic dQ: one CTA per 128-row query tile of one (batch, head) walks its key
@@ -186,6 +192,7 @@ struct MaskPrepParams {
   uint8_t* blocks;
   uint32_t* row_bits;
   uint32_t* col_bits;
+  int32_t* kb_order;  // [Bm * Hm][nkb]: key tiles by live query blocks, most first
 };
 
 // Row dot products Delta = rowsum(O * dO) and zeroing of the dQ accumulator.

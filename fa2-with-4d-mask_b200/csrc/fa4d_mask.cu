@@ -243,6 +243,35 @@ __global__ void __launch_bounds__(128) mask_prepare_kernel(const MaskPrepParams 
 
 }  // namespace
 
+// Key tiles longest first, for the backward grid: one block per (b, h) row of the block
+// map counts each key tile's non-EMPTY 128-row query blocks and writes kb_order[rank] =
+// key tile, by decreasing count (ties by key tile index, so the order is reproducible).
+// With more than kOrderMaxTiles key tiles the order is the identity.
+constexpr int kOrderMaxTiles = 1024;
+
+__global__ void __launch_bounds__(256) kb_order_kernel(const MaskPrepParams p) {
+  __shared__ int cnt[kOrderMaxTiles];
+  const int nkb = p.nkb;
+  const uint8_t* blocks = p.blocks + static_cast<size_t>(blockIdx.x) * p.nqb * nkb;
+  int32_t* out = p.kb_order + static_cast<size_t>(blockIdx.x) * nkb;
+  if (nkb > kOrderMaxTiles) {
+    for (int kb = threadIdx.x; kb < nkb; kb += blockDim.x) out[kb] = kb;
+    return;
+  }
+  for (int kb = threadIdx.x; kb < nkb; kb += blockDim.x) {
+    int c = 0;
+    for (int qb = 0; qb < p.nqb; ++qb) c += blocks[static_cast<size_t>(qb) * nkb + kb] != 0;
+    cnt[kb] = c;
+  }
+  __syncthreads();
+  for (int kb = threadIdx.x; kb < nkb; kb += blockDim.x) {
+    const int c = cnt[kb];
+    int rank = 0;
+    for (int j = 0; j < nkb; ++j) rank += (cnt[j] > c) || (cnt[j] == c && j < kb);
+    out[rank] = kb;
+  }
+}
+
 cudaError_t launch_mask_prepare(const MaskPrepParams& p, cudaStream_t s) {
   dim3 grid((p.nkb + kPrepTiles - 1) / kPrepTiles, p.nqb, p.Bm * p.Hm);
   if (p.doc_q)
@@ -251,6 +280,9 @@ cudaError_t launch_mask_prepare(const MaskPrepParams& p, cudaStream_t s) {
     mask_prepare_kernel<0><<<grid, 128, 0, s>>>(p);
   else
     mask_prepare_kernel<1><<<grid, 128, 0, s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || !p.kb_order) return e;
+  kb_order_kernel<<<p.Bm * p.Hm, 256, 0, s>>>(p);
   return cudaGetLastError();
 }
 

@@ -225,6 +225,10 @@ int fa4d_mask_blocks(const uint8_t* mask, const int64_t mask_stride[3], int32_t 
  *     (kt, q, w) holds the flags of keys 128*kt + 32*w + 0..31 for query q;
  *   - column bits: per (b, h) a [ceil(Tq/64)][Tk][2] array of uint32 whose entry
  *     (qt, k, w) holds the flags of queries 64*qt + 32*w + 0..31 for key k;
+ *   - key-tile order: per (b, h) a [ceil(Tk/128)] array of int32 listing the key
+ *     tiles by decreasing number of non-EMPTY 128-row query blocks (ties by index;
+ *     the identity past 1024 key tiles); the backward launches its key tiles in this
+ *     order so the longest CTAs start first;
  * with flags past Tk / Tq zero.  The forward reads one 16-byte row-bit word group
  * per query row and key tile, the backward one 8-byte column-bit group per key and
  * query tile, instead of 128 or 64 mask bytes.  Like the block map, the buffer stays

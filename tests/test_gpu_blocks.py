@@ -50,6 +50,12 @@ def _check_prepared(mask_dev, ref_mask):
     rw, cw = mask_bits_ref(ref_mask)
     np.testing.assert_array_equal(pm.row_bits().cpu().numpy(), rw)
     np.testing.assert_array_equal(pm.col_bits().cpu().numpy(), cw)
+    # Key tiles by decreasing count of non-EMPTY query blocks, ties by index: the order
+    # the backward launches its key tiles in.
+    live = (pm.blocks().cpu().numpy() != EMPTY).sum(axis=2)  # [Bm, Hm, nkb]
+    nkb = live.shape[-1]
+    want = np.argsort(-live * (nkb + 1) + np.arange(nkb), axis=-1, kind="stable")
+    np.testing.assert_array_equal(pm.kb_order().cpu().numpy(), want)
     return pm
 
 
