@@ -54,7 +54,7 @@ constexpr uint32_t kRegsLaunch = 128, kRegsCtl = 88, kRegsSoftmax = 160, kRegsDr
 static_assert(128 * kRegsCtl + 256 * kRegsSoftmax + 128 * kRegsDrain <= kBwdThreads * kRegsLaunch,
               "register split exceeds the launch allocation");
 
-template <int D, int kQStages, bool kMask = false>
+template <int D, int kQStages>
 struct BwdLayout {
   static constexpr int kKV = 128 * D * 2;   // K or V tile (128 keys)
   static constexpr int kQT = 64 * D * 2;    // Q or dO tile (64 queries)
@@ -66,10 +66,7 @@ struct BwdLayout {
   static constexpr int kDSb = kDO + kQStages * kQT;   // 2 buffers
   static constexpr int kLSE = kDSb + 2 * kDS;            // kQStages x 64 floats
   static constexpr int kDelta = kLSE + kQStages * 256;   // kQStages x 64 floats
-  // Mask variants: a shared copy of the key tile's block-map column (kMapBytes at most).
-  static constexpr int kMapBytes = kMask ? 16384 : 0;
-  static constexpr int kMap = kDelta + kQStages * 256;
-  static constexpr int kBar = kMap + kMapBytes;
+  static constexpr int kBar = kDelta + kQStages * 256;
   static constexpr int kNumBars = 18 + 2 * kQStages;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
@@ -123,7 +120,7 @@ __device__ __forceinline__ void issue_dq(uint32_t tD, uint32_t sK, uint32_t sDS)
 template <int D, bool kBF16, bool kMask, bool kScore>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_constant__ BwdParams p) {
   constexpr int kQStages = kQStagesFor<kMask, kScore>;
-  using L = BwdLayout<D, kQStages, kMask>;
+  using L = BwdLayout<D, kQStages>;
   extern __shared__ uint8_t smem_raw[];
   if (L::kSlack == 0 && (smem_u32(smem_raw) & 1023u) != 0u) {
     // No room to realign: report and leave before touching anything (uniform exit).
@@ -190,22 +187,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
   first.first_qt = first_qt;
   first.N = G * nq;
   first.lin = 0;
-  if (kMask && first.map) {
-    // Copy the map entries of this key tile's (head, query block) pairs into shared
-    // memory with independent loads; every role's walk then reads them from there.
-    const int q_b0 = first_qt >> 1, nqb_loc = (p.Tq + 127) / 128 - q_b0;
-    if (nqb_loc > 0 && G * nqb_loc <= L::kMapBytes) {
-      uint8_t* smap = smem + L::kMap;
-      for (int i = threadIdx.x; i < G * nqb_loc; i += kBwdThreads) {
-        const int g = i / nqb_loc, qb = q_b0 + i - g * nqb_loc;
-        smap[i] = __ldg(first.map + g * first.head_stride + static_cast<int64_t>(qb) * first.row_stride);
-      }
-      __syncthreads();
-      first.smap = smap;
-      first.sstride = nqb_loc;
-      first.sq0 = q_b0;
-    }
-  }
   first.skip_empty();
   const bool any_work = first.valid();
 
@@ -757,7 +738,7 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const ConvertParams p) 
 
 template <int D, bool kBF16, bool kMask, bool kScore>
 cudaError_t launch_bwd_t(const BwdParams& p, cudaStream_t s) {
-  using L = BwdLayout<D, kQStagesFor<kMask, kScore>, kMask>;
+  using L = BwdLayout<D, kQStagesFor<kMask, kScore>>;
   auto kern = bwd_kernel<D, kBF16, kMask, kScore>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return e;

@@ -56,11 +56,6 @@ struct QTiles {
   int64_t head_stride, row_stride;
   int nq, first_qt, N;  // N = G * nq pairs before skipping
   int lin;              // current pair g * nq + qi; lin >= N past the end
-  // Optional shared-memory copy of the map entries this walk reads, [g][qb - sq0] with
-  // row length sstride: each state() is then a shared load instead of a dependent
-  // global one.
-  const uint8_t* smap = nullptr;
-  int sstride = 0, sq0 = 0;
   __device__ __forceinline__ int g() const { return lin / nq; }
   __device__ __forceinline__ int q0() const { return (first_qt + lin % nq) * 64; }
   // 0: skip; 1: visit and apply the mask; 2: visit, the mask keeps every pair.
@@ -68,8 +63,7 @@ struct QTiles {
     if (!kMask) return 2;
     if (!map) return 1;
     const int gg = lin / nq;
-    const int qb = (first_qt + lin - gg * nq) >> 1;
-    const int v = smap ? smap[gg * sstride + qb - sq0] : __ldg(map + gg * head_stride + qb * row_stride);
+    const int v = __ldg(map + gg * head_stride + ((first_qt + lin - gg * nq) >> 1) * row_stride);
     return v == 0 ? 0 : (v == 2 ? 2 : 1);
   }
   __device__ __forceinline__ bool valid() const { return lin < N; }
