@@ -147,6 +147,9 @@ __global__ void __launch_bounds__(128) mask_prepare_kernel(const MaskPrepParams 
   const int kt0 = blockIdx.x * kPrepTiles;
   const int c = tid & 7, r0 = tid >> 3;
   const uint8_t* mask_base = kSrc == 2 ? nullptr : p.mask + b * p.stride[0] + h * p.stride[1];
+  // The key-tile order pass may be scheduled now; it waits for this grid's completion
+  // (griddepcontrol.wait) before reading the block map.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // kSrc 0: one block's 16-byte chunks, loaded into registers ahead of their use.
   auto load_block = [&](int kt, uint4 (&v)[8]) {
@@ -251,6 +254,9 @@ constexpr int kOrderMaxTiles = 1024;
 
 __global__ void __launch_bounds__(256) kb_order_kernel(const MaskPrepParams p) {
   __shared__ int cnt[kOrderMaxTiles];
+  // Launched as a programmatic dependent of the prepare kernel: wait until that grid has
+  // finished and its block map is visible.  The map is read through L2 only (__ldcg).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int nkb = p.nkb;
   const uint8_t* blocks = p.blocks + static_cast<size_t>(blockIdx.x) * p.nqb * nkb;
   int32_t* out = p.kb_order + static_cast<size_t>(blockIdx.x) * nkb;
@@ -258,10 +264,23 @@ __global__ void __launch_bounds__(256) kb_order_kernel(const MaskPrepParams p) {
     for (int kb = threadIdx.x; kb < nkb; kb += blockDim.x) out[kb] = kb;
     return;
   }
-  for (int kb = threadIdx.x; kb < nkb; kb += blockDim.x) {
-    int c = 0;
-    for (int qb = 0; qb < p.nqb; ++qb) c += blocks[static_cast<size_t>(qb) * nkb + kb] != 0;
-    cnt[kb] = c;
+  for (int kb = threadIdx.x; kb < nkb; kb += blockDim.x) cnt[kb] = 0;
+  __syncthreads();
+  // The whole CTA reads the map row-major, kUnroll independent byte loads per thread in
+  // flight, and adds the non-EMPTY ones into shared counters (a walk down one column
+  // per thread would wait out one load latency per query block).
+  constexpr int kUnroll = 8;
+  const int n = p.nqb * nkb;
+  for (int i0 = threadIdx.x; i0 < n; i0 += blockDim.x * kUnroll) {
+    uint8_t st[kUnroll];
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) {
+      const int i = i0 + j * static_cast<int>(blockDim.x);
+      st[j] = i < n ? __ldcg(blocks + i) : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j)
+      if (st[j] != 0) atomicAdd(&cnt[(i0 + j * static_cast<int>(blockDim.x)) % nkb], 1);
   }
   __syncthreads();
   for (int kb = threadIdx.x; kb < nkb; kb += blockDim.x) {
@@ -282,8 +301,18 @@ cudaError_t launch_mask_prepare(const MaskPrepParams& p, cudaStream_t s) {
     mask_prepare_kernel<1><<<grid, 128, 0, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !p.kb_order) return e;
-  kb_order_kernel<<<p.Bm * p.Hm, 256, 0, s>>>(p);
-  return cudaGetLastError();
+  // Programmatic dependent launch: the order pass's CTAs are scheduled while the
+  // prepare kernel's last wave runs, instead of after a launch gap.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.Bm * p.Hm);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kb_order_kernel, p);
 }
 
 cudaError_t launch_mask_blocks(const MaskBlocksParams& p, cudaStream_t s) {
