@@ -38,6 +38,29 @@ def mask_blocks_ref(mask, block: int = BLOCK) -> np.ndarray:
     return out
 
 
+ORDER_MAX_TILES = 1024
+
+
+def kb_order_ref(blocks: np.ndarray) -> np.ndarray:
+    """The key-tile order a prepared mask stores for the backward's launch: for each
+    (b, h) row of the block map [Bm, Hm, nqb, nkb], the key tiles sorted by decreasing
+    count of non-EMPTY query blocks, ties by ascending key-tile index; the identity
+    when nkb exceeds ORDER_MAX_TILES.  Returns int32 [Bm, Hm, nkb] with entry r = the
+    key tile launched at rank r.  The order is this library's own launch schedule (the
+    reference launches key tiles in index order, python/fa2.py:242-302); it changes no
+    result, only which CTAs start first."""
+    b = np.asarray(blocks)
+    Bm, Hm, _, nkb = b.shape
+    if nkb > ORDER_MAX_TILES:
+        return np.broadcast_to(np.arange(nkb, dtype=np.int32), (Bm, Hm, nkb)).copy()
+    live = (b != EMPTY).sum(axis=2)  # [Bm, Hm, nkb]
+    out = np.empty((Bm, Hm, nkb), dtype=np.int32)
+    for i in range(Bm):
+        for j in range(Hm):
+            out[i, j] = sorted(range(nkb), key=lambda kb: (-int(live[i, j, kb]), kb))
+    return out
+
+
 def empty_fraction(mask, block: int = BLOCK) -> float:
     """Share of blocks with no True element."""
     b = mask_blocks_ref(mask, block)

@@ -1,6 +1,7 @@
 """CPU: the block-occupancy map — the oracle's classification against a direct
-per-block loop, the sparsity of the packed-document workload, and the reuse rules
-of the op's per-mask map cache (no device work)."""
+per-block loop, the sparsity of the packed-document workload, the key-tile launch
+order a prepared mask carries, and the reuse rules of the op's per-mask map cache
+(no device work)."""
 
 from __future__ import annotations
 
@@ -9,7 +10,7 @@ import pytest
 import torch
 
 from oracle import inputs as I
-from oracle.blocks import EMPTY, FULL, PARTIAL, empty_fraction, mask_blocks_ref
+from oracle.blocks import EMPTY, FULL, ORDER_MAX_TILES, PARTIAL, empty_fraction, kb_order_ref, mask_blocks_ref
 
 impl_fa2 = __import__("fa2_with_4d_mask_b200.fa2", fromlist=["x"])
 
@@ -104,3 +105,32 @@ def test_bits_oracle_layout():
     # Flags past Tk / Tq are zero.
     assert (rw[0, :, 1, :, 3] == 0).all() and (cw[0, :, 1, :, 1] == 0).all()
     assert (rw[0, :, 1, :, 2].view(np.uint32) >> 8 == 0).all()
+
+
+def test_kb_order_oracle_by_hand():
+    """Live counts per key tile [2, 0, 3, 2] give ranks 2, 0, 3, 1 (ties by index)."""
+    blocks = np.full((1, 1, 3, 4), EMPTY, dtype=np.uint8)
+    blocks[0, 0, :2, 0] = PARTIAL
+    blocks[0, 0, :, 2] = FULL
+    blocks[0, 0, 1:, 3] = PARTIAL
+    np.testing.assert_array_equal(kb_order_ref(blocks)[0, 0], [2, 0, 3, 1])
+    # An all-EMPTY map keeps index order.
+    np.testing.assert_array_equal(kb_order_ref(np.zeros((1, 1, 2, 5), np.uint8))[0, 0], np.arange(5))
+
+
+def test_kb_order_oracle_rows_and_identity_past_limit():
+    rng = np.random.default_rng(7)
+    blocks = rng.integers(0, 3, size=(2, 3, 9, 40)).astype(np.uint8)
+    got = kb_order_ref(blocks)
+    live = (blocks != EMPTY).sum(axis=2)
+    nkb = blocks.shape[-1]
+    # The same order by a stable sort on one combined key.
+    want = np.argsort(-live * (nkb + 1) + np.arange(nkb), axis=-1, kind="stable")
+    np.testing.assert_array_equal(got, want)
+    for i in range(2):
+        for j in range(3):
+            assert sorted(got[i, j]) == list(range(nkb))  # a permutation
+            assert all(np.diff(live[i, j][got[i, j]]) <= 0)  # counts never rise with rank
+    big = np.zeros((1, 2, 1, ORDER_MAX_TILES + 1), np.uint8)
+    big[..., -1] = FULL
+    np.testing.assert_array_equal(kb_order_ref(big), np.broadcast_to(np.arange(ORDER_MAX_TILES + 1), (1, 2, ORDER_MAX_TILES + 1)))

@@ -15,7 +15,7 @@ import torch
 
 from conftest import out_err, rel_err
 from oracle import inputs as I
-from oracle.blocks import EMPTY, FULL, PARTIAL, mask_bits_ref, mask_blocks_ref
+from oracle.blocks import EMPTY, FULL, PARTIAL, kb_order_ref, mask_bits_ref, mask_blocks_ref
 from test_gpu_parity import DEV, _fp32_oracle_and_status, check, oracle, run_api  # noqa: F401
 
 from fa2_with_4d_mask_b200 import _lib
@@ -52,10 +52,7 @@ def _check_prepared(mask_dev, ref_mask):
     np.testing.assert_array_equal(pm.col_bits().cpu().numpy(), cw)
     # Key tiles by decreasing count of non-EMPTY query blocks, ties by index: the order
     # the backward launches its key tiles in.
-    live = (pm.blocks().cpu().numpy() != EMPTY).sum(axis=2)  # [Bm, Hm, nkb]
-    nkb = live.shape[-1]
-    want = np.argsort(-live * (nkb + 1) + np.arange(nkb), axis=-1, kind="stable")
-    np.testing.assert_array_equal(pm.kb_order().cpu().numpy(), want)
+    np.testing.assert_array_equal(pm.kb_order().cpu().numpy(), kb_order_ref(mask_blocks_ref(ref_mask)))
     return pm
 
 
