@@ -956,10 +956,17 @@ def run_e2e(api, dev, args, dist=None, world=1):
     if dist:
         dist.barrier()
     torch.cuda.synchronize(dev)
+    try:
+        free_gib = round(torch.cuda.mem_get_info(dev)[0] / 2**30, 1)
+    except RuntimeError:
+        free_gib = None
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(comp)
     up.wait_event(a)
+    t0 = time.perf_counter()
     run(args.e2e_steps)
+    # Host time to enqueue the steps: near ms_per_step means the leg was host-bound.
+    host_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
     comp.wait_stream(up)
     comp.wait_stream(down)
     b.record(comp)
@@ -967,6 +974,7 @@ def run_e2e(api, dev, args, dist=None, world=1):
     ms = shard.max_over_ranks(a.elapsed_time(b) / args.e2e_steps, dist, dev)
     return {"value": round(world * fwd_bwd_flops(B, HQ, T, T, D, False) / (ms * 1e-3) / 1e12, 2), "unit": UNIT,
             "ms_per_step": round(ms, 4), "h2d_bytes_per_step": world * h2d, "d2h_bytes_per_step": world * d2h,
+            "host_enqueue_ms_per_step": round(host_ms, 4), "device_free_gib_at_start": free_gib,
             "path": "tilelang_flash_attention + autograd backward; each step uploads its pinned inputs and "
                     "downloads O, dQ, dK, dV on separate copy streams, double-buffered so copies of "
                     "neighbouring steps overlap compute"}
