@@ -38,6 +38,8 @@ def test_bench_line_contract():
     B, T, HQ, HK, D = 1, 8192, 32, 8, 128
     io = 2 * B * T * D * (2 * HQ + 2 * HK)
     assert e2e["h2d_bytes_per_step"] == io and e2e["d2h_bytes_per_step"] == io
+    # Diagnostics of the e2e leg: host enqueue time per step and free device memory.
+    assert e2e["host_enqueue_ms_per_step"] > 0 and "device_free_gib_at_start" in e2e
     # Four launches per step (forward, preprocess, main, convert) plus the slice sum
     # when the group split is on.
     assert line["gpu_launches"] in (4 * 3, 5 * 3)
