@@ -150,7 +150,8 @@ int nblocks(int T) { return (T + 127) / 128; }
 
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
-// Byte offsets inside a prepared-mask buffer: [block map][row bits][column bits].
+// Byte offsets inside a prepared-mask buffer: [block map][row bits][column bits]
+// [key-tile order], each region starting on a 256-byte boundary.
 struct PrepLayout {
   size_t blocks, row_bits, col_bits, kb_order, total;
   int nqb, nkb, nqt;

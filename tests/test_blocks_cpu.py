@@ -134,3 +134,25 @@ def test_kb_order_oracle_rows_and_identity_past_limit():
     big = np.zeros((1, 2, 1, ORDER_MAX_TILES + 1), np.uint8)
     big[..., -1] = FULL
     np.testing.assert_array_equal(kb_order_ref(big), np.broadcast_to(np.arange(ORDER_MAX_TILES + 1), (1, 2, ORDER_MAX_TILES + 1)))
+
+
+@pytest.mark.parametrize("dims", [(1, 1, 1, 1), (2, 3, 300, 520), (1, 16, 4096, 4096), (4, 1, 77, 4099)])
+def test_prepared_views_match_the_library_layout(dims):
+    """The Python views of a prepared-mask buffer (block map, row bits, column bits,
+    key-tile order) sit in that order, do not overlap, start on 256-byte boundaries and
+    end where the library's own size function says the buffer ends."""
+    from fa2_with_4d_mask_b200 import _lib
+
+    Bm, Hm, Tq, Tk = dims
+    size = int(_lib.load_library().fa4d_mask_prepare_size(Bm, Hm, Tq, Tk))
+    pm = _lib.PreparedMask(torch.empty(size, dtype=torch.uint8), Bm, Hm, Tq, Tk)
+    views = [pm.blocks(), pm.row_bits(), pm.col_bits(), pm.kb_order()]
+    nqb, nkb, nqt = -(-Tq // 128), -(-Tk // 128), -(-Tq // 64)
+    assert [tuple(v.shape) for v in views] == [(Bm, Hm, nqb, nkb), (Bm, Hm, nkb, Tq, 4), (Bm, Hm, nqt, Tk, 2),
+                                              (Bm, Hm, nkb)]
+    base = pm.buffer.data_ptr()
+    spans = [(v.data_ptr() - base, v.data_ptr() - base + v.numel() * v.element_size()) for v in views]
+    assert spans[0][0] == 0
+    for (s0, e0), (s1, _) in zip(spans, spans[1:]):
+        assert s1 % 256 == 0 and s1 >= e0
+    assert -(-spans[-1][1] // 256) * 256 == size
